@@ -1,0 +1,296 @@
+"""CPU oracle for the paged KV-cache hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and the cpu_baseline / reference arm
+of ``bench.py`` may import this package.  It is the checker, never the thing
+measured as the product, and the product package (``voidweb_b200``) never
+imports it.
+
+PARITY UNPINNED: the reference is written in the BlackMagic language, which
+cannot be compiled here, and it ships no tests or golden vectors.  The oracle
+(``vw_oracle.cpp``) restates the reference source function by function and is
+cross-checked against the independent pure-Python transliteration in
+``tests/golden/make_golden.py`` (fixtures committed under ``tests/golden/``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libvw_oracle.so")
+
+F16, BF16, FP8 = 0, 1, 2
+FP8_REFERENCE, FP8_OCP = 0, 1
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (only when the .so is stale)."""
+    src = os.path.join(_HERE, "vw_oracle.cpp")
+    if (not os.path.exists(_LIB_PATH)) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.check_call(["make", "-s", "-C", _HERE])
+    return _LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        u8, u16, u32, u64, i32, i64 = (ctypes.c_uint8, ctypes.c_uint16, ctypes.c_uint32,
+                                       ctypes.c_uint64, ctypes.c_int32, ctypes.c_int64)
+        f32, f64, vp = ctypes.c_float, ctypes.c_double, ctypes.c_void_p
+        sig = {
+            "vwo_bf16_to_f32": (f32, [u16]), "vwo_f32_to_bf16": (u16, [f32]),
+            "vwo_f16_to_f32": (f32, [u16]), "vwo_f32_to_f16": (u16, [f32]),
+            "vwo_fp8_encode_ref": (u8, [f32]), "vwo_fp8_decode_ref": (f32, [u8]),
+            "vwo_fp8_encode_ocp": (u8, [f32]), "vwo_fp8_decode_ocp": (f32, [u8]),
+            "vwo_fp8_quant_row": (None, [vp, ctypes.c_int, ctypes.c_int, vp, vp]),
+            "vwo_kv_append": (None, [vp, vp, vp, u32, vp, vp, vp, u32]),
+            "vwo_block_copy": (None, [vp, vp, vp, vp, u32]),
+            "vwo_kv_gather": (None, [vp, vp, vp, u32, vp, u32, vp, vp, vp, vp]),
+            "vwo_paged_decode_f32": (i32, [vp, vp, vp, u32, vp, u32, vp, u32, vp, u32, f32, vp,
+                                           ctypes.c_int]),
+            "vwo_paged_decode_f64": (i32, [vp, vp, vp, u32, vp, u32, vp, u32, vp, u32, f64, vp,
+                                           ctypes.c_int]),
+            "vwo_rolling_hash": (u64, [u64, vp, u32]),
+            "vwo_bm_new": (vp, [u32, u32]), "vwo_bm_delete": (None, [vp]),
+            "vwo_bm_capacity": (u32, [vp]), "vwo_bm_free_count": (u32, [vp]),
+            "vwo_bm_alloc": (i64, [vp]), "vwo_bm_alloc_seq": (i32, [vp, u32, vp]),
+            "vwo_bm_incref": (None, [vp, u32]), "vwo_bm_decref": (None, [vp, u32]),
+            "vwo_bm_free_seq": (None, [vp, vp, u32]), "vwo_bm_ref_count": (u32, [vp, u32]),
+            "vwo_bm_prefix_lookup": (u32, [vp, vp, u32, vp, u32]),
+            "vwo_bm_register_prefix_block": (None, [vp, u32, u64]),
+            "vwo_bm_free_list": (u32, [vp, vp, u32]),
+            "vwo_radix_new": (vp, [u32, u32]), "vwo_radix_delete": (None, [vp]),
+            "vwo_radix_lookup": (u32, [vp, vp, u32, vp, vp, u32]),
+            "vwo_radix_total_blocks": (u32, [vp]),
+            "vwo_radix_insert": (u32, [vp, vp, u32, vp, u32, vp, u32]),
+            "vwo_radix_evict_lru": (u32, [vp, u32, vp, u32]),
+            "vwo_radix_lock": (None, [vp, vp, u32]), "vwo_radix_unlock": (None, [vp, vp, u32]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else None
+
+
+class Geom(ctypes.Structure):
+    _fields_ = [("num_layers", ctypes.c_uint32), ("num_kv_heads", ctypes.c_uint32),
+                ("head_dim", ctypes.c_uint32), ("num_blocks", ctypes.c_uint32),
+                ("kv_dtype", ctypes.c_uint32), ("io_dtype", ctypes.c_uint32),
+                ("fp8_mode", ctypes.c_uint32)]
+
+
+def geom(L, Hkv, D, NB, kv_dtype, io_dtype, fp8_mode=FP8_REFERENCE) -> Geom:
+    return Geom(L, Hkv, D, NB, kv_dtype, io_dtype, fp8_mode)
+
+
+# ---- codecs (numpy, vectorised through the scalar C functions) -------------
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """utils/simd.bm:153-158 round-to-nearest-even on the raw bits."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def io_bits_to_f32(h: np.ndarray, io_dtype: int) -> np.ndarray:
+    if io_dtype == BF16:
+        return bf16_bits_to_f32(h)
+    return np.asarray(h, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def f32_to_io_bits(x: np.ndarray, io_dtype: int) -> np.ndarray:
+    if io_dtype == BF16:
+        return f32_to_bf16_bits(x)
+    return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def fp8_encode(x: np.ndarray, mode: int = FP8_REFERENCE) -> np.ndarray:
+    f = lib().vwo_fp8_encode_ref if mode == FP8_REFERENCE else lib().vwo_fp8_encode_ocp
+    flat = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    return np.array([f(float(v)) for v in flat], dtype=np.uint8).reshape(np.shape(x))
+
+
+def fp8_decode(c: np.ndarray, mode: int = FP8_REFERENCE) -> np.ndarray:
+    f = lib().vwo_fp8_decode_ref if mode == FP8_REFERENCE else lib().vwo_fp8_decode_ocp
+    table = np.array([f(i) for i in range(256)], dtype=np.float32)
+    return table[np.asarray(c, dtype=np.uint8)]
+
+
+def fp8_quant_row(x: np.ndarray, mode: int = FP8_REFERENCE):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    codes = np.zeros(x.shape, dtype=np.uint8)
+    scale = np.zeros(1, dtype=np.float32)
+    lib().vwo_fp8_quant_row(_p(x), x.size, mode, _p(codes), _p(scale))
+    return codes, float(scale[0])
+
+
+# ---- pool-level ops ----------------------------------------------------------
+
+def pool_shape(g: Geom):
+    return (g.num_layers, g.num_blocks, 2, g.num_kv_heads, 16, g.head_dim)
+
+
+def kv_append(g: Geom, data: np.ndarray, scales, layer: int, k_new: np.ndarray,
+              v_new: np.ndarray, slots: np.ndarray) -> None:
+    slots = np.ascontiguousarray(slots, dtype=np.int64)
+    lib().vwo_kv_append(ctypes.byref(g), _p(data), _p(scales), layer,
+                        _p(np.ascontiguousarray(k_new)), _p(np.ascontiguousarray(v_new)),
+                        _p(slots), slots.size)
+
+
+def block_copy(g: Geom, data: np.ndarray, scales, pairs: np.ndarray) -> None:
+    pairs = np.ascontiguousarray(pairs, dtype=np.uint32).reshape(-1, 2)
+    lib().vwo_block_copy(ctypes.byref(g), _p(data), _p(scales), _p(pairs), pairs.shape[0])
+
+
+def kv_gather(g: Geom, data, scales, layer, block_table, seq_len):
+    eb_dtype = np.uint8 if g.kv_dtype == FP8 else np.uint16
+    H, D = g.num_kv_heads, g.head_dim
+    ok = np.zeros((H, seq_len, D), dtype=eb_dtype)
+    ov = np.zeros((H, seq_len, D), dtype=eb_dtype)
+    oks = np.zeros((H, seq_len), dtype=np.float32)
+    ovs = np.zeros((H, seq_len), dtype=np.float32)
+    bt = np.ascontiguousarray(block_table, dtype=np.uint32)
+    lib().vwo_kv_gather(ctypes.byref(g), _p(data), _p(scales), layer, _p(bt), seq_len,
+                        _p(ok), _p(ov), _p(oks), _p(ovs))
+    return ok, ov, oks, ovs
+
+
+def paged_decode_f32(g: Geom, data, scales, layer, q, Hq, block_tables, seq_lens, scale,
+                     nthreads=0) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    bt = np.ascontiguousarray(block_tables, dtype=np.uint32)
+    sl = np.ascontiguousarray(seq_lens, dtype=np.uint32)
+    B = sl.size
+    out = np.zeros((B, Hq, g.head_dim), dtype=np.uint16)
+    rc = lib().vwo_paged_decode_f32(ctypes.byref(g), _p(data), _p(scales), layer, _p(q), Hq,
+                                    _p(bt), bt.shape[1], _p(sl), B, scale, _p(out), nthreads)
+    if rc != 0:
+        raise ValueError("oracle: seq_len 0")
+    return out
+
+
+def paged_decode_f64(g: Geom, data, scales, layer, q, Hq, block_tables, seq_lens, scale,
+                     nthreads=0) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    bt = np.ascontiguousarray(block_tables, dtype=np.uint32)
+    sl = np.ascontiguousarray(seq_lens, dtype=np.uint32)
+    B = sl.size
+    out = np.zeros((B, Hq, g.head_dim), dtype=np.float64)
+    rc = lib().vwo_paged_decode_f64(ctypes.byref(g), _p(data), _p(scales), layer, _p(q), Hq,
+                                    _p(bt), bt.shape[1], _p(sl), B, scale, _p(out), nthreads)
+    if rc != 0:
+        raise ValueError("oracle: seq_len 0")
+    return out
+
+
+def rolling_hash(prev: int, tokens) -> int:
+    t = np.ascontiguousarray(tokens, dtype=np.uint32)
+    return int(lib().vwo_rolling_hash(prev, _p(t), t.size))
+
+
+class BlockManager:
+    """engine/kv_cache.bm:29-151 restated (see vw_oracle.cpp)."""
+
+    def __init__(self, block_size: int, max_blocks: int):
+        self._h = lib().vwo_bm_new(block_size, max_blocks)
+        self.max_blocks = max_blocks
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().vwo_bm_delete(self._h)
+            self._h = None
+
+    def capacity(self): return lib().vwo_bm_capacity(self._h)
+    def free_count(self): return lib().vwo_bm_free_count(self._h)
+
+    def alloc(self):
+        r = lib().vwo_bm_alloc(self._h)
+        return None if r < 0 else int(r)
+
+    def alloc_seq(self, n):
+        out = np.zeros(max(n, 1), dtype=np.uint32)
+        if lib().vwo_bm_alloc_seq(self._h, n, _p(out)) != 0:
+            raise MemoryError("KV cache OOM")
+        return [int(x) for x in out[:n]]
+
+    def incref(self, i): lib().vwo_bm_incref(self._h, i)
+    def decref(self, i): lib().vwo_bm_decref(self._h, i)
+    def ref_count(self, i): return lib().vwo_bm_ref_count(self._h, i)
+
+    def free_seq(self, table):
+        t = np.ascontiguousarray(table, dtype=np.uint32)
+        lib().vwo_bm_free_seq(self._h, _p(t), t.size)
+
+    def prefix_lookup(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        cap = 4096
+        out = np.zeros(cap, dtype=np.uint32)
+        n = lib().vwo_bm_prefix_lookup(self._h, _p(t), t.size, _p(out), cap)
+        return [int(x) for x in out[:min(n, cap)]]
+
+    def register_prefix_block(self, i, h): lib().vwo_bm_register_prefix_block(self._h, i, h)
+
+    def free_list(self):
+        out = np.zeros(self.max_blocks + 1, dtype=np.uint32)
+        n = lib().vwo_bm_free_list(self._h, _p(out), out.size)
+        return [int(x) for x in out[:n]]
+
+
+class RadixCache:
+    """radix_cache/radix_cache.bm:199-285 restated with the documented fixes."""
+
+    def __init__(self, block_size: int, max_blocks: int):
+        self._h = lib().vwo_radix_new(block_size, max_blocks)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().vwo_radix_delete(self._h)
+            self._h = None
+
+    def lookup(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        cap = 1 << 16
+        out = np.zeros(cap, dtype=np.uint32)
+        ml = ctypes.c_uint32(0)
+        n = lib().vwo_radix_lookup(self._h, _p(t), t.size, ctypes.byref(ml), _p(out), cap)
+        return int(ml.value), [int(x) for x in out[:n]]
+
+    def insert(self, tokens, blocks):
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        b = np.ascontiguousarray(blocks, dtype=np.uint32)
+        out = np.zeros(4096, dtype=np.uint32)
+        n = lib().vwo_radix_insert(self._h, _p(t), t.size, _p(b), b.size, _p(out), out.size)
+        return [int(x) for x in out[:n]]
+
+    def evict_lru(self, target):
+        out = np.zeros(1 << 16, dtype=np.uint32)
+        n = lib().vwo_radix_evict_lru(self._h, target, _p(out), out.size)
+        return [int(x) for x in out[:n]]
+
+    def total_blocks(self): return lib().vwo_radix_total_blocks(self._h)
+
+    def lock(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        lib().vwo_radix_lock(self._h, _p(t), t.size)
+
+    def unlock(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        lib().vwo_radix_unlock(self._h, _p(t), t.size)
