@@ -1,0 +1,488 @@
+#!/usr/bin/env python
+"""Paged-KV decode benchmark: KV GB/s (fraction of HBM peak) and tok/s.
+
+One step = append one token per sequence + paged decode attention over every
+layer (the fused vw_paged_decode launch, one per layer), on the
+Qwen2.5-7B-shaped batch by default: 28 layers, 28 query / 4 KV heads,
+head_dim 128, bf16 KV, 16 sequences with context lengths uniform in
+[512, 4096] (seed 1), random non-contiguous block tables, 16-token pages.
+Synthetic inputs (no dataset); K/V/Q drawn N(0,1).
+
+N GPUs (torchrun, one process per GPU): every rank holds its own shard of
+sequences (weak scaling: 16 sequences per GPU), and the per-shard attention
+outputs of each step are all-gathered over NCCL.
+
+--impl reference times the reference's CPU implementation of this path (the
+oracle's restatement of paged_attention_decode + append, f32, all host
+threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: layers, q heads, kv heads, head_dim, seqs per GPU, ctx rule, kv / io dtype, seed
+    "qwen2.5-7b-decode-b16": dict(L=28, Hq=28, Hkv=4, D=128, B=16, ctx=("uniform", 512, 4096),
+                                  kv="bf16", io="bf16", seed=1),
+    "plumbing-l1-b8": dict(L=1, Hq=14, Hkv=2, D=64, B=8, ctx=("uniform", 1, 512),
+                           kv="f16", io="f16", seed=0),
+    "llama3-8b-fp8-b64": dict(L=32, Hq=32, Hkv=8, D=128, B=64, ctx=("loguniform", 1024, 32768),
+                              kv="fp8", io="bf16", seed=3),
+    "llama3-70b-1kvhead-b256": dict(L=80, Hq=8, Hkv=1, D=128, B=256, ctx=("uniform", 2048, 8192),
+                                    kv="bf16", io="bf16", seed=4),
+}
+DEFAULT = "qwen2.5-7b-decode-b16"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def ctx_lengths(w, rank=0):
+    rng = np.random.Generator(np.random.PCG64(w["seed"] * 1000 + rank))
+    kind, lo, hi = w["ctx"]
+    if kind == "uniform":
+        return rng.integers(lo, hi + 1, w["B"]).astype(np.int64)
+    return np.rint(np.exp(rng.uniform(math.log(lo), math.log(hi), w["B"]))).astype(np.int64)
+
+
+def algorithmic_bytes_per_launch(w, seq_lens):
+    """Bytes one layer's append + decode must move (SURVEY-defined formula):
+    KV read ctx*2*Hkv*(D*e+s), append write 2*Hkv*(D*e+s) + new rows read
+    2*Hkv*D*2, q read and o write Hq*D*2 each, block table ceil(ctx/16)*4*Hkv."""
+    e = 1 if w["kv"] == "fp8" else 2
+    s = 4 if w["kv"] == "fp8" else 0
+    H, D, Hq = w["Hkv"], w["D"], w["Hq"]
+    ctx = np.asarray(seq_lens, dtype=np.int64)
+    per = (ctx * 2 * H * (D * e + s) + 2 * H * (D * e + s) + 2 * H * D * 2 + 2 * Hq * D * 2 +
+           ((ctx + 15) // 16) * 4 * H)
+    return int(per.sum())
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+class CpuSample:
+    """The oracle (the reference's paged_attention_decode restated in C++: f32,
+    per-token online softmax in reference order, OpenMP over (seq, head)) plus
+    the append, on one layer of the workload's sequences."""
+
+    def __init__(self, w, seq_lens, threads):
+        import oracle
+        self.o, self.w, self.threads = oracle, w, threads
+        kvk = {"f16": oracle.F16, "bf16": oracle.BF16, "fp8": oracle.FP8}
+        rng = np.random.Generator(np.random.PCG64(w["seed"]))
+        self.seq_lens = np.asarray(seq_lens, dtype=np.int64)
+        pages = (self.seq_lens + 15) // 16
+        NB = int(pages.sum()) + 1
+        self.g = oracle.geom(1, w["Hkv"], w["D"], NB, kvk[w["kv"]], kvk[w["io"]])
+        shape = oracle.pool_shape(self.g)
+        if w["kv"] == "fp8":
+            self.data = rng.integers(0, 255, shape, dtype=np.uint8)
+            self.scales = np.full(shape[:-1], 0.01, dtype=np.float32)
+        else:
+            self.data = oracle.f32_to_io_bits(rng.standard_normal(shape, dtype=np.float32),
+                                              kvk[w["io"]])
+            self.scales = None
+        perm = rng.permutation(NB)
+        self.bt = np.zeros((w["B"], int(pages.max())), dtype=np.uint32)
+        off = 0
+        for b in range(w["B"]):
+            self.bt[b, :pages[b]] = perm[off:off + pages[b]]
+            off += pages[b]
+        io = kvk[w["io"]]
+        self.q = oracle.f32_to_io_bits(rng.standard_normal((w["B"], w["Hq"], w["D"]),
+                                                           dtype=np.float32), io)
+        self.kn = oracle.f32_to_io_bits(rng.standard_normal((w["B"], w["Hkv"], w["D"]),
+                                                            dtype=np.float32), io)
+        pos = self.seq_lens - 1
+        self.slots = np.array([int(self.bt[b, pos[b] // 16]) * 16 + int(pos[b] % 16)
+                               for b in range(w["B"])], dtype=np.int64)
+        self.scale = float(np.float32(1.0) / np.sqrt(np.float32(w["D"])))
+
+    def launch(self, seqs):
+        """Append + decode of one layer over the sequence indices `seqs`;
+        returns the algorithmic bytes moved."""
+        o, w = self.o, self.w
+        o.kv_append(self.g, self.data, self.scales, 0, self.kn[seqs], self.kn[seqs],
+                    self.slots[seqs])
+        o.paged_decode_f32(self.g, self.data, self.scales, 0, self.q[seqs], w["Hq"],
+                           self.bt[seqs], self.seq_lens[seqs].astype(np.uint32), self.scale,
+                           nthreads=self.threads)
+        return algorithmic_bytes_per_launch(w, self.seq_lens[seqs])
+
+
+def cpu_decode_sample(w, seq_lens, launches, threads):
+    cs = CpuSample(w, seq_lens, threads)
+    allseq = np.arange(w["B"])
+    cs.launch(allseq)
+    t0 = time.perf_counter()
+    moved = sum(cs.launch(allseq) for _ in range(launches))
+    dt = time.perf_counter() - t0
+    gbs = moved / dt / 1e9
+    tok_s = w["B"] / (dt / launches * w["L"])
+    return gbs, tok_s, dt, launches
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = cpu_threads()
+    seq_lens = ctx_lengths(w, 0)
+    cs = CpuSample(w, seq_lens, threads)
+    allseq = np.arange(w["B"])
+    t0 = time.perf_counter()
+    cs.launch(allseq)
+    t_full = time.perf_counter() - t0
+    # bounded sample: each step is one layer over a rotating window of
+    # sequences, sized so warm-up + K steps take about a minute at most
+    budget = 60.0
+    per = max(1, min(w["B"], int(w["B"] * budget / ((args.steps + args.warmup) * t_full))))
+    windows = [np.arange(i, i + per) % w["B"] for i in range(0, w["B"] * 64, per)]
+    for i in range(args.warmup):
+        cs.launch(windows[i % len(windows)])
+    moved = 0
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        moved += cs.launch(windows[(i + args.warmup) % len(windows)])
+    dt = time.perf_counter() - t0
+    gbs = moved / dt / 1e9
+    # tok/s of a full step (all layers, all sequences) at the sampled speed
+    full_step_s = algorithmic_bytes_per_launch(w, seq_lens) * w["L"] / (moved / dt)
+    tok_s = w["B"] / full_step_s
+    sample = (f"{args.steps} steps, each 1 of {w['L']} layers over {per} of {w['B']} sequences "
+              f"(rotating); ctx {int(seq_lens.min())}-{int(seq_lens.max())}; oracle f32 "
+              f"reference-order decode + append, {threads} OpenMP threads")
+    line = {
+        "impl": "reference", "metric": "paged decode KV GB/s", "value": round(gbs, 4),
+        "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": w["kv"], "data": "synthetic",
+        "config": {"workload": args.workload, "layers": w["L"], "q_heads": w["Hq"],
+                   "kv_heads": w["Hkv"], "head_dim": w["D"], "seqs_per_gpu": w["B"],
+                   "ctx": list(w["ctx"]), "block_size": 16, "parallelism": "cpu"},
+        "tok_per_s": round(tok_s, 3),
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default=DEFAULT, choices=sorted(WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args, w)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from voidweb_b200.kv import KvPool, PoolSpec
+
+    L, Hq, Hkv, D, B = w["L"], w["Hq"], w["Hkv"], w["D"], w["B"]
+    seq_lens = ctx_lengths(w, rank)                  # each rank: its own shard of sequences
+    pages = (seq_lens + 15) // 16
+    NB = int(pages.sum()) + 64
+    rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919 + rank))
+    perm = rng.permutation(NB)
+    stride = int(pages.max())
+    bt = np.zeros((B, stride), dtype=np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[off:off + pages[b]]
+        off += pages[b]
+
+    spec = PoolSpec(num_layers=L, num_kv_heads=Hkv, head_dim=D, num_blocks=NB, kv_dtype=w["kv"],
+                    io_dtype=w["io"], max_batch=B)
+    pool = KvPool(spec, device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(w["seed"] * 31 + rank)
+    iod = torch.bfloat16 if w["io"] == "bf16" else torch.float16
+    pages_t = pool.pages_u8()
+    if w["kv"] == "fp8":
+        chunk = 1 << 28
+        for o in range(0, pages_t.numel(), chunk):
+            n = min(chunk, pages_t.numel() - o)
+            pages_t[o:o + n].copy_(torch.randint(0, 120, (n,), device=dev, generator=gen,
+                                                 dtype=torch.uint8))
+        pool.scales_f32().fill_(0.01)
+    else:
+        view = pages_t.view(iod)
+        chunk = 1 << 27
+        for o in range(0, view.numel(), chunk):
+            n = min(chunk, view.numel() - o)
+            view[o:o + n].copy_(torch.randn(n, device=dev, generator=gen, dtype=torch.float32))
+    q = torch.randn((L, B, Hq, D), device=dev, generator=gen, dtype=torch.float32).to(iod)
+    kn = torch.randn((L, B, Hkv, D), device=dev, generator=gen, dtype=torch.float32).to(iod)
+    vn = torch.randn((L, B, Hkv, D), device=dev, generator=gen, dtype=torch.float32).to(iod)
+    out = torch.zeros((L, B, Hq, D), device=dev, dtype=iod)
+    bt_d = torch.from_numpy(bt).to(dev)
+    sl_d = torch.from_numpy(seq_lens.astype(np.int32)).to(dev)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s):
+        for layer in range(L):
+            pool.paged_decode(layer, q[layer], bt_d, sl_d, out[layer], k_new=kn[layer],
+                              v_new=vn[layer], stream=s)
+
+    # first launches outside capture (per-device kernel attribute set-up)
+    with torch.cuda.stream(stream):
+        step(stream)
+    stream.synchronize()
+    assert pool.check() == 0, "device bounds check tripped"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(torch.cuda.current_stream())
+    gathered = torch.empty((world, L, B, Hq, D), device=dev, dtype=iod) if world > 1 else None
+
+    def run_step():
+        graph.replay()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run_step()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps):
+            run_step()
+        t1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    assert pool.check() == 0, "device bounds check tripped"
+
+    bytes_launch = algorithmic_bytes_per_launch(w, seq_lens)
+    if world > 1:
+        t = torch.tensor([bytes_launch], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_launch_bytes = float(t.item())
+        tb = torch.tensor([float(B)], device=dev, dtype=torch.float64)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        total_seqs = float(tb.item())
+    else:
+        total_launch_bytes, total_seqs = float(bytes_launch), float(B)
+    step_bytes_all = total_launch_bytes * L
+    value = step_bytes_all / (ms * 1e-3) / 1e9
+    tok_s = total_seqs / (ms * 1e-3)
+    peak, peak_kind = hbm_peak()
+    launch_us = ms * 1e3 / L
+    achieved = bytes_launch / (launch_us * 1e-6) / 1e9
+
+    # per-launch kernel durations with events around each launch (ungraphed pass)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(L)]
+    kdur = []
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            for layer in range(L):
+                evs[layer][0].record(stream)
+                pool.paged_decode(layer, q[layer], bt_d, sl_d, out[layer], k_new=kn[layer],
+                                  v_new=vn[layer], stream=stream)
+                evs[layer][1].record(stream)
+            stream.synchronize()
+            kdur += [a.elapsed_time(b) for a, b in evs]
+    kernel_us = statistics.median(kdur) * 1e3
+
+    # end to end through the public host-buffer API (pinned host memory)
+    e2e = None
+    if args.e2e_steps > 0:
+        hq = q.cpu().pin_memory()
+        hk = kn.cpu().pin_memory()
+        hv = vn.cpu().pin_memory()
+        hbt = torch.from_numpy(bt).pin_memory()
+        hsl = torch.from_numpy(seq_lens.astype(np.int32)).pin_memory()
+        ho = torch.empty_like(out, device="cpu").pin_memory()
+        for _ in range(3):
+            pool.decode_step_host(hq, hk, hv, hbt, hsl, ho, stream=stream)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            pool.decode_step_host(hq, hk, hv, hbt, hsl, ho, stream=stream)
+        e1.record(stream)
+        e1.synchronize()
+        ems = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            m = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(m, op=dist.ReduceOp.MAX)
+            ems = float(m.item())
+        h2d = (hq.numel() + hk.numel() + hv.numel()) * 2 + hbt.numel() * 4 + hsl.numel() * 4
+        e2e = {"value": round(step_bytes_all / (ems * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "ms_per_step": round(ems, 4), "tok_per_s": round(total_seqs / (ems * 1e-3), 1),
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(ho.numel() * 2),
+               "path": "vw_decode_step_host (host buffers, pinned)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        threads = cpu_threads()
+        cs_probe = CpuSample(w, seq_lens, threads)
+        tp = time.perf_counter()
+        cs_probe.launch(np.arange(B))
+        n_launch = max(1, min(200, int(10.0 / max(time.perf_counter() - tp, 1e-3))))
+        del cs_probe
+        gbs, ctok, dt, launches = cpu_decode_sample(w, seq_lens, n_launch, threads)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "tok_per_s": round(ctok, 2),
+               "sample": f"{launches} layer launches (1 of {w['L']} layers, same {B} sequences), "
+                         f"{dt:.1f} s; oracle f32 reference-order decode + append, OpenMP",
+               "block_ops_ns_per_op_1_thread": oracle.bench_block_ops(200000)}
+
+    if rank == 0:
+        line = {
+            "metric": "paged decode KV GB/s", "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": w["kv"], "data": "synthetic",
+            "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv,
+                       "head_dim": D, "seqs_per_gpu": B, "ctx": list(w["ctx"]),
+                       "block_size": 16, "kv_dtype": w["kv"],
+                       "parallelism": f"sequence-shard x{world}" if world > 1 else "single",
+                       "l2": f"inputs larger than L2 ({bytes_launch * L / 1e9:.2f} GB of KV "
+                             f"per step per GPU vs {L2_BYTES / 1e6:.0f} MB L2)",
+                       "graph": "one CUDA graph per step: one fused append+decode launch per layer"},
+            "tok_per_s": round(tok_s, 1),
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_kind": peak_kind, "launch_us_in_region": round(launch_us, 3),
+                         "kernel_us_event_median": round(kernel_us, 3),
+                         "kernel_only_frac": round(bytes_launch / (kernel_us * 1e-6) / 1e9 / peak, 4),
+                         "algorithmic_bytes_per_launch": bytes_launch},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": args.steps * L,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    pool.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

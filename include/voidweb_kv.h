@@ -1,0 +1,270 @@
+/* voidweb_kv.h -- C ABI of the B200 paged KV-cache library (libvoidweb_kv.so).
+ *
+ * Drop-in boundary for VOIDWEB's paged KV-cache hot path.  The engine binds
+ * exactly one symbol of its kernel library, voidweb_forward_pass, through
+ * dlopen/dlsym (engine/ffi.bm:61-77) with the packed ForwardArgs /
+ * SeqDescriptor structs (engine/ffi.bm:15-40); that symbol is declared at the
+ * end of this header.  The op-level entry points below are the library-side
+ * surface behind it: the reference's launcher
+ * launch_paged_attn_decode(q, kv_cache, block_table, seq_lens, o)
+ * (kernels/attention/flash_attention.bm:180-189) plus the append, block-copy,
+ * gather and FP8 operations the engine's block manager and radix tree need
+ * (engine/kv_cache.bm, radix_cache/radix_cache.bm), and the host block manager
+ * and radix tree themselves.
+ *
+ * Conventions (engine/ffi.bm:112-118): every function returns int32_t, 0 on
+ * success, a nonzero vw_status otherwise; vw_last_error() returns a message
+ * for the calling thread.  Device pointers are plain CUDA device addresses;
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * Nothing here throws across the boundary.
+ *
+ * Pool layout in HBM (a block id addresses 16 token slots in every layer,
+ * engine/engine.bm:170-182):
+ *   data  [num_layers][num_blocks][2][num_kv_heads][16][head_dim]
+ *         (2 = K, V; element = f16, bf16, or one E4M3 code byte)
+ *   scale [num_layers][num_blocks][2][num_kv_heads][16]  f32, FP8 pools only
+ */
+#ifndef VOIDWEB_KV_H
+#define VOIDWEB_KV_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VW_API __attribute__((visibility("default")))
+#else
+#define VW_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VW_BLOCK_SIZE 16
+
+typedef enum {
+    VW_OK = 0,
+    VW_ERR_INVALID_ARG = 1,   /* a size, pointer or alignment was rejected before launch */
+    VW_ERR_UNSUPPORTED = 2,   /* a valid but unimplemented shape (e.g. head_dim 96) */
+    VW_ERR_CUDA = 3,          /* a CUDA runtime call failed */
+    VW_ERR_OOM = 4,           /* device or block-pool allocation failed */
+    VW_ERR_DEVICE_CHECK = 5   /* a kernel's bounds check tripped (vw_pool_check) */
+} vw_status;
+
+typedef enum { VW_F16 = 0, VW_BF16 = 1, VW_FP8_E4M3 = 2 } vw_dtype;
+
+/* FP8 codec: the reference's truncating encoder (kernels/norm/rms_norm.bm:98-113)
+ * is the default; OCP E4M3FN round-to-nearest-even saturating is optional. */
+typedef enum { VW_FP8_REFERENCE = 0, VW_FP8_OCP = 1 } vw_fp8_mode;
+
+/* Device error word bits returned by vw_pool_check. */
+#define VW_DEV_ERR_BLOCK_ID 0x1u  /* a block id >= num_blocks was seen and skipped */
+#define VW_DEV_ERR_SEQ_LEN 0x2u   /* seq_len == 0 or longer than its block-table row */
+#define VW_DEV_ERR_TIMEOUT 0x4u   /* a bounded device wait gave up */
+#define VW_DEV_ERR_SLOT 0x8u      /* an append slot was outside the pool */
+
+typedef struct vw_pool vw_pool;
+
+typedef struct {
+    uint32_t num_layers;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;       /* 64 or 128 (FP8 pools: 128) */
+    uint32_t num_blocks;     /* pool size in 16-token blocks, shared by all layers */
+    uint32_t kv_dtype;       /* vw_dtype of the pages */
+    uint32_t io_dtype;       /* VW_F16 or VW_BF16: q, new K/V rows, outputs; equals
+                                kv_dtype unless the pool is FP8 */
+    uint32_t fp8_mode;       /* vw_fp8_mode */
+    uint32_t max_batch;      /* most sequences one decode call may carry (<= 2048) */
+    int32_t device;          /* CUDA device ordinal */
+    uint32_t reserved;       /* must be 0 */
+    void* kv_data;           /* optional caller-owned device buffer (NULL: allocate) */
+    void* kv_scales;         /* optional caller-owned FP8 scale buffer (NULL: allocate) */
+} vw_pool_config;
+
+/* Replaces: the pool the engine sizes in Engine::load (engine/engine.bm:98-104)
+ * and keeps implicitly behind voidweb_forward_pass.  Allocates the pages
+ * (unless given), the split-K scratch and the device error word. */
+VW_API int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out);
+VW_API int32_t vw_pool_destroy(vw_pool* pool);
+/* Device addresses and byte sizes of the page and scale buffers. */
+VW_API int32_t vw_pool_info(const vw_pool* pool, void** kv_data, void** kv_scales,
+                     uint64_t* data_bytes, uint64_t* scale_bytes);
+/* Synchronises the device, returns the device error word in *device_error and
+ * clears it.  Returns VW_ERR_DEVICE_CHECK when the word was nonzero. */
+VW_API int32_t vw_pool_check(vw_pool* pool, uint32_t* device_error);
+
+/* Reshape-and-cache (no reference kernel; paging rule of
+ * flash_attention.bm:132-140).  k_new, v_new: [num_tokens][num_kv_heads][head_dim]
+ * io dtype; slot_mapping: [num_tokens] int64, slot = block*16 + offset, a
+ * negative slot skips the token.  FP8 pools quantise each row on the way in. */
+VW_API int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const void* v_new,
+                     const int64_t* slot_mapping, uint32_t num_tokens, void* stream);
+
+typedef struct {
+    uint32_t layer;
+    uint32_t num_seqs;
+    uint32_t num_q_heads;          /* multiple of num_kv_heads; group <= 16 */
+    uint32_t block_table_stride;   /* entries per block-table row */
+    const void* q;                 /* [num_seqs][num_q_heads][head_dim] io dtype */
+    const uint32_t* block_tables;  /* [num_seqs][block_table_stride] physical block ids */
+    const uint32_t* seq_lens;      /* [num_seqs] context length, including the new token */
+    void* out;                     /* [num_seqs][num_q_heads][head_dim] io dtype */
+    const void* k_new;             /* optional fused append: [num_seqs][num_kv_heads][head_dim] */
+    const void* v_new;             /*   written at position seq_len-1 before attending */
+    float scale;                   /* softmax scale; 0 means 1/sqrt(head_dim) (flash_attention.bm:187) */
+    uint32_t reserved;             /* must be 0 */
+} vw_decode_args;
+
+/* Replaces: launch_paged_attn_decode (kernels/attention/flash_attention.bm:180-189,
+ * kernel :113-162), generalised to GQA and split-K; with k_new/v_new set it is
+ * also the append of the step's token (one launch per layer).  Device pointers;
+ * all of them 16-byte aligned.  One decode at a time per pool (its split-K
+ * scratch is shared). */
+VW_API int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream);
+
+/* Copy-on-write block copy / compaction move (no reference counterpart; the
+ * decision point is the ref-count in engine/kv_cache.bm:94-113).  pairs:
+ * device [num_pairs][2] uint32 (src, dst); every layer's K, V and scales of
+ * src are copied to dst.  Destinations must be distinct and not also sources. */
+VW_API int32_t vw_block_copy(vw_pool* pool, const uint32_t* pairs, uint32_t num_pairs, void* stream);
+
+/* Block-table gather of one sequence (paging walk of flash_attention.bm:132-140):
+ * raw rows out_k, out_v [num_kv_heads][seq_len][head_dim] in the page element
+ * type; FP8 pools also write out_k_scales, out_v_scales [num_kv_heads][seq_len]. */
+VW_API int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block_table,
+                     uint32_t seq_len, void* out_k, void* out_v, float* out_k_scales,
+                     float* out_v_scales, void* stream);
+
+/* One decode step over every layer with HOST buffers (the end-to-end path):
+ * copies the step's inputs host->device, runs append + decode per layer, and
+ * copies the attention outputs device->host before returning. */
+typedef struct {
+    uint32_t num_seqs;
+    uint32_t num_q_heads;
+    uint32_t block_table_stride;
+    uint32_t reserved;
+    const void* q;                 /* host [L][num_seqs][num_q_heads][head_dim] io dtype */
+    const void* k_new;             /* host [L][num_seqs][num_kv_heads][head_dim] */
+    const void* v_new;             /* host [L][num_seqs][num_kv_heads][head_dim] */
+    const uint32_t* block_tables;  /* host [num_seqs][block_table_stride] */
+    const uint32_t* seq_lens;      /* host [num_seqs] (including the new token) */
+    void* out;                     /* host [L][num_seqs][num_q_heads][head_dim] */
+    float scale;
+    uint32_t reserved2;
+} vw_step_host_args;
+VW_API int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* args, void* stream);
+
+/* ---- Host block manager (engine/kv_cache.bm:29-164, C++ implementation) ---- */
+typedef struct vw_block_manager vw_block_manager;
+/* kv_cache.bm:41-58: free list 0..max_blocks, the next alloc pops the last. */
+VW_API int32_t vw_bm_create(uint32_t block_size, uint32_t max_blocks, vw_block_manager** out);
+VW_API int32_t vw_bm_destroy(vw_block_manager* bm);
+VW_API uint32_t vw_bm_capacity(const vw_block_manager* bm);                 /* kv_cache.bm:60-62 */
+VW_API uint32_t vw_bm_free_count(const vw_block_manager* bm);               /* kv_cache.bm:64-66 */
+/* kv_cache.bm:69-78: LIFO pop, ref_count 1; *out = id.  VW_ERR_OOM when empty. */
+VW_API int32_t vw_bm_alloc(vw_block_manager* bm, uint32_t* out);
+/* kv_cache.bm:81-91: all-or-nothing, VW_ERR_OOM when fewer than n are free. */
+VW_API int32_t vw_bm_alloc_seq(vw_block_manager* bm, uint32_t n, uint32_t* out);
+VW_API void vw_bm_incref(vw_block_manager* bm, uint32_t id);                /* kv_cache.bm:94-98 */
+VW_API void vw_bm_decref(vw_block_manager* bm, uint32_t id);                /* kv_cache.bm:101-113 */
+VW_API void vw_bm_free_seq(vw_block_manager* bm, const uint32_t* table, uint32_t n); /* :116-120 */
+VW_API uint32_t vw_bm_ref_count(const vw_block_manager* bm, uint32_t id);   /* 0 when free */
+/* kv_cache.bm:127-138; returns the number of ids (written up to cap). */
+VW_API uint32_t vw_bm_prefix_lookup(const vw_block_manager* bm, const uint32_t* tokens, uint32_t n,
+                             uint32_t* out, uint32_t cap);
+/* kv_cache.bm:142-151 */
+VW_API void vw_bm_register_prefix_block(vw_block_manager* bm, uint32_t id, uint64_t token_hash);
+/* kv_cache.bm:157-164 */
+VW_API uint64_t vw_rolling_hash(uint64_t prev, const uint32_t* tokens, uint32_t n);
+/* Snapshot of the free list in pop order reversed (the last entry pops next). */
+VW_API uint32_t vw_bm_free_list(const vw_block_manager* bm, uint32_t* out, uint32_t cap);
+/* Copy-on-write before appending into table[index] (no reference counterpart):
+ * when that block's ref_count > 1, allocate a fresh block, decref the old one,
+ * store the new id in table[index] and return the (src, dst) pair in
+ * *pair_out, setting *copied = 1; otherwise *copied = 0.  VW_ERR_OOM if no
+ * block is free. */
+VW_API int32_t vw_bm_cow(vw_block_manager* bm, uint32_t* table, uint32_t index, uint32_t* pair_out,
+                  uint32_t* copied);
+/* Compaction plan: moves every used block with id >= used_count to the lowest
+ * free id below used_count (ascending), returning the (src, dst) pairs and
+ * updating the manager (ids, free list back to new()'s order over the tail).
+ * Callers remap their block tables with the same pairs.  Returns the number of
+ * pairs (written up to cap). */
+VW_API uint32_t vw_bm_compact(vw_block_manager* bm, uint32_t* pairs_out, uint32_t cap);
+
+/* ---- Host radix prefix tree (radix_cache/radix_cache.bm:27-285) ---- */
+typedef struct vw_radix vw_radix;
+VW_API int32_t vw_radix_create(uint32_t block_size, uint32_t max_blocks, vw_radix** out);
+VW_API int32_t vw_radix_destroy(vw_radix* r);
+/* radix_cache.bm:77-108 (reuse blocks of a partial edge match included). */
+VW_API uint32_t vw_radix_lookup(vw_radix* r, const uint32_t* tokens, uint32_t n, uint32_t* matched_len,
+                         uint32_t* out, uint32_t cap);
+/* radix_cache.bm:111-179 + :222-228; ids freed by the over-budget eviction are
+ * written to freed_out (up to cap) and counted in the return value. */
+VW_API uint32_t vw_radix_insert(vw_radix* r, const uint32_t* tokens, uint32_t n, const uint32_t* blocks,
+                         uint32_t nb, uint32_t* freed_out, uint32_t cap);
+/* radix_cache.bm:231-240 with the leaf walk done edge by edge; returns ids freed. */
+VW_API uint32_t vw_radix_evict_lru(vw_radix* r, uint32_t target, uint32_t* freed_out, uint32_t cap);
+VW_API uint32_t vw_radix_total_blocks(const vw_radix* r);                   /* radix_cache.bm:242-244 */
+/* Pin / unpin every node on the matched path (ref_count of radix_cache.bm:32). */
+VW_API void vw_radix_lock(vw_radix* r, const uint32_t* tokens, uint32_t n);
+VW_API void vw_radix_unlock(vw_radix* r, const uint32_t* tokens, uint32_t n);
+/* Rename block ids after a compaction: every id equal to pairs[i].src becomes pairs[i].dst. */
+VW_API void vw_radix_remap(vw_radix* r, const uint32_t* pairs, uint32_t num_pairs);
+
+/* Message for the last failure on this thread ("" if none). */
+VW_API const char* vw_last_error(void);
+
+/* ---- The symbol the engine dlopens (engine/ffi.bm:15-40, :68, :113) ---- */
+#pragma pack(push, 1)
+typedef struct {
+    uint64_t seq_id;
+    uint64_t token_ptr;    /* host uint32_t[num_tokens] */
+    uint32_t num_tokens;
+    uint64_t block_ptr;    /* host uint32_t[num_blocks] physical block ids */
+    uint32_t num_blocks;
+    uint8_t is_prefill;
+} SeqDescriptor;
+
+typedef struct {
+    const SeqDescriptor* seqs;
+    uint32_t num_seqs;
+    uint32_t hidden_size;
+    uint32_t num_heads;
+    uint32_t num_kv_heads;
+    uint32_t num_layers;
+    uint32_t vocab_size;
+    uint32_t head_dim;
+    float rope_theta;
+    uint32_t quant_type;   /* QuantScheme ordinal (quantization/quantization.bm:13-19) */
+    float* logits_out;     /* host [num_seqs][vocab_size] */
+} ForwardArgs;
+#pragma pack(pop)
+
+/* Host-side I/O of the attention slice: the transformer layers around
+ * attention (embedding, QKV/O projections, MLP, LM head) are outside this
+ * library, so the caller binds the pool and the per-layer q / new K / new V
+ * rows and the attention output buffer that voidweb_forward_pass reads and
+ * writes (host, shapes as in vw_step_host_args, sequence order = descriptor
+ * order).  The binding is process-wide. */
+VW_API int32_t vw_forward_bind(vw_pool* pool, const void* q, const void* k_new, const void* v_new,
+                        void* attn_out);
+/* Number of tokens already cached for seq_id (e.g. after a prefill done
+ * elsewhere; unseen sequences start at 0).  voidweb_forward_pass advances it
+ * by one per decode step; vw_forward_release forgets the sequence. */
+VW_API int32_t vw_forward_set_seq_len(uint64_t seq_id, uint32_t len);
+VW_API int32_t vw_forward_release(uint64_t seq_id);
+
+/* engine/ffi.bm:68,113: returns 0 on success.  For each decode descriptor
+ * (num_tokens == 1, is_prefill == 0) the new token goes to position
+ * len(seq_id) of the sequence, its host block list (block_ptr, num_blocks) is
+ * the block table, attention covers len(seq_id)+1 tokens on every layer, and
+ * len(seq_id) then grows by one.  Prefill descriptors return
+ * VW_ERR_UNSUPPORTED (nothing runs); logits_out is not written (no LM head in
+ * this library). */
+VW_API int32_t voidweb_forward_pass(const ForwardArgs* args);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOIDWEB_KV_H */

@@ -73,6 +73,7 @@ def lib() -> ctypes.CDLL:
             "vwo_radix_insert": (u32, [vp, vp, u32, vp, u32, vp, u32]),
             "vwo_radix_evict_lru": (u32, [vp, u32, vp, u32]),
             "vwo_radix_lock": (None, [vp, vp, u32]), "vwo_radix_unlock": (None, [vp, vp, u32]),
+            "vwo_bench_block_ops": (None, [u32, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -294,3 +295,14 @@ class RadixCache:
     def unlock(self, tokens):
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         lib().vwo_radix_unlock(self._h, _p(t), t.size)
+
+
+BLOCK_OP_NAMES = ["alloc", "alloc_seq_16", "free_seq_16", "prefix_lookup_16", "radix_insert_256",
+                  "radix_lookup_hit", "radix_lookup_miss", "radix_evict_lru_1", "rolling_hash_16"]
+
+
+def bench_block_ops(iters: int = 200000) -> dict:
+    """ns/op of the reference's block bookkeeping restated in C++ (one thread)."""
+    out = np.zeros(len(BLOCK_OP_NAMES), dtype=np.float64)
+    lib().vwo_bench_block_ops(iters, _p(out))
+    return {k: round(float(v), 1) for k, v in zip(BLOCK_OP_NAMES, out)}

@@ -728,3 +728,82 @@ void vwo_radix_lock(void* p, const uint32_t* tokens, uint32_t n) { lock_path((OR
 void vwo_radix_unlock(void* p, const uint32_t* tokens, uint32_t n) { lock_path((ORadix*)p, tokens, n, -1); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// CPU baseline timing of the reference's block bookkeeping (the operations
+// the reference's benchmark table lists: BENCHMARKS.md:118-135), single
+// thread, ns per operation.  out[0..8] = alloc single, alloc_seq(16),
+// free_seq(16), prefix_lookup(16-block chain), radix insert(256 tokens),
+// radix lookup full hit, radix lookup cold miss, radix evict_lru(1 leaf),
+// rolling_hash(16 tokens).
+// ---------------------------------------------------------------------------
+#include <chrono>
+extern "C" void vwo_bench_block_ops(uint32_t iters, double* out) {
+    using clk = std::chrono::steady_clock;
+    auto ns = [](clk::time_point a, clk::time_point b, double n) {
+        return std::chrono::duration<double, std::nano>(b - a).count() / n;
+    };
+    volatile uint64_t sink = 0;
+    void* bm = vwo_bm_new(16, 1u << 16);
+    auto t0 = clk::now();
+    for (uint32_t i = 0; i < iters; ++i) { int64_t id = vwo_bm_alloc(bm); vwo_bm_decref(bm, (uint32_t)id); }
+    out[0] = ns(t0, clk::now(), iters) / 2.0;           // one alloc (+ one free, halved)
+    uint32_t ids[16];
+    double a_ns = 0, f_ns = 0;
+    for (uint32_t i = 0; i < iters; ++i) {
+        auto a = clk::now(); vwo_bm_alloc_seq(bm, 16, ids); auto b = clk::now();
+        vwo_bm_free_seq(bm, ids, 16); auto c = clk::now();
+        a_ns += std::chrono::duration<double, std::nano>(b - a).count();
+        f_ns += std::chrono::duration<double, std::nano>(c - b).count();
+    }
+    out[1] = a_ns / iters; out[2] = f_ns / iters;
+    std::vector<uint32_t> toks(256);
+    for (uint32_t i = 0; i < 256; ++i) toks[i] = (i * 2654435761u) % 151000u;
+    uint64_t h = 0;
+    for (uint32_t c = 0; c < 16; ++c) {
+        int64_t id = vwo_bm_alloc(bm);
+        h = vwo_rolling_hash(h, &toks[c * 16], 16);
+        vwo_bm_register_prefix_block(bm, (uint32_t)id, h);
+    }
+    uint32_t outids[64];
+    t0 = clk::now();
+    for (uint32_t i = 0; i < iters; ++i) sink += vwo_bm_prefix_lookup(bm, toks.data(), 256, outids, 64);
+    out[3] = ns(t0, clk::now(), iters);
+    vwo_bm_delete(bm);
+    // radix: a cache of 64 finished 256-token sequences sharing a 128-token
+    // prefix, rebuilt every round so the tree size stays bounded (the
+    // reference's insert recounts the whole tree, radix_cache.bm:225)
+    std::vector<uint32_t> seq(toks), blocks(16);
+    uint32_t freed[16], ml = 0;
+    const uint32_t rounds = iters / 64 < 200 ? (iters / 64 ? iters / 64 : 1) : 200;
+    double ins_ns = 0, hit_ns = 0, miss_ns = 0, ev_ns = 0;
+    uint64_t ins_n = 0, hit_n = 0, miss_n = 0, ev_n = 0;
+    uint32_t miss = 151001u;
+    for (uint32_t r = 0; r < rounds; ++r) {
+        void* rx = vwo_radix_new(16, 1u << 30);
+        for (uint32_t i = 0; i < 64; ++i) {
+            for (uint32_t k = 128; k < 256; ++k) seq[k] = (toks[k] + i * 7919u + k) % 151000u;
+            for (uint32_t k = 0; k < 16; ++k) blocks[k] = i * 16 + k;
+            auto a = clk::now();
+            vwo_radix_insert(rx, seq.data(), 256, blocks.data(), 16, freed, 16);
+            ins_ns += std::chrono::duration<double, std::nano>(clk::now() - a).count();
+            ++ins_n;
+        }
+        auto a = clk::now();
+        for (uint32_t i = 0; i < 64; ++i) sink += vwo_radix_lookup(rx, seq.data(), 256, &ml, outids, 64);
+        hit_ns += std::chrono::duration<double, std::nano>(clk::now() - a).count(); hit_n += 64;
+        a = clk::now();
+        for (uint32_t i = 0; i < 64; ++i) sink += vwo_radix_lookup(rx, &miss, 1, &ml, outids, 64);
+        miss_ns += std::chrono::duration<double, std::nano>(clk::now() - a).count(); miss_n += 64;
+        a = clk::now();
+        for (uint32_t i = 0; i < 32; ++i) sink += vwo_radix_evict_lru(rx, 1, freed, 16);
+        ev_ns += std::chrono::duration<double, std::nano>(clk::now() - a).count(); ev_n += 32;
+        vwo_radix_delete(rx);
+    }
+    out[4] = ins_ns / ins_n; out[5] = hit_ns / hit_n; out[6] = miss_ns / miss_n; out[7] = ev_ns / ev_n;
+    t0 = clk::now();
+    uint64_t hh = 0;
+    for (uint32_t i = 0; i < iters; ++i) hh = vwo_rolling_hash(hh, &toks[(i & 7) * 16], 16);
+    out[8] = ns(t0, clk::now(), iters);
+    sink += hh;
+}

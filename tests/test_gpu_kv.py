@@ -1,0 +1,288 @@
+"""GPU parity tests: every CUDA path of libvoidweb_kv.so against the oracle.
+
+Bars: bit-exact for append, gather, block copy and FP8 codes/scales;
+attention outputs within |gpu - ref| <= 2e-3 + 1e-2 * |ref| of the fp64
+oracle (the fp32-reference tolerance of bf16 attention, applied to f16 and to
+FP8 pages too, where ref is computed from the same dequantised codes).
+"""
+import zlib
+
+import numpy as np
+import pytest
+
+import oracle
+from tests import kvgen
+from tests.kvgen import BF16, F16, FP8
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def make_pool(c, dev):
+    from voidweb_b200.kv import KvPool, PoolSpec
+    pool = KvPool(PoolSpec(**kvgen.pool_spec_kwargs(c)), device=dev.index or 0)
+    upload_pool(pool, c)
+    return pool
+
+
+def upload_pool(pool, c):
+    pool.pages_u8().copy_(torch.from_numpy(np.ascontiguousarray(c.data).view(np.uint8).ravel()))
+    if c.kv == FP8:
+        pool.scales_f32().copy_(torch.from_numpy(c.scales.ravel()))
+    torch.cuda.synchronize()
+
+
+def download_pool(pool, c):
+    raw = pool.pages_u8().cpu().numpy()
+    data = raw.view(np.uint8 if c.kv == FP8 else np.uint16).reshape(oracle.pool_shape(c.geom))
+    scales = pool.scales_f32().cpu().numpy().reshape(oracle.pool_shape(c.geom)[:-1]) \
+        if c.kv == FP8 else None
+    return data, scales
+
+
+def t16(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev)
+
+
+def tu32(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a).astype(np.int32)).to(dev)
+
+
+def check_close(got_bits, ref64, io, what=""):
+    got = oracle.io_bits_to_f32(got_bits, io).astype(np.float64)
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    err = np.abs(got - ref64)
+    bound = ATOL + RTOL * np.abs(ref64)
+    bad = err > bound
+    assert not bad.any(), (f"{what}: {bad.sum()} of {bad.size} outside tolerance, "
+                           f"max err {err.max():.3g} (worst ratio {(err / bound).max():.3g})")
+
+
+def run_decode(pool, c, layer, dev, fused=False):
+    q = t16(c.q[layer], dev)
+    out = torch.zeros_like(q)
+    bt, sl = tu32(c.block_tables, dev), tu32(c.seq_lens, dev)
+    kn = t16(c.k_new[layer], dev) if fused else None
+    vn = t16(c.v_new[layer], dev) if fused else None
+    pool.paged_decode(layer, q, bt, sl, out, k_new=kn, v_new=vn)
+    torch.cuda.synchronize()
+    return out.cpu().numpy().view(np.uint16)
+
+
+DECODE_CASES = [
+    # (name, L, Hkv, D, Hq, B, ctx_lo, ctx_hi, kv, io)
+    ("plumbing_f16_d64_g7", 1, 2, 64, 14, 8, 1, 512, F16, F16),
+    ("qwen_bf16_d128_g7", 1, 4, 128, 28, 6, 300, 1500, BF16, BF16),
+    ("llama70b_bf16_g8", 1, 2, 128, 16, 5, 100, 900, BF16, BF16),
+    ("g16_two_ntiles", 1, 1, 128, 16, 4, 20, 700, BF16, BF16),
+    ("bf16_d64", 1, 3, 64, 12, 7, 1, 300, BF16, BF16),
+    ("f16_d128_g4", 1, 2, 128, 8, 6, 1, 800, F16, F16),
+    ("fp8_llama8b_g4", 1, 2, 128, 8, 5, 50, 900, FP8, BF16),
+    ("fp8_f16io_g8", 1, 1, 128, 8, 4, 1, 400, FP8, F16),
+]
+
+
+@pytest.mark.parametrize("case", DECODE_CASES, ids=[c[0] for c in DECODE_CASES])
+def test_decode_matches_fp64(dev, case):
+    name, L, Hkv, D, Hq, B, lo, hi, kv, io = case
+    c = kvgen.make_case(zlib.crc32(name.encode()) % 1000, L, Hkv, D, Hq, B, lo, hi, kv, io)
+    pool = make_pool(c, dev)
+    got = run_decode(pool, c, 0, dev)
+    assert pool.check() == 0
+    ref = oracle.paged_decode_f64(c.geom, c.data, c.scales, 0, c.q[0], Hq, c.block_tables,
+                                  c.seq_lens, 1.0 / np.sqrt(D))
+    check_close(got, ref, io, name)
+    # the reference's own f32 order agrees with the fp64 reference too
+    f32 = oracle.paged_decode_f32(c.geom, c.data, c.scales, 0, c.q[0], Hq, c.block_tables,
+                                  c.seq_lens, float(np.float32(1.0) / np.sqrt(np.float32(D))))
+    check_close(f32, ref, io, name + " (oracle f32 order)")
+    pool.close()
+
+
+@pytest.mark.parametrize("kv,io,mode", [(F16, F16, 0), (BF16, BF16, 0), (FP8, BF16, 0),
+                                        (FP8, BF16, 1), (FP8, F16, 0)])
+def test_fused_append_decode(dev, kv, io, mode):
+    D = 128 if kv != F16 else 64
+    c = kvgen.make_case(7 + kv * 3 + mode, 2, 2, D, 8, 6, 1, 600, kv, io, fp8_mode=mode)
+    pool = make_pool(c, dev)
+    got = [run_decode(pool, c, layer, dev, fused=True) for layer in range(c.L)]
+    assert pool.check() == 0
+    data, scales = c.data.copy(), None if c.scales is None else c.scales.copy()
+    slots = kvgen.new_token_slots(c)
+    for layer in range(c.L):
+        oracle.kv_append(c.geom, data, scales, layer, c.k_new[layer], c.v_new[layer], slots)
+    gdata, gscales = download_pool(pool, c)
+    assert np.array_equal(gdata, data), "pages after fused append differ from the oracle"
+    if kv == FP8:
+        assert np.array_equal(gscales.view(np.uint32), scales.view(np.uint32))
+    for layer in range(c.L):
+        ref = oracle.paged_decode_f64(c.geom, data, scales, layer, c.q[layer], c.Hq,
+                                      c.block_tables, c.seq_lens, 1.0 / np.sqrt(D))
+        check_close(got[layer], ref, io, f"layer {layer}")
+    pool.close()
+
+
+@pytest.mark.parametrize("kv,io,mode", [(F16, F16, 0), (BF16, BF16, 0), (FP8, BF16, 0),
+                                        (FP8, BF16, 1), (FP8, F16, 1)])
+def test_append_bit_exact(dev, kv, io, mode):
+    D = 128
+    c = kvgen.make_case(21 + kv + mode, 3, 2, D, 4, 5, 10, 200, kv, io, fp8_mode=mode)
+    pool = make_pool(c, dev)
+    rng = np.random.default_rng(5)
+    n = 70
+    slots = rng.choice(c.NB * 16, n, replace=False).astype(np.int64)
+    slots[[3, 17, 40]] = -1                               # padding tokens are skipped
+    k = kvgen.io_bits(rng, (n, c.Hkv, D), io, 3.0, True)
+    v = kvgen.io_bits(rng, (n, c.Hkv, D), io, 3.0, True)
+    k[0, 0, :] = 0                                        # amax == 0 -> scale 1
+    pool.append(1, t16(k, dev), t16(v, dev), torch.from_numpy(slots).to(dev))
+    assert pool.check() == 0
+    data, scales = c.data.copy(), None if c.scales is None else c.scales.copy()
+    oracle.kv_append(c.geom, data, scales, 1, k, v, slots)
+    gdata, gscales = download_pool(pool, c)
+    assert np.array_equal(gdata, data)
+    if kv == FP8:
+        assert np.array_equal(gscales.view(np.uint32), scales.view(np.uint32))
+    pool.close()
+
+
+@pytest.mark.parametrize("kv", [BF16, FP8])
+def test_gather_and_block_copy_bit_exact(dev, kv):
+    io = BF16
+    c = kvgen.make_case(33 + kv, 2, 2, 128, 4, 4, 17, 300, kv, io)
+    pool = make_pool(c, dev)
+    b = 2
+    n = int(c.seq_lens[b])
+    ok, ov, ks, vs = pool.gather(1, tu32(c.block_tables[b], dev), n)
+    rk, rv, rks, rvs = oracle.kv_gather(c.geom, c.data, c.scales, 1, c.block_tables[b], n)
+    dt = np.uint8 if kv == FP8 else np.uint16
+    assert np.array_equal(ok.cpu().numpy().view(dt), rk)
+    assert np.array_equal(ov.cpu().numpy().view(dt), rv)
+    if kv == FP8:
+        assert np.array_equal(ks.cpu().numpy(), rks) and np.array_equal(vs.cpu().numpy(), rvs)
+    # copy-on-write / compaction copies (distinct destinations, not sources)
+    used = set(c.block_tables[:, :].ravel().tolist())
+    free = [i for i in range(c.NB) if i not in used] or [c.NB - 1]
+    srcs = [int(c.block_tables[0, 0]), int(c.block_tables[1, 1])]
+    dsts = free[:2] if len(free) >= 2 else [free[0], int(c.block_tables[3, 0])]
+    pairs = np.array(list(zip(srcs, dsts)), dtype=np.uint32)
+    pool.block_copy(torch.from_numpy(pairs.astype(np.int32)).to(dev))
+    assert pool.check() == 0
+    data, scales = c.data.copy(), None if c.scales is None else c.scales.copy()
+    oracle.block_copy(c.geom, data, scales, pairs)
+    gdata, gscales = download_pool(pool, c)
+    assert np.array_equal(gdata, data)
+    if kv == FP8:
+        assert np.array_equal(gscales.view(np.uint32), scales.view(np.uint32))
+    pool.close()
+
+
+def test_split_k_extremes(dev):
+    """Very long and very short sequences in one batch: segments cut across many
+    CTAs and CTAs spanning many segments; repeated launches reuse the arrival
+    counters (they must reset to zero)."""
+    ctx = [1, 2, 15, 16, 17, 31, 32, 33, 9000, 3, 1, 4097, 64, 5, 12000]
+    c = kvgen.make_case(99, 1, 2, 128, 14, len(ctx), 0, 0, BF16, BF16, ctx=ctx)
+    pool = make_pool(c, dev)
+    first = run_decode(pool, c, 0, dev)
+    for _ in range(3):
+        again = run_decode(pool, c, 0, dev)
+        assert np.array_equal(first, again), "repeated launch changed the result"
+    assert pool.check() == 0
+    ref = oracle.paged_decode_f64(c.geom, c.data, None, 0, c.q[0], c.Hq, c.block_tables,
+                                  c.seq_lens, 1.0 / np.sqrt(128), nthreads=0)
+    check_close(first, ref, BF16, "split-K extremes")
+    pool.close()
+
+
+def test_single_sequence_ctx1(dev):
+    c = kvgen.make_case(5, 1, 1, 128, 1, 1, 1, 1, BF16, BF16)
+    pool = make_pool(c, dev)
+    got = run_decode(pool, c, 0, dev)
+    # one token: softmax weight 1, output is exactly V row 0
+    blk = int(c.block_tables[0, 0])
+    assert np.array_equal(got[0, 0], c.data[0, blk, 1, 0, 0])
+    pool.close()
+
+
+def test_bad_block_id_and_seq_len_are_flagged(dev):
+    from voidweb_b200 import _lib as C
+    c = kvgen.make_case(8, 1, 2, 128, 4, 3, 20, 60, BF16, BF16)
+    pool = make_pool(c, dev)
+    bt = c.block_tables.copy()
+    bt[1, 0] = c.NB + 7                        # outside the pool
+    q = t16(c.q[0], dev)
+    out = torch.zeros_like(q)
+    pool.paged_decode(0, q, tu32(bt, dev), tu32(c.seq_lens, dev), out,
+                      k_new=t16(c.k_new[0], dev), v_new=t16(c.v_new[0], dev))
+    err = pool.check()
+    assert err & C.DEV_ERR_BLOCK_ID
+    assert not (err & C.DEV_ERR_TIMEOUT)
+    sl = c.seq_lens.copy()
+    sl[2] = 0
+    pool.paged_decode(0, q, tu32(c.block_tables, dev), tu32(sl, dev), out)
+    assert pool.check() & C.DEV_ERR_SEQ_LEN
+    # untouched data outside the pool: the bad id was skipped, not written
+    pool.close()
+
+
+def test_host_step_and_forward_pass_match_device_path(dev):
+    from voidweb_b200 import KernelLib
+    from voidweb_b200 import _lib as C
+    c = kvgen.make_case(12, 3, 2, 128, 8, 4, 5, 200, BF16, BF16)
+    pool = make_pool(c, dev)
+    dev_out = [run_decode(pool, c, layer, dev, fused=True) for layer in range(c.L)]
+    upload_pool(pool, c)
+    out = np.zeros_like(c.q)
+    pool.decode_step_host(torch.from_numpy(c.q.view(np.int16)),
+                          torch.from_numpy(c.k_new.view(np.int16)),
+                          torch.from_numpy(c.v_new.view(np.int16)),
+                          torch.from_numpy(c.block_tables.astype(np.int32)),
+                          torch.from_numpy(c.seq_lens.astype(np.int32)),
+                          torch.from_numpy(out.view(np.int16)))
+    for layer in range(c.L):
+        assert np.array_equal(out[layer], dev_out[layer])
+    # the engine-facing symbol: same step through voidweb_forward_pass
+    upload_pool(pool, c)
+    out2 = np.zeros_like(c.q)
+    L = C.lib()
+    L.vw_forward_bind(pool.handle, c.q.ctypes.data, c.k_new.ctypes.data, c.v_new.ctypes.data,
+                      out2.ctypes.data)
+    for b in range(c.B):
+        L.vw_forward_set_seq_len(1000 + b, int(c.seq_lens[b]) - 1)
+    kl = KernelLib.open(C.LIB_PATH)
+    seqs = [(1000 + b, 7, c.block_tables[b, : (int(c.seq_lens[b]) + 15) // 16])
+            for b in range(c.B)]
+    kl.forward_pass(dict(num_heads=c.Hq, num_kv_heads=c.Hkv, num_layers=c.L, head_dim=c.D),
+                    seqs)
+    for layer in range(c.L):
+        assert np.array_equal(out2[layer], dev_out[layer])
+    for b in range(c.B):
+        L.vw_forward_release(1000 + b)
+    L.vw_forward_bind(None, None, None, None, None)
+    pool.close()
+
+
+def test_full_size_qwen_layer_sampled(dev):
+    """Qwen2.5-7B decode shapes at full size (B 16, ctx U[512,4096], 28/4 heads,
+    D 128, bf16), one layer: fused append + decode, checked on every sequence
+    against the fp64 oracle."""
+    c = kvgen.make_case(1, 1, 4, 128, 28, 16, 512, 4096, BF16, BF16)
+    pool = make_pool(c, dev)
+    got = run_decode(pool, c, 0, dev, fused=True)
+    assert pool.check() == 0
+    data = c.data.copy()
+    oracle.kv_append(c.geom, data, None, 0, c.k_new[0], c.v_new[0], kvgen.new_token_slots(c))
+    ref = oracle.paged_decode_f64(c.geom, data, None, 0, c.q[0], c.Hq, c.block_tables,
+                                  c.seq_lens, 1.0 / np.sqrt(128))
+    check_close(got, ref, BF16, "qwen full-size layer")
+    pool.close()

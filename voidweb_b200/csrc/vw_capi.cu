@@ -1,0 +1,582 @@
+// vw_capi.cu -- the C ABI of libvoidweb_kv.so (declared in include/voidweb_kv.h):
+// pool lifetime, argument validation, TMA descriptor encoding, kernel dispatch,
+// the host-buffer decode step, and the voidweb_forward_pass shim the engine
+// dlopens (engine/ffi.bm:61-77, :113).
+//
+// Every entry point validates its arguments on the host before any launch and
+// reports failure through an int32 status plus a thread-local message, as the
+// engine expects (engine/ffi.bm:112-118); nothing throws across the boundary.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/voidweb_kv.h"
+#include "vw_internal.h"
+
+using namespace vw;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int32_t cuda_fail(cudaError_t e, const char* what) {
+    return fail(VW_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// RAII-free device scope switch: the library never leaves the caller's
+// current device changed.
+struct DeviceScope {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceScope() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+struct vw_pool {
+    vw_pool_config cfg{};
+    PoolGeom geom{};
+    uint8_t* data = nullptr;
+    float* scales = nullptr;
+    bool own_data = false, own_scales = false;
+    uint64_t data_bytes = 0, scale_bytes = 0;
+    alignas(64) CUtensorMap tmap;
+    float* part_o = nullptr;
+    float* part_ml = nullptr;
+    uint32_t* counters = nullptr;
+    uint32_t* err = nullptr;
+    int grid = 0;
+    // staging for vw_decode_step_host (grow-only)
+    uint8_t* stage = nullptr;
+    size_t stage_bytes = 0;
+    cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
+    std::vector<cudaEvent_t> ev_in, ev_done;
+    cudaEvent_t ev_entry = nullptr, ev_exit = nullptr;
+};
+
+namespace {
+
+void pool_free_all(vw_pool* p) {
+    if (p->own_data && p->data) cudaFree(p->data);
+    if (p->own_scales && p->scales) cudaFree(p->scales);
+    if (p->part_o) cudaFree(p->part_o);
+    if (p->part_ml) cudaFree(p->part_ml);
+    if (p->counters) cudaFree(p->counters);
+    if (p->err) cudaFree(p->err);
+    if (p->stage) cudaFree(p->stage);
+    if (p->s_h2d) cudaStreamDestroy(p->s_h2d);
+    if (p->s_d2h) cudaStreamDestroy(p->s_d2h);
+    for (auto e : p->ev_in) cudaEventDestroy(e);
+    for (auto e : p->ev_done) cudaEventDestroy(e);
+    if (p->ev_entry) cudaEventDestroy(p->ev_entry);
+    if (p->ev_exit) cudaEventDestroy(p->ev_exit);
+}
+
+int32_t encode_pool_map(vw_pool* p) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(VW_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const PoolGeom& g = p->geom;
+    const uint64_t eb = elem_bytes(g.kv_kind);
+    const uint64_t row = (uint64_t)g.head_dim * eb;
+    const uint64_t chunk_elems = 128 / eb;
+    cuuint64_t dims[5] = {chunk_elems, row / 128, 16, 2ull * g.num_kv_heads,
+                          (cuuint64_t)g.num_layers * g.num_blocks};
+    cuuint64_t strides[4] = {128, row, 16 * row, 2ull * g.num_kv_heads * 16 * row};
+    cuuint32_t box[5] = {(cuuint32_t)chunk_elems, 1, 16, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(&p->tmap, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                    5, p->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VW_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return VW_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* vw_last_error(void) { return g_last_error.c_str(); }
+
+int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
+    if (!cfg || !out) return fail(VW_ERR_INVALID_ARG, "vw_pool_create: null argument");
+    *out = nullptr;
+    const vw_pool_config& c = *cfg;
+    if (c.reserved != 0) return fail(VW_ERR_INVALID_ARG, "vw_pool_create: reserved must be 0");
+    if (c.num_layers == 0 || c.num_kv_heads == 0 || c.num_blocks == 0)
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: layers, kv heads and blocks must be > 0");
+    if (c.kv_dtype > VW_FP8_E4M3 || (c.io_dtype != VW_F16 && c.io_dtype != VW_BF16))
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: bad kv_dtype %u / io_dtype %u",
+                    c.kv_dtype, c.io_dtype);
+    if (c.kv_dtype != VW_FP8_E4M3 && c.kv_dtype != c.io_dtype)
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: f16/bf16 pools need io_dtype == kv_dtype");
+    if (c.fp8_mode > VW_FP8_OCP) return fail(VW_ERR_INVALID_ARG, "vw_pool_create: bad fp8_mode");
+    if (c.head_dim != 64 && c.head_dim != 128)
+        return fail(VW_ERR_UNSUPPORTED, "vw_pool_create: head_dim %u (64 or 128)", c.head_dim);
+    if (c.kv_dtype == VW_FP8_E4M3 && c.head_dim != 128)
+        return fail(VW_ERR_UNSUPPORTED, "vw_pool_create: FP8 pools need head_dim 128");
+    if (c.max_batch == 0 || c.max_batch > (uint32_t)kMaxBatchPerLaunch)
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: max_batch must be 1..%d", kMaxBatchPerLaunch);
+    if ((uint64_t)c.num_layers * c.num_blocks > 0x7FFFFFFFull)
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: num_layers * num_blocks exceeds 2^31-1");
+    if (c.kv_data && !aligned(c.kv_data, 256))
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: kv_data must be 256-byte aligned");
+    if (c.kv_scales && !aligned(c.kv_scales, 256))
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: kv_scales must be 256-byte aligned");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || c.device < 0 || c.device >= ndev)
+        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: device %d not available", c.device);
+    DeviceScope ds(c.device);
+    if (!ds.ok) return fail(VW_ERR_CUDA, "vw_pool_create: cudaSetDevice failed");
+
+    vw_pool* p = new vw_pool();
+    p->cfg = c;
+    p->geom = PoolGeom{c.num_layers, c.num_kv_heads, c.head_dim, c.num_blocks, c.kv_dtype,
+                       c.io_dtype, c.fp8_mode};
+    const uint64_t eb = elem_bytes(c.kv_dtype);
+    const uint64_t rows = (uint64_t)c.num_layers * c.num_blocks * 2 * c.num_kv_heads * 16;
+    p->data_bytes = rows * c.head_dim * eb;
+    p->scale_bytes = c.kv_dtype == VW_FP8_E4M3 ? rows * 4 : 0;
+    cudaError_t e;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.device);
+    p->grid = sms > 0 ? sms : 148;
+    if (c.kv_data) {
+        p->data = static_cast<uint8_t*>(c.kv_data);
+    } else {
+        if ((e = cudaMalloc(&p->data, p->data_bytes)) != cudaSuccess) {
+            delete p;
+            return fail(VW_ERR_OOM, "vw_pool_create: %llu bytes of pages: %s",
+                        (unsigned long long)p->data_bytes, cudaGetErrorString(e));
+        }
+        p->own_data = true;
+    }
+    if (p->scale_bytes) {
+        if (c.kv_scales) {
+            p->scales = static_cast<float*>(c.kv_scales);
+        } else if ((e = cudaMalloc(&p->scales, p->scale_bytes)) == cudaSuccess) {
+            p->own_scales = true;
+        } else {
+            pool_free_all(p);
+            delete p;
+            return fail(VW_ERR_OOM, "vw_pool_create: scales: %s", cudaGetErrorString(e));
+        }
+    }
+    const size_t n_o = decode_scratch_floats_o(p->grid, c.head_dim);
+    const size_t n_ml = decode_scratch_floats_ml(p->grid);
+    const size_t n_ctr = (size_t)c.max_batch * c.num_kv_heads;
+    if ((e = cudaMalloc(&p->part_o, n_o * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&p->part_ml, n_ml * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&p->counters, n_ctr * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&p->err, 4)) != cudaSuccess) {
+        pool_free_all(p);
+        delete p;
+        return fail(VW_ERR_OOM, "vw_pool_create: scratch: %s", cudaGetErrorString(e));
+    }
+    if ((e = cudaMemset(p->counters, 0, n_ctr * 4)) != cudaSuccess ||
+        (e = cudaMemset(p->err, 0, 4)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        pool_free_all(p);
+        delete p;
+        return cuda_fail(e, "vw_pool_create: memset");
+    }
+    int32_t rc = encode_pool_map(p);
+    if (rc != VW_OK) {
+        pool_free_all(p);
+        delete p;
+        return rc;
+    }
+    *out = p;
+    return VW_OK;
+}
+
+int32_t vw_pool_destroy(vw_pool* pool) {
+    if (!pool) return VW_OK;
+    DeviceScope ds(pool->cfg.device);
+    cudaDeviceSynchronize();
+    pool_free_all(pool);
+    delete pool;
+    return VW_OK;
+}
+
+int32_t vw_pool_info(const vw_pool* pool, void** kv_data, void** kv_scales, uint64_t* data_bytes,
+                     uint64_t* scale_bytes) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_pool_info: null pool");
+    if (kv_data) *kv_data = pool->data;
+    if (kv_scales) *kv_scales = pool->scales;
+    if (data_bytes) *data_bytes = pool->data_bytes;
+    if (scale_bytes) *scale_bytes = pool->scale_bytes;
+    return VW_OK;
+}
+
+int32_t vw_pool_check(vw_pool* pool, uint32_t* device_error) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_pool_check: null pool");
+    DeviceScope ds(pool->cfg.device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "vw_pool_check: synchronize");
+    uint32_t w = 0;
+    if ((e = cudaMemcpy(&w, pool->err, 4, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "vw_pool_check: read");
+    if ((e = cudaMemset(pool->err, 0, 4)) != cudaSuccess) return cuda_fail(e, "vw_pool_check: clear");
+    if (device_error) *device_error = w;
+    if (w) return fail(VW_ERR_DEVICE_CHECK, "device bounds check flags 0x%x", w);
+    return VW_OK;
+}
+
+int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const void* v_new,
+                     const int64_t* slot_mapping, uint32_t num_tokens, void* stream) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_kv_append: null pool");
+    if (layer >= pool->geom.num_layers)
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_append: layer %u >= %u", layer, pool->geom.num_layers);
+    if (num_tokens == 0) return VW_OK;
+    if (!k_new || !v_new || !slot_mapping)
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_append: null device pointer");
+    if (!aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(slot_mapping, 8))
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_append: k_new/v_new must be 16-byte aligned");
+    DeviceScope ds(pool->cfg.device);
+    cudaError_t e = launch_kv_append(pool->geom, pool->data, pool->scales, layer, k_new, v_new,
+                                     slot_mapping, num_tokens, pool->err,
+                                     static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_kv_append launch");
+}
+
+static int32_t decode_validate(const vw_pool* pool, const vw_decode_args* a) {
+    if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: null argument");
+    const PoolGeom& g = pool->geom;
+    if (a->reserved != 0) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: reserved must be 0");
+    if (a->layer >= g.num_layers)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: layer %u >= %u", a->layer, g.num_layers);
+    if (a->num_seqs > pool->cfg.max_batch)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: num_seqs %u > max_batch %u", a->num_seqs,
+                    pool->cfg.max_batch);
+    if (a->num_q_heads == 0 || a->num_q_heads % g.num_kv_heads != 0)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: num_q_heads %u not a multiple of %u",
+                    a->num_q_heads, g.num_kv_heads);
+    if (a->num_q_heads / g.num_kv_heads > 16)
+        return fail(VW_ERR_UNSUPPORTED, "vw_paged_decode: GQA group %u > 16",
+                    a->num_q_heads / g.num_kv_heads);
+    if (a->block_table_stride == 0)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: block_table_stride must be > 0");
+    if (!a->q || !a->block_tables || !a->seq_lens || !a->out)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: null device pointer");
+    if ((a->k_new == nullptr) != (a->v_new == nullptr))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: k_new and v_new go together");
+    if (!aligned(a->q, 16) || !aligned(a->out, 16) || !aligned(a->block_tables, 4) ||
+        !aligned(a->seq_lens, 4) || (a->k_new && (!aligned(a->k_new, 16) || !aligned(a->v_new, 16))))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: misaligned pointer");
+    if (!(a->scale >= 0.0f) || std::isinf(a->scale))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: bad scale");
+    return VW_OK;
+}
+
+static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_t s) {
+    const PoolGeom& g = pool->geom;
+    DecodeLaunch L{};
+    DecodeParams& p = L.p;
+    p.q = a->q;
+    p.out = a->out;
+    p.k_new = a->k_new;
+    p.v_new = a->v_new;
+    p.block_tables = a->block_tables;
+    p.seq_lens = a->seq_lens;
+    p.kv_data = pool->data;
+    p.kv_scales = pool->scales;
+    p.part_o = pool->part_o;
+    p.part_ml = pool->part_ml;
+    p.counters = pool->counters;
+    p.err = pool->err;
+    p.B = a->num_seqs;
+    p.Hq = a->num_q_heads;
+    p.Hkv = g.num_kv_heads;
+    p.group = a->num_q_heads / g.num_kv_heads;
+    p.num_blocks = g.num_blocks;
+    p.layer = a->layer;
+    p.bt_stride = a->block_table_stride;
+    p.fp8_ocp = g.fp8_ocp;
+    // reference scale: 1.0 / (HEAD_DIM as f32).sqrt() (flash_attention.bm:187)
+    const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    L.tmap = &pool->tmap;
+    L.head_dim = g.head_dim;
+    L.kv_kind = g.kv_kind;
+    L.io_kind = g.io_kind;
+    L.grid = pool->grid;
+    L.stream = s;
+    cudaError_t e = launch_paged_decode(L);
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_paged_decode launch");
+}
+
+int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream) {
+    int32_t rc = decode_validate(pool, args);
+    if (rc != VW_OK) return rc;
+    if (args->num_seqs == 0) return VW_OK;
+    DeviceScope ds(pool->cfg.device);
+    return decode_launch(pool, args, static_cast<cudaStream_t>(stream));
+}
+
+int32_t vw_block_copy(vw_pool* pool, const uint32_t* pairs, uint32_t num_pairs, void* stream) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_block_copy: null pool");
+    if (num_pairs == 0) return VW_OK;
+    if (!pairs || !aligned(pairs, 8)) return fail(VW_ERR_INVALID_ARG, "vw_block_copy: bad pairs");
+    DeviceScope ds(pool->cfg.device);
+    cudaError_t e = launch_block_copy(pool->geom, pool->data, pool->scales, pairs, num_pairs,
+                                      pool->err, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_block_copy launch");
+}
+
+int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block_table, uint32_t seq_len,
+                     void* out_k, void* out_v, float* out_k_scales, float* out_v_scales,
+                     void* stream) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: null pool");
+    if (layer >= pool->geom.num_layers) return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: bad layer");
+    if (seq_len == 0) return VW_OK;
+    if (!block_table || !out_k || !out_v || !aligned(out_k, 16) || !aligned(out_v, 16))
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: bad output pointers");
+    if (pool->geom.kv_kind == kFP8 && (!out_k_scales || !out_v_scales))
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: FP8 pools need scale outputs");
+    DeviceScope ds(pool->cfg.device);
+    cudaError_t e = launch_kv_gather(pool->geom, pool->data, pool->scales, layer, block_table,
+                                     seq_len, out_k, out_v, out_k_scales, out_v_scales, pool->err,
+                                     static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_kv_gather launch");
+}
+
+// ---------------------------------------------------------------------------
+// Host-buffer step: H2D of the step's inputs, append + decode on every layer,
+// D2H of the outputs.  Layers are processed in chunks so the copies of chunk
+// c+1 and the read-back of chunk c-1 overlap the kernels of chunk c.
+// ---------------------------------------------------------------------------
+
+int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* stream) {
+    if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: null argument");
+    if (a->reserved || a->reserved2) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: reserved");
+    const PoolGeom& g = pool->geom;
+    const uint32_t B = a->num_seqs, Hq = a->num_q_heads, L = g.num_layers, D = g.head_dim;
+    if (B == 0) return VW_OK;
+    if (!a->q || !a->k_new || !a->v_new || !a->block_tables || !a->seq_lens || !a->out)
+        return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: null host pointer");
+    const size_t qb = (size_t)B * Hq * D * 2, kb = (size_t)B * g.num_kv_heads * D * 2;
+    const size_t btb = (size_t)B * a->block_table_stride * 4, slb = (size_t)B * 4;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    const size_t need = up(qb * L) * 2 + up(kb * L) * 2 + up(btb) + up(slb);
+    DeviceScope ds(pool->cfg.device);
+    cudaError_t e;
+    if (pool->stage_bytes < need) {
+        if (pool->stage) cudaFree(pool->stage);
+        pool->stage = nullptr;
+        pool->stage_bytes = 0;
+        if ((e = cudaMalloc(&pool->stage, need)) != cudaSuccess)
+            return fail(VW_ERR_OOM, "vw_decode_step_host: staging: %s", cudaGetErrorString(e));
+        pool->stage_bytes = need;
+    }
+    if (!pool->s_h2d) {
+        if (cudaStreamCreateWithFlags(&pool->s_h2d, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&pool->s_d2h, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&pool->ev_entry, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&pool->ev_exit, cudaEventDisableTiming) != cudaSuccess)
+            return fail(VW_ERR_CUDA, "vw_decode_step_host: stream/event creation failed");
+    }
+    const uint32_t chunks = L < 4 ? L : 4;
+    while (pool->ev_in.size() < chunks) {
+        cudaEvent_t x, y;
+        cudaEventCreateWithFlags(&x, cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&y, cudaEventDisableTiming);
+        pool->ev_in.push_back(x);
+        pool->ev_done.push_back(y);
+    }
+    uint8_t* base = pool->stage;
+    uint8_t* d_q = base;
+    uint8_t* d_out = d_q + up(qb * L);
+    uint8_t* d_k = d_out + up(qb * L);
+    uint8_t* d_v = d_k + up(kb * L);
+    uint32_t* d_bt = reinterpret_cast<uint32_t*>(d_v + up(kb * L));
+    uint32_t* d_sl = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(d_bt) + up(btb));
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    cudaEventRecord(pool->ev_entry, cs);
+    cudaStreamWaitEvent(pool->s_h2d, pool->ev_entry, 0);
+    cudaMemcpyAsync(d_bt, a->block_tables, btb, cudaMemcpyHostToDevice, pool->s_h2d);
+    cudaMemcpyAsync(d_sl, a->seq_lens, slb, cudaMemcpyHostToDevice, pool->s_h2d);
+    const uint8_t* hq = static_cast<const uint8_t*>(a->q);
+    const uint8_t* hk = static_cast<const uint8_t*>(a->k_new);
+    const uint8_t* hv = static_cast<const uint8_t*>(a->v_new);
+    uint8_t* ho = static_cast<uint8_t*>(a->out);
+    int32_t rc = VW_OK;
+    for (uint32_t c = 0; c < chunks; ++c) {
+        const uint32_t l0 = L * c / chunks, l1 = L * (c + 1) / chunks, nl = l1 - l0;
+        cudaMemcpyAsync(d_q + l0 * qb, hq + l0 * qb, nl * qb, cudaMemcpyHostToDevice, pool->s_h2d);
+        cudaMemcpyAsync(d_k + l0 * kb, hk + l0 * kb, nl * kb, cudaMemcpyHostToDevice, pool->s_h2d);
+        cudaMemcpyAsync(d_v + l0 * kb, hv + l0 * kb, nl * kb, cudaMemcpyHostToDevice, pool->s_h2d);
+        cudaEventRecord(pool->ev_in[c], pool->s_h2d);
+        cudaStreamWaitEvent(cs, pool->ev_in[c], 0);
+        for (uint32_t l = l0; l < l1 && rc == VW_OK; ++l) {
+            vw_decode_args da{};
+            da.layer = l;
+            da.num_seqs = B;
+            da.num_q_heads = Hq;
+            da.block_table_stride = a->block_table_stride;
+            da.q = d_q + l * qb;
+            da.block_tables = d_bt;
+            da.seq_lens = d_sl;
+            da.out = d_out + l * qb;
+            da.k_new = d_k + l * kb;
+            da.v_new = d_v + l * kb;
+            da.scale = a->scale;
+            rc = decode_validate(pool, &da);
+            if (rc == VW_OK) rc = decode_launch(pool, &da, cs);
+        }
+        cudaEventRecord(pool->ev_done[c], cs);
+        cudaStreamWaitEvent(pool->s_d2h, pool->ev_done[c], 0);
+        cudaMemcpyAsync(ho + l0 * qb, d_out + l0 * qb, nl * qb, cudaMemcpyDeviceToHost, pool->s_d2h);
+        if (rc != VW_OK) break;
+    }
+    cudaEventRecord(pool->ev_exit, pool->s_d2h);
+    cudaStreamWaitEvent(cs, pool->ev_exit, 0);
+    e = cudaStreamSynchronize(pool->s_d2h);
+    if (rc != VW_OK) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "vw_decode_step_host");
+    e = cudaGetLastError();
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_decode_step_host");
+}
+
+// ---------------------------------------------------------------------------
+// voidweb_forward_pass: the symbol KernelLib::open binds (engine/ffi.bm:68).
+// ---------------------------------------------------------------------------
+
+namespace {
+struct ForwardState {
+    std::mutex mu;
+    vw_pool* pool = nullptr;
+    const void* q = nullptr;
+    const void* k = nullptr;
+    const void* v = nullptr;
+    void* out = nullptr;
+    std::unordered_map<uint64_t, uint32_t> seq_len;   // tokens cached per sequence
+};
+ForwardState& fwd() {
+    static ForwardState s;
+    return s;
+}
+}  // namespace
+
+int32_t vw_forward_bind(vw_pool* pool, const void* q, const void* k_new, const void* v_new,
+                        void* attn_out) {
+    ForwardState& s = fwd();
+    std::lock_guard<std::mutex> lk(s.mu);
+    s.pool = pool;
+    s.q = q;
+    s.k = k_new;
+    s.v = v_new;
+    s.out = attn_out;
+    return VW_OK;
+}
+
+int32_t vw_forward_set_seq_len(uint64_t seq_id, uint32_t len) {
+    ForwardState& s = fwd();
+    std::lock_guard<std::mutex> lk(s.mu);
+    s.seq_len[seq_id] = len;
+    return VW_OK;
+}
+
+int32_t vw_forward_release(uint64_t seq_id) {
+    ForwardState& s = fwd();
+    std::lock_guard<std::mutex> lk(s.mu);
+    s.seq_len.erase(seq_id);
+    return VW_OK;
+}
+
+int32_t voidweb_forward_pass(const ForwardArgs* args) {
+    if (!args) return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null args");
+    ForwardState& s = fwd();
+    std::lock_guard<std::mutex> lk(s.mu);
+    if (!s.pool || !s.q || !s.k || !s.v || !s.out)
+        return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: no pool / attention I/O bound");
+    ForwardArgs a;
+    std::memcpy(&a, args, sizeof a);     // packed struct: copy out before reading fields
+    const PoolGeom& g = s.pool->geom;
+    if (a.num_kv_heads != g.num_kv_heads || a.head_dim != g.head_dim || a.num_layers != g.num_layers)
+        return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: model shape does not match the pool");
+    if (a.num_seqs == 0) return VW_OK;
+    if (!a.seqs) return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null seqs");
+    std::vector<SeqDescriptor> d(a.num_seqs);
+    std::memcpy(d.data(), a.seqs, sizeof(SeqDescriptor) * a.num_seqs);
+    uint32_t stride = 1;
+    for (const auto& sd : d) {
+        if (sd.is_prefill || sd.num_tokens != 1)
+            return fail(VW_ERR_UNSUPPORTED, "voidweb_forward_pass: prefill descriptors are not supported");
+        if (sd.num_blocks > stride) stride = sd.num_blocks;
+    }
+    std::vector<uint32_t> table((size_t)a.num_seqs * stride, 0), lens(a.num_seqs);
+    for (uint32_t i = 0; i < a.num_seqs; ++i) {
+        const uint32_t pos = s.seq_len.count(d[i].seq_id) ? s.seq_len[d[i].seq_id] : 0;
+        if ((uint64_t)pos + 1 > (uint64_t)d[i].num_blocks * 16)
+            return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: seq %llu needs %u blocks, has %u",
+                        (unsigned long long)d[i].seq_id, pos / 16 + 1, d[i].num_blocks);
+        if (d[i].num_blocks && !d[i].block_ptr)
+            return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null block_ptr");
+        std::memcpy(&table[(size_t)i * stride], reinterpret_cast<const void*>(d[i].block_ptr),
+                    (size_t)d[i].num_blocks * 4);
+        lens[i] = pos + 1;
+    }
+    vw_step_host_args st{};
+    st.num_seqs = a.num_seqs;
+    st.num_q_heads = a.num_heads;
+    st.block_table_stride = stride;
+    st.q = s.q;
+    st.k_new = s.k;
+    st.v_new = s.v;
+    st.block_tables = table.data();
+    st.seq_lens = lens.data();
+    st.out = s.out;
+    st.scale = 0.0f;
+    int32_t rc = vw_decode_step_host(s.pool, &st, nullptr);
+    if (rc != VW_OK) return rc;
+    for (uint32_t i = 0; i < a.num_seqs; ++i) s.seq_len[d[i].seq_id] = lens[i];
+    return VW_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,67 @@
+// vw_internal.h -- structures shared by the kernels (.cu) and the C-ABI layer.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace vw {
+
+enum KvKind : uint32_t { kF16 = 0, kBF16 = 1, kFP8 = 2 };
+
+constexpr int kBlockSize = 16;          // tokens per page (engine/engine.bm:102)
+constexpr int kMaxBatchPerLaunch = 2048; // sequences per decode launch (prefix table in smem)
+constexpr int kMinPagesPerCta = 8;      // work quantum when the batch is tiny
+
+// Everything a decode launch needs besides the tensor map.
+struct DecodeParams {
+    const void* q;              // [B][Hq][D] io dtype
+    void* out;                  // [B][Hq][D] io dtype
+    const void* k_new;          // [B][Hkv][D] io dtype, or null (decode only)
+    const void* v_new;
+    const uint32_t* block_tables;   // [B][bt_stride]
+    const uint32_t* seq_lens;       // [B], context length including the new token
+    uint8_t* kv_data;           // pool pages (append writes)
+    float* kv_scales;           // FP8 scales [L][NB][2][Hkv][16]
+    float* part_o;              // [grid][2][G][D] split-K partial outputs
+    float* part_ml;             // [grid][2][G][2] (running max, sum)
+    uint32_t* counters;         // [max_batch * Hkv] arrival counters, all zero between launches
+    uint32_t* err;              // device error word
+    uint32_t B, Hq, Hkv, group, num_blocks, layer, bt_stride, fp8_ocp;
+    float scale_log2;           // softmax scale * log2(e)
+};
+
+struct DecodeLaunch {
+    DecodeParams p;
+    const CUtensorMap* tmap;    // host copy, passed by value as a __grid_constant__
+    uint32_t head_dim, kv_kind, io_kind;
+    int grid;
+    cudaStream_t stream;
+};
+
+// Returns cudaSuccess or the launch error.  Unsupported shapes must have been
+// rejected by the caller.
+cudaError_t launch_paged_decode(const DecodeLaunch& L);
+size_t decode_scratch_floats_o(int grid, int head_dim);
+size_t decode_scratch_floats_ml(int grid);
+
+struct PoolGeom {
+    uint32_t num_layers, num_kv_heads, head_dim, num_blocks, kv_kind, io_kind, fp8_ocp;
+};
+
+cudaError_t launch_kv_append(const PoolGeom& g, uint8_t* data, float* scales, uint32_t layer,
+                             const void* k_new, const void* v_new, const int64_t* slots,
+                             uint32_t n, uint32_t* err, cudaStream_t s);
+cudaError_t launch_block_copy(const PoolGeom& g, uint8_t* data, float* scales,
+                              const uint32_t* pairs, uint32_t n, uint32_t* err, cudaStream_t s);
+cudaError_t launch_kv_gather(const PoolGeom& g, const uint8_t* data, const float* scales,
+                             uint32_t layer, const uint32_t* block_table, uint32_t seq_len,
+                             void* out_k, void* out_v, float* out_ks, float* out_vs,
+                             uint32_t* err, cudaStream_t s);
+
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline size_t elem_bytes(uint32_t kv_kind) { return kv_kind == kFP8 ? 1 : 2; }
+
+}  // namespace vw
