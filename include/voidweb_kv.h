@@ -20,9 +20,12 @@
  *
  * Pool layout in HBM (a block id addresses 16 token slots in every layer,
  * engine/engine.bm:170-182):
- *   data  [num_layers][num_blocks][2][num_kv_heads][16][head_dim]
- *         (2 = K, V; element = f16, bf16, or one E4M3 code byte)
- *   scale [num_layers][num_blocks][2][num_kv_heads][16]  f32, FP8 pools only
+ *   data  [num_layers][num_blocks][num_kv_heads][2][16][head_dim]
+ *         (2 = K, V; element = f16, bf16, or one E4M3 code byte), i.e. the
+ *         reference's per-head page kv_cache[block][2][16][HEAD_DIM]
+ *         (kernels/attention/flash_attention.bm:116) stacked over heads,
+ *         blocks and layers; one head's K and V page is contiguous
+ *   scale [num_layers][num_blocks][num_kv_heads][2][16]  f32, FP8 pools only
  */
 #ifndef VOIDWEB_KV_H
 #define VOIDWEB_KV_H
@@ -73,7 +76,7 @@ typedef struct {
     uint32_t io_dtype;       /* VW_F16 or VW_BF16: q, new K/V rows, outputs; equals
                                 kv_dtype unless the pool is FP8 */
     uint32_t fp8_mode;       /* vw_fp8_mode */
-    uint32_t max_batch;      /* most sequences one decode call may carry (<= 2048) */
+    uint32_t max_batch;      /* most sequences one decode call may carry (<= 1024) */
     int32_t device;          /* CUDA device ordinal */
     uint32_t reserved;       /* must be 0 */
     void* kv_data;           /* optional caller-owned device buffer (NULL: allocate) */

@@ -145,7 +145,8 @@ def fp8_quant_row(x: np.ndarray, mode: int = FP8_REFERENCE):
 # ---- pool-level ops ----------------------------------------------------------
 
 def pool_shape(g: Geom):
-    return (g.num_layers, g.num_blocks, 2, g.num_kv_heads, 16, g.head_dim)
+    """[L][NB][Hkv][2][16][D]: per head, a page is K rows then V rows."""
+    return (g.num_layers, g.num_blocks, g.num_kv_heads, 2, 16, g.head_dim)
 
 
 def kv_append(g: Geom, data: np.ndarray, scales, layer: int, k_new: np.ndarray,

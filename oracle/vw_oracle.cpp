@@ -16,9 +16,10 @@
 //
 // Pool layout shared by oracle and product (the reference stores one head as
 // kv_cache[TOTAL_BLOCKS][2][BLOCK_SIZE][HEAD_DIM], flash_attention.bm:116; the
-// multi-layer, multi-head generalisation is):
-//   data  [L][NB][2][Hkv][16][D]   element = f16 / bf16 (2 B) or E4M3 code (1 B)
-//   scale [L][NB][2][Hkv][16]      f32, only for the FP8 pool
+// multi-layer, multi-head generalisation keeps that per-head [2][16][D] page
+// and stacks heads, blocks and layers outside it):
+//   data  [L][NB][Hkv][2][16][D]   element = f16 / bf16 (2 B) or E4M3 code (1 B)
+//   scale [L][NB][Hkv][2][16]      f32, only for the FP8 pool
 // Index 0 of the "2" axis is K, index 1 is V (flash_attention.bm:146,155).
 
 #include <cmath>
@@ -190,7 +191,7 @@ static inline size_t elem_bytes(uint32_t dt) { return dt == VWO_FP8 ? 1 : 2; }
 
 static inline size_t row_index(const vwo_geom* g, uint32_t l, uint32_t blk, uint32_t kv,
                                uint32_t h, uint32_t t) {
-    return ((((size_t)l * g->num_blocks + blk) * 2 + kv) * g->num_kv_heads + h) * 16 + t;
+    return ((((size_t)l * g->num_blocks + blk) * g->num_kv_heads + h) * 2 + kv) * 16 + t;
 }
 
 static inline float io_to_f32(const void* p, size_t i, uint32_t io) {

@@ -210,7 +210,7 @@ def test_single_sequence_ctx1(dev):
     got = run_decode(pool, c, 0, dev)
     # one token: softmax weight 1, output is exactly V row 0
     blk = int(c.block_tables[0, 0])
-    assert np.array_equal(got[0, 0], c.data[0, blk, 1, 0, 0])
+    assert np.array_equal(got[0, 0], c.data[0, blk, 0, 1, 0])
     pool.close()
 
 

@@ -105,7 +105,7 @@ def test_small_decode_matches_transliteration(golden):
     c = golden["decode_small"]
     D, NB, seq_len = c["D"], c["NB"], c["seq_len"]
     g = oracle.geom(1, 1, D, NB, oracle.BF16, oracle.BF16)
-    data = np.array(c["kv_bf16"], dtype=np.uint16).reshape(1, NB, 2, 1, 16, D)
+    data = np.array(c["kv_bf16"], dtype=np.uint16).reshape(1, NB, 1, 2, 16, D)
     q = np.array(c["q_bf16"], dtype=np.uint16).reshape(1, 2, D)
     bt = np.array([c["table"] + [0]], dtype=np.uint32)
     sl = np.array([seq_len], dtype=np.uint32)
@@ -175,7 +175,7 @@ def test_block_copy_snapshot_semantics():
     rng = np.random.default_rng(6)
     g = oracle.geom(2, 1, 64, 6, oracle.FP8, oracle.BF16)
     data = rng.integers(0, 255, oracle.pool_shape(g), dtype=np.uint8)
-    scales = rng.random((2, 6, 2, 1, 16)).astype(np.float32)
+    scales = rng.random((2, 6, 1, 2, 16)).astype(np.float32)
     before, sbefore = data.copy(), scales.copy()
     oracle.block_copy(g, data, scales, np.array([[1, 2], [2, 4]]))   # 2 read before written
     assert (data[:, 2] == before[:, 1]).all() and (data[:, 4] == before[:, 2]).all()

@@ -11,7 +11,9 @@ import os
 import subprocess
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libvoidweb_kv.so")
+# VOIDWEB_KV_LIB selects another build of the same library (e.g. one compiled
+# with different tile parameters); by default the in-tree build is used.
+LIB_PATH = os.environ.get("VOIDWEB_KV_LIB") or os.path.join(_HERE, "libvoidweb_kv.so")
 CSRC = os.path.join(_HERE, "csrc")
 
 VW_OK = 0
@@ -135,7 +137,7 @@ def lib() -> ctypes.CDLL:
     """Load the library (building it if the sources are newer); raise if absent."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH) or _stale():
+        if not os.environ.get("VOIDWEB_KV_LIB") and (not os.path.exists(LIB_PATH) or _stale()):
             try:
                 build()
             except Exception as e:  # no silent fallback: the product path needs the .so

@@ -124,14 +124,15 @@ int32_t encode_pool_map(vw_pool* p) {
     const PoolGeom& g = p->geom;
     const uint64_t eb = elem_bytes(g.kv_kind);
     const uint64_t row = (uint64_t)g.head_dim * eb;
-    const uint64_t chunk_elems = 128 / eb;
-    cuuint64_t dims[5] = {chunk_elems, row / 128, 16, 2ull * g.num_kv_heads,
-                          (cuuint64_t)g.num_layers * g.num_blocks};
-    cuuint64_t strides[4] = {128, row, 16 * row, 2ull * g.num_kv_heads * 16 * row};
-    cuuint32_t box[5] = {(cuuint32_t)chunk_elems, 1, 16, 1, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    // 2-D view of the pool: rows of head_dim elements; one box = the 32 rows of a
+    // page-head (K rows then V rows) by 128 bytes, 128-B swizzled in smem
+    const uint64_t rows = (uint64_t)g.num_layers * g.num_blocks * g.num_kv_heads * 32;
+    cuuint64_t dims[2] = {g.head_dim, rows};
+    cuuint64_t strides[1] = {row};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / eb), 32};
+    cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(&p->tmap, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                    5, p->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    2, p->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(VW_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -163,8 +164,9 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
         return fail(VW_ERR_UNSUPPORTED, "vw_pool_create: FP8 pools need head_dim 128");
     if (c.max_batch == 0 || c.max_batch > (uint32_t)kMaxBatchPerLaunch)
         return fail(VW_ERR_INVALID_ARG, "vw_pool_create: max_batch must be 1..%d", kMaxBatchPerLaunch);
-    if ((uint64_t)c.num_layers * c.num_blocks > 0x7FFFFFFFull)
-        return fail(VW_ERR_INVALID_ARG, "vw_pool_create: num_layers * num_blocks exceeds 2^31-1");
+    if ((uint64_t)c.num_layers * c.num_blocks * c.num_kv_heads * 32 > 0x7FFFFFFFull)
+        return fail(VW_ERR_INVALID_ARG,
+                    "vw_pool_create: layers * blocks * kv_heads * 32 rows exceed 2^31-1");
     if (c.kv_data && !aligned(c.kv_data, 256))
         return fail(VW_ERR_INVALID_ARG, "vw_pool_create: kv_data must be 256-byte aligned");
     if (c.kv_scales && !aligned(c.kv_scales, 256))
@@ -186,7 +188,7 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
     cudaError_t e;
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.device);
-    p->grid = sms > 0 ? sms : 148;
+    p->grid = (sms > 0 ? sms : 148) * decode_ctas_per_sm();
     if (c.kv_data) {
         p->data = static_cast<uint8_t*>(c.kv_data);
     } else {

@@ -7,24 +7,34 @@
 // o = softmax(q K^T * scale) V over the sequence's pages found through its
 // block table, the last page partial (:132-140) -- re-designed for B200:
 //
-//  * Work split.  The unit of work is one (sequence, KV head) page: 16 tokens of
-//    K and V for one KV head.  All pages of all (sequence, KV head) segments are
-//    laid end to end and cut into equal contiguous ranges, one per CTA of a
-//    persistent grid sized to the SM count, so every CTA streams the same number
-//    of bytes whatever the context lengths (split-K over pages).  A segment cut
-//    by a range boundary leaves (o, max, sum) partials; the last CTA to finish a
-//    piece of it (an atomic arrival counter, no waiting) merges them.
+//  * Work split.  The unit of work is one page-head: 16 tokens of K and V of one
+//    KV head, 8 KB contiguous in the pool ([L][NB][Hkv][2][16][D]).  All
+//    page-heads of all (sequence, KV head) segments are laid end to end and cut
+//    into equal contiguous ranges, one per CTA of a persistent grid of two CTAs
+//    per SM, so every CTA streams the same number of bytes whatever the context
+//    lengths (split-K over pages).  A segment cut by a range boundary leaves
+//    (o, max, sum) partials; the last CTA to finish a piece of it (an atomic
+//    arrival counter, no waiting) merges them.
 //  * GQA.  The Hq/Hkv query heads that share a KV head are processed together:
-//    each K/V page is read from HBM once per KV head, never once per query head.
-//  * Data movement.  One producer warp walks the block table and issues TMA
-//    tensor loads of whole K and V page tiles (128-B swizzled) into a ring of
-//    shared-memory stages tracked by mbarriers; no multicast.
-//  * Math.  Each consumer warp takes every W-th page of the range and runs the
-//    per-page micro-tiles on the tensor cores with warp-level mma.sync m16n8k16
-//    (tokens as M, query heads as N: S^T = K Q^T, then O^T = V^T P^T), f32
-//    accumulation, online softmax in the log2 domain with warp-shuffle maxima.
-//    A page gives a 16 x 8 x 128 micro-tile, below the 64-row minimum of a
-//    tcgen05 MMA, and the kernel is HBM-bound with tensor pipes mostly idle.
+//    each page is read from HBM once per KV head, never once per query head.
+//  * Data movement.  A producer warp resolves block ids 32 pages at a time, one
+//    batch ahead, and four of its lanes issue TMA tensor loads in parallel: one
+//    or two boxes of 32 rows x 128 B (128-B swizzled) bring a page-head's K and
+//    V into a ring of shared-memory stages tracked by mbarriers, plus one bulk
+//    copy of each segment's query tile into a small ring.  A single issuing
+//    thread serialises on the TMA round trip, which is why several lanes issue.
+//    No multicast and no L2 eviction hints (an evict-first hint measurably
+//    lowered throughput).
+//  * Math.  Each of the W consumer warps takes every W-th page of the range and
+//    runs the per-page micro-tiles on the tensor cores with warp-level mma.sync
+//    m16n8k16 (tokens as M, query heads as N: S^T = K Q^T, then O^T = V^T P^T),
+//    f32 accumulation, online softmax in the log2 domain.  The running maximum
+//    is only raised (with a warp-shuffle reduction and a rescale of O) when some
+//    score exceeds it by more than 2^8; otherwise probabilities up to 256 are
+//    accumulated against the stale maximum, which changes no result but takes
+//    the reduction off the per-page critical path.  A page gives a 16 x 8 x 128
+//    micro-tile, below the 64-row minimum of a tcgen05 MMA; the kernel is
+//    HBM-bound with the tensor pipes mostly idle.
 //  * Fused append.  With k_new / v_new given, the warp that owns a segment's last
 //    page writes the new token's K/V row (quantised for FP8 pools) to its slot
 //    block_table[p/16]*16 + p%16, p = seq_len-1, in HBM and into the staged page.
@@ -43,53 +53,118 @@
 #include "vw_internal.h"
 #include "vw_ptx.cuh"
 
+#ifndef VW_DECODE_WARPS
+#define VW_DECODE_WARPS 4
+#endif
+#ifndef VW_DECODE_CTAS_PER_SM
+#define VW_DECODE_CTAS_PER_SM 2
+#endif
+#ifndef VW_DECODE_ISSUERS
+#define VW_DECODE_ISSUERS 4
+#endif
+#ifndef VW_DECODE_MAX_STAGES
+#define VW_DECODE_MAX_STAGES 16
+#endif
+
 namespace vw {
+
+#ifdef VW_DECODE_TRACE
+// Optional per-CTA phase timeline (build with -DVW_DECODE_TRACE): %globaltimer
+// stamps of [start, prologue done, first load issued, first page ready, last
+// load issued, last page done, merges done, exit] and combines done, for the
+// most recent launch; read back with vw_debug_trace().
+__device__ unsigned long long g_vw_trace[1024 * 10];
+#define VW_TRACE(slot, val) (g_vw_trace[blockIdx.x * 10 + (slot)] = (val))
+#else
+#define VW_TRACE(slot, val) ((void)0)
+#endif
 
 namespace {
 
-constexpr int kConsumerWarps = 4;
+constexpr int kConsumerWarps = VW_DECODE_WARPS;
+constexpr int kCtasPerSm = VW_DECODE_CTAS_PER_SM;
+constexpr int kIssuers = VW_DECODE_ISSUERS;           // producer lanes issuing loads
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kQSlots = 4;                            // query tiles in flight (one per segment)
+constexpr int kMaxStages = VW_DECODE_MAX_STAGES;
+// per-CTA shared memory: an SM holds 228 KB and reserves 1 KB per resident CTA
+constexpr int kSmemPerCta = (233472 / kCtasPerSm) - 1024;
+constexpr float kRescaleThreshold = 8.0f;             // log2 units: p <= 2^8 vs a stale max
 
 __host__ __device__ constexpr int align_up_c(int x, int a) { return (x + a - 1) / a * a; }
+__host__ __device__ constexpr int gcd_c(int a, int b) { return b == 0 ? a : gcd_c(b, a % b); }
 
 template <int D_, int NT_, int KV_, int IO_>
 struct Traits {
     static constexpr int D = D_, NT = NT_, KV = KV_, IO = IO_;
+    static constexpr int W = kConsumerWarps;
     static constexpr int G = 8 * NT;                         // padded query heads per KV head
     static constexpr int EB = KV == kFP8 ? 1 : 2;            // pool element bytes
     static constexpr int ROW = D * EB;                       // bytes of one token row
-    static constexpr int CHUNKS = ROW / 128;                 // 128-B swizzle rows per token
-    static constexpr int TILE = 16 * ROW;                    // one K (or V) page tile
-    static constexpr int STAGE = align_up_c(2 * TILE + (KV == kFP8 ? 128 : 0), 1024);
+    static constexpr int CHUNKS = ROW / 128;                 // 128-B swizzle columns per row
+    static constexpr int STAGE = 32 * ROW;                   // one page-head: K rows 0-15, V 16-31
+    static constexpr int SCAL = KV == kFP8 ? 128 : 0;        // K and V scales of a page-head
     static constexpr bool MMA_BF16 = KV == kBF16;            // FP8 pages compute in f16
     static constexpr int KT = D / 16;                        // k-steps of Q K^T
     static constexpr int MT = D / 16;                        // d-tiles of V^T P^T
-    static constexpr int CTILE = KV == kFP8 ? 16 * D * 2 : 0;  // f16 tile per K/V per warp
-    static constexpr int MERGE = kConsumerWarps * G * (D + 2) * 4;
-    static constexpr int PFX = align_up_c((kMaxBatchPerLaunch + 1) * 4, 128);
-    static constexpr int FIXED = kConsumerWarps * 2 * CTILE + align_up_c(MERGE, 1024) + PFX +
-                                 1024 /* mbarriers + flags */;
-    static constexpr int S = (kSmemBudget - FIXED) / STAGE > 16 ? 16
-                                                                 : (kSmemBudget - FIXED) / STAGE;
-    static constexpr int SMEM = 1024 /*align slack*/ + S * STAGE + FIXED;
+    static constexpr int CTILE = KV == kFP8 ? 32 * D * 2 : 0;  // f16 page-head per warp
+    static constexpr int MERGE = W * G * (D + 2) * 4;
+    static constexpr int QTILE = G * D * 2;
+    static constexpr int PFX = align_up_c(2 * (kMaxBatchPerLaunch + 1) * 4, 128);
+    static constexpr int FIXED = W * CTILE + align_up_c(MERGE, 1024) +
+                                 align_up_c(kQSlots * QTILE, 1024) + PFX + 2048;
+    static constexpr int BUDGET = kSmemPerCta - 1024 /* base alignment slack */ -
+                                  (SCAL ? 1024 : 0) /* scale ring alignment */;
+    // Stage count: as many as fit, rounded down to a multiple of the consumer
+    // warps and of the issuing lanes.  Page i lives in stage i % S, is issued by
+    // lane i % kIssuers and consumed by warp i % W; with S a multiple of both,
+    // every stage is filled by one lane and drained by one warp, each in page
+    // order.  That is what the mbarrier parity waits require: a parity wait can
+    // only tell the current phase from the one before it, so no waiter may ever
+    // run two phases ahead of a barrier.
+    static constexpr int LCM_WI = W * kIssuers / gcd_c(W, kIssuers);
+    static constexpr int S_FIT = (BUDGET - FIXED) / (STAGE + SCAL) > kMaxStages
+                                     ? kMaxStages : (BUDGET - FIXED) / (STAGE + SCAL);
+    static constexpr int S = S_FIT / LCM_WI * LCM_WI;
+    static constexpr int SMEM = 1024 + S * STAGE + align_up_c(S * SCAL, 1024) + FIXED;
+    // FP8: probabilities carry the V scale but not the 1/256 of the f16 code
+    // expansion; the output is multiplied back by 256
+    static constexpr float VFOLD = KV == kFP8 ? 256.0f : 1.0f;
+    static constexpr int E = (G * D + W * 32 - 1) / (W * 32);   // combine elements per thread
+    static constexpr int CU = E > 4 ? 2 : 4;                     // combine pieces loaded at once
     static_assert(CHUNKS >= 1, "row must be at least 128 bytes");
     static_assert(S >= 4, "too few pipeline stages");
-    static_assert(SMEM <= 227 * 1024, "shared memory over the per-CTA limit");
-    static_assert((S * STAGE) % 1024 == 0 && (2 * CTILE) % 1024 == 0, "1024-B tile alignment");
+    static_assert(S % W == 0 && S % kIssuers == 0, "stage ownership needs S % W == S % issuers == 0");
+    static_assert(32 % kIssuers == 0, "issuing lanes must divide the 32-page batch");
+    static_assert(SMEM <= kSmemPerCta, "shared memory over the per-CTA limit");
+    static_assert(STAGE % 1024 == 0 && CTILE % 1024 == 0, "1024-B tile alignment");
+};
+
+// Page as the producer publishes it to its issuing lanes: KV head, TMA row of
+// its first K row (negative for an invalid block id: TMA zero-fills), and the
+// segment ordinal and first query row when the page starts a segment of this
+// CTA's range (else qseg = -1).
+struct PageInfo {
+    int h, row0, qseg, qrow;
 };
 
 struct Smem {
-    uint8_t* stages;
-    uint8_t* ctile;      // FP8 only: [W][2][CTILE]
+    uint8_t* stages;     // [S][STAGE]
+    float* scal;         // [S][32] FP8 scales (K 16, V 16)
+    uint8_t* ctile;      // FP8 only: [W][CTILE]
     float* mo;           // [W][G][D]
     float* mm;           // [W][G]
     float* ml;           // [W][G]
+    uint8_t* qring;      // [kQSlots][G][D] io dtype
     int* pfx;            // [B+1] exclusive prefix of pages per sequence
+    int* nzp;            // [B+1] exclusive prefix of sequences with pages
+    PageInfo* pinfo;     // [2][32] producer batches
     uint64_t* full;      // [S]
     uint64_t* empty;     // [S]
-    int* flag;           // scratch word for broadcasts
+    uint64_t* qfull;     // [kQSlots]
+    uint64_t* qempty;    // [kQSlots]
+    int* flag;           // [0] last-arrival broadcast, [1] abort marker
 };
 
 template <class T>
@@ -97,27 +172,35 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     Smem s;
     uint8_t* p = base;
     s.stages = p; p += T::S * T::STAGE;
-    s.ctile = p; p += kConsumerWarps * 2 * T::CTILE;
+    s.scal = reinterpret_cast<float*>(p); p += align_up_c(T::S * T::SCAL, 1024);
+    s.ctile = p; p += T::W * T::CTILE;
     s.mo = reinterpret_cast<float*>(p);
-    s.mm = s.mo + kConsumerWarps * T::G * T::D;
-    s.ml = s.mm + kConsumerWarps * T::G;
+    s.mm = s.mo + T::W * T::G * T::D;
+    s.ml = s.mm + T::W * T::G;
     p += align_up_c(T::MERGE, 1024);
-    s.pfx = reinterpret_cast<int*>(p); p += T::PFX;               // keeps p 128-B aligned
+    s.qring = p; p += align_up_c(kQSlots * T::QTILE, 1024);
+    s.pfx = reinterpret_cast<int*>(p);
+    s.nzp = s.pfx + (kMaxBatchPerLaunch + 1);
+    p += T::PFX;
+    s.pinfo = reinterpret_cast<PageInfo*>(p); p += 1024;
     s.full = reinterpret_cast<uint64_t*>(p);
     s.empty = s.full + T::S;
-    s.flag = reinterpret_cast<int*>(s.empty + T::S);
+    s.qfull = s.empty + T::S;
+    s.qempty = s.qfull + kQSlots;
+    s.flag = reinterpret_cast<int*>(s.qempty + kQSlots);
     return s;
 }
 
-// Byte offset of element (t, d) inside a 128-B-swizzled tile of 2-byte rows of D.
-__device__ __forceinline__ uint32_t swz16(int t, int d) {
-    int byte = d * 2;
-    return (uint32_t)((byte >> 7) * 2048 + t * 128 + ((((byte & 127) >> 4) ^ (t & 7)) << 4) +
+// Byte offset of element d of row `row` (0..31) inside a page-head tile of
+// 2-byte elements stored as [CHUNKS][32 rows][128 B], 128-B swizzled.
+__device__ __forceinline__ uint32_t swz16(int row, int d) {
+    const int byte = d * 2;
+    return (uint32_t)((byte >> 7) * 4096 + row * 128 + ((((byte & 127) >> 4) ^ (row & 7)) << 4) +
                       (byte & 15));
 }
-// Same for 1-byte rows of 128 (FP8, D = 128).
-__device__ __forceinline__ uint32_t swz8(int t, int d) {
-    return (uint32_t)(t * 128 + ((((d & 127) >> 4) ^ (t & 7)) << 4) + (d & 15));
+// Same for 1-byte rows of 128 (FP8, D = 128): [32 rows][128 B].
+__device__ __forceinline__ uint32_t swz8(int row, int d) {
+    return (uint32_t)(row * 128 + ((((d & 127) >> 4) ^ (row & 7)) << 4) + (d & 15));
 }
 
 // Largest b with Hkv * pfx[b] <= x (x < Hkv * pfx[B]).
@@ -143,94 +226,159 @@ __device__ __forceinline__ uint16_t f32_to_io(float f) {
 
 // ------------------------------------------------------------------ producer
 
-template <class T>
-__device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const Smem& sm,
-                         int begin, int n, uint64_t deadline) {
-    const int lane = threadIdx.x & 31;
-    const uint64_t pol = policy_evict_first();
-    const int Hkv = (int)p.Hkv;
-    const int layer_base = (int)(p.layer * p.num_blocks);
-    bool ok = true;
-    for (int i0 = 0; i0 < n && ok; i0 += 32) {
-        // each lane resolves one page of the next 32: segment, page, block id
-        int i = i0 + lane;
-        int c3 = 0, c4 = -1;
-        if (i < n) {
-            long long x = (long long)begin + i;
-            int b = find_seq(sm.pfx, (int)p.B, Hkv, x);
-            int np = sm.pfx[b + 1] - sm.pfx[b];
-            int r = (int)(x - (long long)Hkv * sm.pfx[b]);
-            int h = r / np, pg = r - h * np;
-            uint32_t blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg);
-            c3 = h;
-            if (blk < p.num_blocks) c4 = layer_base + (int)blk;
-            else set_err(p.err, kDevErrBlockId);        // c4 = -1: TMA zero-fills the tile
-        }
-        const int m = min(32, n - i0);
-        for (int j = 0; j < m; ++j) {
-            const int ii = i0 + j;
-            const int h = __shfl_sync(0xffffffffu, c3, j);
-            const int row = __shfl_sync(0xffffffffu, c4, j);
-            const int s = ii % T::S;
-            if (ii >= T::S && !mbar_wait(&sm.empty[s], ((ii / T::S) - 1) & 1, deadline)) {
-                ok = false;
-                break;
-            }
-            if (lane == 0) {
-                uint8_t* st = sm.stages + s * T::STAGE;
-                const bool scales = T::KV == kFP8 && row >= 0;
-                if (T::KV == kFP8 && !scales) {
-                    // invalid block id: zero scales (plain stores, ordered before the
-                    // arrive below, and fenced against this stage's next TMA write)
-                    float* dst = reinterpret_cast<float*>(st + 2 * T::TILE);
-                    for (int k = 0; k < 32; ++k) dst[k] = 0.0f;
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                }
-                mbar_arrive_expect_tx(&sm.full[s], 2 * T::TILE + (scales ? 128 : 0));
-                for (int c = 0; c < T::CHUNKS; ++c) {
-                    tma_load_5d(st + c * 2048, tmap, &sm.full[s], 0, c, 0, h, row, pol);
-                    tma_load_5d(st + T::TILE + c * 2048, tmap, &sm.full[s], 0, c, 0, Hkv + h,
-                                row, pol);
-                }
-                if (scales) {
-                    // scales of this page: K then V, 16 f32 each
-                    const float* ks = p.kv_scales + ((size_t)row * 2 * Hkv + h) * 16;
-                    const float* vs = p.kv_scales + ((size_t)row * 2 * Hkv + Hkv + h) * 16;
-                    bulk_load(st + 2 * T::TILE, ks, 64, &sm.full[s], pol);
-                    bulk_load(st + 2 * T::TILE + 64, vs, 64, &sm.full[s], pol);
-                }
-            }
-            __syncwarp();
+struct Resolved {
+    int h, qseg, qrow;
+    uint32_t blk;
+    bool live;
+};
+
+// Lane-parallel resolution of CTA-relative page i: its segment, KV head and
+// block id (the block-table load is consumed one batch later).
+__device__ __forceinline__ Resolved resolve_page(const DecodeParams& p, const Smem& sm, int begin,
+                                                 int first_ord, int i, int n) {
+    Resolved r{0, -1, -1, 0xFFFFFFFFu, false};
+    if (i < n) {
+        const long long x = (long long)begin + i;
+        const int b = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, x);
+        const int np = sm.pfx[b + 1] - sm.pfx[b];
+        const int rr = (int)(x - (long long)p.Hkv * sm.pfx[b]);
+        const int h = rr / np, pg = rr - h * np;
+        r.h = h;
+        r.live = true;
+        r.blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg);
+        if (i == 0 || pg == 0) {
+            r.qseg = sm.nzp[b] * (int)p.Hkv + h - first_ord;
+            r.qrow = (int)(b * p.Hq + h * p.group);
         }
     }
+    return r;
+}
+
+template <class T>
+__device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const Smem& sm,
+                         int begin, int n, int first_ord, uint64_t deadline) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t Hkv = p.Hkv;
+    const uint32_t qbytes = p.group * T::D * 2;
+    const uint8_t* qbase = reinterpret_cast<const uint8_t*>(p.q);
+    int segs_issued = 0;                             // highest segment ordinal issued + 1
+    bool ok = true;
+
+    auto publish = [&](const Resolved& r, int buf) {
+        PageInfo pi;
+        pi.h = r.h;
+        pi.qseg = r.qseg;
+        pi.qrow = r.qrow;
+        pi.row0 = -32;
+        if (r.live) {
+            if (r.blk < p.num_blocks)
+                pi.row0 = (int)(((p.layer * p.num_blocks + r.blk) * Hkv + (uint32_t)r.h) * 32u);
+            else
+                set_err(p.err, kDevErrBlockId);     // negative row: TMA zero-fills the tile
+        }
+        sm.pinfo[buf * 32 + lane] = pi;
+    };
+
+    Resolved cur = resolve_page(p, sm, begin, first_ord, lane, n);
+    publish(cur, 0);
+    __syncwarp();
+    int buf = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const Resolved nxt = resolve_page(p, sm, begin, first_ord, i0 + 32 + lane, n);
+        const int m = min(32, n - i0);
+        if (lane < kIssuers) {
+            // lane 0 scans every page of the batch for segment starts so that query
+            // tiles are issued in segment order by one thread (the query ring's
+            // parity waits need that); each lane issues the pages of its own stages
+            for (int j = lane == 0 ? 0 : lane; j < m && ok; j += lane == 0 ? 1 : kIssuers) {
+                const int ii = i0 + j;
+                const PageInfo pi = sm.pinfo[buf * 32 + j];
+                if (lane == 0 && pi.qseg >= 0) {
+                    // a new segment starts here: its query tile
+                    const int k = pi.qseg, qs = k % kQSlots;
+                    if (k >= kQSlots &&
+                        !mbar_wait(&sm.qempty[qs], ((k / kQSlots) - 1) & 1, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&sm.qfull[qs], qbytes);
+                    bulk_load(sm.qring + qs * T::QTILE, qbase + (size_t)pi.qrow * T::D * 2, qbytes,
+                              &sm.qfull[qs]);
+                    segs_issued = k + 1;
+                }
+                if ((j % kIssuers) != lane) continue;   // another lane's stage
+                const int s = ii % T::S;
+                if (ii >= T::S && !mbar_wait(&sm.empty[s], ((ii / T::S) - 1) & 1, deadline)) {
+                    ok = false;
+                    break;
+                }
+                if (ii == 0) VW_TRACE(2, globaltimer());
+                if (ii == n - 1) VW_TRACE(4, globaltimer());
+                uint8_t* st = sm.stages + s * T::STAGE;
+                if constexpr (T::KV == kFP8) {
+                    float* sc = sm.scal + s * 32;
+                    if (pi.row0 >= 0) {
+                        // the page-head's K and V scales: 32 consecutive f32
+                        mbar_arrive_expect_tx(&sm.full[s], T::STAGE + 128);
+                        bulk_load(sc, p.kv_scales + pi.row0, 128, &sm.full[s]);
+                    } else {
+                        // invalid block id: zero scales with plain stores, ordered before
+                        // the arrive and fenced against this slot's next bulk write
+                        for (int k = 0; k < 32; ++k) sc[k] = 0.0f;
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
+                    }
+                } else {
+                    mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
+                }
+#pragma unroll
+                for (int c = 0; c < T::CHUNKS; ++c)
+                    tma_load_2d(st + c * 4096, tmap, &sm.full[s], c * (128 / T::EB), pi.row0);
+            }
+        }
+        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+        __syncwarp();
+        buf ^= 1;
+        publish(nxt, buf);
+        __syncwarp();
+    }
     if (!ok) set_err(p.err, kDevErrTimeout);
-    // Drain: never leave the CTA while a TMA load may still write its smem.
-    const int first = n > T::S ? n - T::S : 0;
-    for (int ii = first; ii < n; ++ii) {
-        if (!mbar_wait(&sm.full[ii % T::S], (ii / T::S) & 1, deadline)) {
-            set_err(p.err, kDevErrTimeout);
-            break;
+    // Drain: never leave the CTA while a TMA or bulk load may still write its smem.
+    // lane 0 issued every query tile; share its count for the drain below
+    segs_issued = __shfl_sync(0xffffffffu, segs_issued, 0);
+    if (lane == 0) {
+        for (int ii = n > T::S ? n - T::S : 0; ii < n; ++ii) {
+            if (!mbar_wait(&sm.full[ii % T::S], (ii / T::S) & 1, deadline)) {
+                set_err(p.err, kDevErrTimeout);
+                break;
+            }
+        }
+        for (int k = segs_issued > kQSlots ? segs_issued - kQSlots : 0; k < segs_issued; ++k) {
+            if (!mbar_wait(&sm.qfull[k % kQSlots], (k / kQSlots) & 1, deadline)) {
+                set_err(p.err, kDevErrTimeout);
+                break;
+            }
         }
     }
 }
 
 // ------------------------------------------------------------------ consumer
 
+// Query fragments (B operand of S^T = K Q^T) from the staged query tile.
 template <class T>
-__device__ __forceinline__ void load_q(const DecodeParams& p, int b, int h, int lane,
+__device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qtile, int lane,
                                        uint32_t (&qf)[T::NT][T::KT][2]) {
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(p.q);
 #pragma unroll
     for (int nt = 0; nt < T::NT; ++nt) {
         const int j = nt * 8 + (lane >> 2);
         const bool live = j < (int)p.group;
-        const uint16_t* row = q + ((size_t)b * p.Hq + (size_t)h * p.group + (live ? j : 0)) * T::D;
+        const uint8_t* row = qtile + (live ? j : 0) * T::D * 2;
 #pragma unroll
         for (int kt = 0; kt < T::KT; ++kt) {
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
-                uint32_t v = live ? __ldg(reinterpret_cast<const uint32_t*>(row + d)) : 0u;
+                uint32_t v = live ? *reinterpret_cast<const uint32_t*>(row + d * 2) : 0u;
                 if constexpr (T::KV == kFP8 && T::IO == kBF16) {
                     // pages compute in f16: convert the bf16 query pair
                     v = pack2<false>(bf16_bits_to_f32(v & 0xFFFFu), bf16_bits_to_f32(v >> 16));
@@ -242,10 +390,11 @@ __device__ __forceinline__ void load_q(const DecodeParams& p, int b, int h, int 
 }
 
 // Write the new token's row (t = valid-1) of one KV head into HBM and into the
-// staged page.  One warp; each lane owns D/32 consecutive elements.
+// staged page-head (K at row t, V at row 16+t).  One warp; each lane owns D/32
+// consecutive elements.
 template <class T>
-__device__ __forceinline__ void append_row(const DecodeParams& p, uint8_t* stage, int b, int h,
-                                           uint32_t blk, int t, int lane) {
+__device__ __forceinline__ void append_row(const DecodeParams& p, uint8_t* stage, float* scal,
+                                           int b, int h, uint32_t blk, int t, int lane) {
     constexpr int PER = T::D / 32;    // 2 (D=64) or 4 (D=128)
     const bool blk_ok = blk < p.num_blocks;
     if (!blk_ok && lane == 0) set_err(p.err, kDevErrBlockId);
@@ -253,14 +402,15 @@ __device__ __forceinline__ void append_row(const DecodeParams& p, uint8_t* stage
     for (int kv = 0; kv < 2; ++kv) {
         const uint16_t* src = reinterpret_cast<const uint16_t*>(kv == 0 ? p.k_new : p.v_new) +
                               ((size_t)b * p.Hkv + h) * T::D + lane * PER;
-        const size_t row = (((size_t)p.layer * p.num_blocks + blk) * 2 + kv) * p.Hkv + h;
-        uint8_t* tile = stage + kv * T::TILE;
+        // pool row of (layer, block, head, kv, t) in [L][NB][Hkv][2][16]
+        const size_t prow = ((((size_t)p.layer * p.num_blocks + blk) * p.Hkv + h) * 2 + kv) * 16 + t;
+        const int srow = kv * 16 + t;
         if constexpr (T::KV != kFP8) {
             uint32_t w[PER / 2];
 #pragma unroll
             for (int k = 0; k < PER / 2; ++k) w[k] = __ldg(reinterpret_cast<const uint32_t*>(src) + k);
-            uint8_t* gdst = p.kv_data + (row * 16 + t) * T::ROW + lane * PER * 2;
-            uint8_t* sdst = tile + swz16(t, lane * PER);
+            uint8_t* gdst = p.kv_data + prow * T::ROW + lane * PER * 2;
+            uint8_t* sdst = stage + swz16(srow, lane * PER);
             if constexpr (PER == 4) {
                 if (blk_ok) *reinterpret_cast<uint2*>(gdst) = make_uint2(w[0], w[1]);
                 *reinterpret_cast<uint2*>(sdst) = make_uint2(w[0], w[1]);
@@ -279,50 +429,45 @@ __device__ __forceinline__ void append_row(const DecodeParams& p, uint8_t* stage
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
             const float scale = fp8_row_scale(amax);
             const uint32_t codes = fp8_encode4(v, scale, p.fp8_ocp != 0);
-            uint8_t* gdst = p.kv_data + (row * 16 + t) * T::ROW + lane * 4;
+            uint8_t* gdst = p.kv_data + prow * T::ROW + lane * 4;
             if (blk_ok) *reinterpret_cast<uint32_t*>(gdst) = codes;
-            *reinterpret_cast<uint32_t*>(tile + swz8(t, lane * 4)) = codes;
+            *reinterpret_cast<uint32_t*>(stage + swz8(srow, lane * 4)) = codes;
             if (lane == 0) {
-                if (blk_ok) p.kv_scales[row * 16 + t] = scale;
-                reinterpret_cast<float*>(stage + 2 * T::TILE)[kv * 16 + t] = scale;
+                if (blk_ok) p.kv_scales[prow] = scale;
+                scal[srow] = scale;
             }
         }
     }
 }
 
-// Zero V rows [valid, 16) of a staged page so masked tokens cannot inject
+// Zero V rows [valid, 16) of a staged page-head so masked tokens cannot inject
 // NaN/Inf through 0 * garbage in the P.V product.
 template <class T>
 __device__ __forceinline__ void zero_tail(uint8_t* stage, int valid, int lane) {
-    uint8_t* vt = stage + T::TILE;
-    const int per_row = T::ROW / 16;                 // 16-B pieces per row
+    const int per_row = T::CHUNKS * 8;                   // 16-B pieces per row
     const int total = (16 - valid) * per_row;
     for (int k = lane; k < total; k += 32) {
-        const int t = valid + k / per_row, piece = k % per_row;
+        const int piece = k % per_row, row = 16 + valid + k / per_row;
         const int c = piece >> 3, ch = piece & 7;
-        *reinterpret_cast<uint4*>(vt + c * 2048 + t * 128 + (ch << 4)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(stage + c * 4096 + row * 128 + (ch << 4)) = make_uint4(0, 0, 0, 0);
     }
 }
 
-// FP8: expand the staged K and V code tiles into this warp's f16 tiles.
+// FP8: expand the staged page-head of codes [32 rows][128 B] into this warp's
+// f16 tile [2][32 rows][128 B] (same swizzled layout as a 2-byte stage).
 template <class T>
 __device__ __forceinline__ void dequant_page(const uint8_t* stage, uint8_t* ctile, int lane) {
 #pragma unroll
-    for (int kv = 0; kv < 2; ++kv) {
-        const uint8_t* src = stage + kv * T::TILE;
-        uint8_t* dst = ctile + kv * T::CTILE;
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int t = it * 4 + (lane >> 3), c16 = lane & 7;
-            const uint4 w = *reinterpret_cast<const uint4*>(src + t * 128 + ((c16 ^ (t & 7)) << 4));
-            uint4 lo, hi;
-            lo.x = fp8x2_to_f16x2_scaled(w.x, 0); lo.y = fp8x2_to_f16x2_scaled(w.x, 1);
-            lo.z = fp8x2_to_f16x2_scaled(w.y, 0); lo.w = fp8x2_to_f16x2_scaled(w.y, 1);
-            hi.x = fp8x2_to_f16x2_scaled(w.z, 0); hi.y = fp8x2_to_f16x2_scaled(w.z, 1);
-            hi.z = fp8x2_to_f16x2_scaled(w.w, 0); hi.w = fp8x2_to_f16x2_scaled(w.w, 1);
-            *reinterpret_cast<uint4*>(dst + swz16(t, c16 * 16)) = lo;
-            *reinterpret_cast<uint4*>(dst + swz16(t, c16 * 16 + 8)) = hi;
-        }
+    for (int it = 0; it < 8; ++it) {
+        const int row = it * 4 + (lane >> 3), c16 = lane & 7;
+        const uint4 w = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c16 ^ (row & 7)) << 4));
+        uint4 lo, hi;
+        lo.x = fp8x2_to_f16x2_scaled(w.x, 0); lo.y = fp8x2_to_f16x2_scaled(w.x, 1);
+        lo.z = fp8x2_to_f16x2_scaled(w.y, 0); lo.w = fp8x2_to_f16x2_scaled(w.y, 1);
+        hi.x = fp8x2_to_f16x2_scaled(w.z, 0); hi.y = fp8x2_to_f16x2_scaled(w.z, 1);
+        hi.z = fp8x2_to_f16x2_scaled(w.w, 0); hi.w = fp8x2_to_f16x2_scaled(w.w, 1);
+        *reinterpret_cast<uint4*>(ctile + swz16(row, c16 * 16)) = lo;
+        *reinterpret_cast<uint4*>(ctile + swz16(row, c16 * 16 + 8)) = hi;
     }
 }
 
@@ -332,22 +477,25 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ctid = threadIdx.x;                     // 0 .. W*32-1
     const int Hkv = (int)p.Hkv;
-    const int W = kConsumerWarps;
+    constexpr int W = T::W;
+    constexpr int NTH = W * 32;
     const bool append = p.k_new != nullptr;
 
-    // ldmatrix lane geometry (see the fragment layout notes at the top)
+    // ldmatrix lane geometry: K rows feed A = K (tokens x d), V rows (16..31)
+    // feed A = V^T (d x tokens) through the transposing load
     const int mi = lane >> 3;
     const int k_tok = (lane & 7) + ((mi & 1) << 3), k_hs = mi >> 1;
     const int v_tok = (lane & 7) + ((mi >> 1) << 3), v_hs = mi & 1;
     const int t0 = lane >> 2, t1 = t0 + 8;
 
-    uint8_t* my_ctile = sm.ctile + warp * 2 * T::CTILE;
+    uint8_t* my_ctile = sm.ctile + warp * T::CTILE;
     bool alive = true;
+    int seg_k = 0;
 
     for (int x = begin; x < end;) {
         const int b = find_seq(sm.pfx, (int)p.B, Hkv, x);
         const int np = sm.pfx[b + 1] - sm.pfx[b];
-        const int seg_start = Hkv * sm.pfx[b] + 0;
+        const int seg_start = Hkv * sm.pfx[b];
         const int r = x - seg_start;
         const int h = r / np, pg0 = r - h * np;
         const int s_begin = seg_start + h * np;       // flat index of this segment's page 0
@@ -356,8 +504,22 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         const int i_base = x - begin;
         const int seq_len = (int)__ldg(p.seq_lens + b);
 
+        // query tile of this segment (staged by the producer)
         uint32_t qf[T::NT][T::KT][2];
-        load_q<T>(p, b, h, lane, qf);
+        {
+            const int qs = seg_k % kQSlots;
+            // every lane waits, then the warp agrees (and reconverges) before the
+            // warp-collective fragment loads that follow
+            const bool got = !alive || mbar_wait(&sm.qfull[qs], (seg_k / kQSlots) & 1, deadline);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) set_err(p.err, kDevErrTimeout);
+                alive = false;
+            }
+            load_q<T>(p, sm.qring + qs * T::QTILE, lane, qf);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.qempty[qs]);
+            ++seg_k;
+        }
 
         float o[T::NT][T::MT][4];
         float mrun[T::NT][2], lrun[T::NT][2];
@@ -374,17 +536,20 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             const int pg = pg0 + (i - i_base);
             const int s = i % T::S;
             uint8_t* st = sm.stages + s * T::STAGE;
-            if (!mbar_wait(&sm.full[s], (i / T::S) & 1, deadline)) {
+            float* sc = sm.scal + s * 32;
+            // warp-uniform wait: ldmatrix / mma.sync below need the whole warp
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (i / T::S) & 1, deadline))) {
                 if (lane == 0) set_err(p.err, kDevErrTimeout);
                 alive = false;
                 break;
             }
+            if (i == 0 && lane == 0) VW_TRACE(3, globaltimer());
             int valid = 16;
             if (pg == np - 1) {
                 valid = seq_len - pg * 16;
                 if (append) {
                     const uint32_t blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg);
-                    append_row<T>(p, st, b, h, blk, valid - 1, lane);
+                    append_row<T>(p, st, sc, b, h, blk, valid - 1, lane);
                 }
                 if (valid < 16) zero_tail<T>(st, valid, lane);
                 // plain stores into a TMA-filled stage: order them before the stage's
@@ -392,64 +557,78 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
             }
-            const float* kscale = reinterpret_cast<const float*>(st + 2 * T::TILE);
             float ks0 = 1.0f, ks1 = 1.0f, vs0 = 1.0f, vs1 = 1.0f;
-            uint32_t kbase, vbase;
+            uint32_t tbase;
             if constexpr (T::KV == kFP8) {
-                ks0 = kscale[t0] * 256.0f; ks1 = kscale[t1] * 256.0f;
-                vs0 = kscale[16 + t0] * 256.0f; vs1 = kscale[16 + t1] * 256.0f;
+                ks0 = sc[t0] * 256.0f; ks1 = sc[t1] * 256.0f;
+                vs0 = sc[16 + t0]; vs1 = sc[16 + t1];
                 dequant_page<T>(st, my_ctile, lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.empty[s]);   // stage no longer needed
-                kbase = smem_u32(my_ctile);
-                vbase = smem_u32(my_ctile + T::CTILE);
+                tbase = smem_u32(my_ctile);
             } else {
-                kbase = smem_u32(st);
-                vbase = smem_u32(st + T::TILE);
+                tbase = smem_u32(st);
             }
 
-            // ---- S^T = K Q^T  (16 tokens x 8*NT heads)
-            float sacc[T::NT][4];
+            // ---- S^T = K Q^T  (16 tokens x 8*NT heads), two independent chains
+            float sa[T::NT][4], sb[T::NT][4];
 #pragma unroll
-            for (int nt = 0; nt < T::NT; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+            for (int nt = 0; nt < T::NT; ++nt)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) sa[nt][k] = sb[nt][k] = 0.0f;
 #pragma unroll
             for (int kt = 0; kt < T::KT; ++kt) {
                 uint32_t a0, a1, a2, a3;
-                const uint32_t addr = kbase + (kt >> 2) * 2048 + k_tok * 128 +
+                const uint32_t addr = tbase + (kt >> 2) * 4096 + k_tok * 128 +
                                       ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4);
                 ldsm_x4(addr, a0, a1, a2, a3);
 #pragma unroll
-                for (int nt = 0; nt < T::NT; ++nt)
-                    mma_16816<T::MMA_BF16>(sacc[nt], a0, a1, a2, a3, qf[nt][kt][0], qf[nt][kt][1]);
+                for (int nt = 0; nt < T::NT; ++nt) {
+                    if (kt & 1) mma_16816<T::MMA_BF16>(sb[nt], a0, a1, a2, a3, qf[nt][kt][0], qf[nt][kt][1]);
+                    else mma_16816<T::MMA_BF16>(sa[nt], a0, a1, a2, a3, qf[nt][kt][0], qf[nt][kt][1]);
+                }
             }
 
-            // ---- online softmax (log2 domain), P^T fragments via movmatrix
-            uint32_t pb[T::NT][2];
+            // ---- online softmax (log2 domain) with a lazily raised maximum
             const bool v0 = t0 < valid, v1 = t1 < valid;
+            float sv[T::NT][4];
+            bool need = false;
 #pragma unroll
             for (int nt = 0; nt < T::NT; ++nt) {
-                float s00 = v0 ? sacc[nt][0] * p.scale_log2 * ks0 : -INFINITY;
-                float s01 = v0 ? sacc[nt][1] * p.scale_log2 * ks0 : -INFINITY;
-                float s10 = v1 ? sacc[nt][2] * p.scale_log2 * ks1 : -INFINITY;
-                float s11 = v1 ? sacc[nt][3] * p.scale_log2 * ks1 : -INFINITY;
-                float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+                sv[nt][0] = v0 ? (sa[nt][0] + sb[nt][0]) * p.scale_log2 * ks0 : -INFINITY;
+                sv[nt][1] = v0 ? (sa[nt][1] + sb[nt][1]) * p.scale_log2 * ks0 : -INFINITY;
+                sv[nt][2] = v1 ? (sa[nt][2] + sb[nt][2]) * p.scale_log2 * ks1 : -INFINITY;
+                sv[nt][3] = v1 ? (sa[nt][3] + sb[nt][3]) * p.scale_log2 * ks1 : -INFINITY;
+                need |= fmaxf(sv[nt][0], sv[nt][2]) > mrun[nt][0] + kRescaleThreshold;
+                need |= fmaxf(sv[nt][1], sv[nt][3]) > mrun[nt][1] + kRescaleThreshold;
+            }
+            if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-                }
-                const float mn0 = fmaxf(mrun[nt][0], mx0), mn1 = fmaxf(mrun[nt][1], mx1);
-                const float al0 = ex2(mrun[nt][0] - mn0), al1 = ex2(mrun[nt][1] - mn1);
-                mrun[nt][0] = mn0; mrun[nt][1] = mn1;
-                const float p00 = ex2(s00 - mn0), p01 = ex2(s01 - mn1);
-                const float p10 = ex2(s10 - mn0), p11 = ex2(s11 - mn1);
-                lrun[nt][0] = lrun[nt][0] * al0 + (p00 + p10);
-                lrun[nt][1] = lrun[nt][1] * al1 + (p01 + p11);
+                for (int nt = 0; nt < T::NT; ++nt) {
+                    float mx0 = fmaxf(sv[nt][0], sv[nt][2]), mx1 = fmaxf(sv[nt][1], sv[nt][3]);
 #pragma unroll
-                for (int mt = 0; mt < T::MT; ++mt) {
-                    o[nt][mt][0] *= al0; o[nt][mt][1] *= al1;
-                    o[nt][mt][2] *= al0; o[nt][mt][3] *= al1;
+                    for (int off = 4; off < 32; off <<= 1) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                    }
+                    const float mn0 = fmaxf(mrun[nt][0], mx0), mn1 = fmaxf(mrun[nt][1], mx1);
+                    const float al0 = ex2(mrun[nt][0] - mn0), al1 = ex2(mrun[nt][1] - mn1);
+                    mrun[nt][0] = mn0; mrun[nt][1] = mn1;
+                    lrun[nt][0] *= al0; lrun[nt][1] *= al1;
+#pragma unroll
+                    for (int mt = 0; mt < T::MT; ++mt) {
+                        o[nt][mt][0] *= al0; o[nt][mt][1] *= al1;
+                        o[nt][mt][2] *= al0; o[nt][mt][3] *= al1;
+                    }
                 }
+            }
+            uint32_t pb[T::NT][2];
+#pragma unroll
+            for (int nt = 0; nt < T::NT; ++nt) {
+                const float p00 = ex2(sv[nt][0] - mrun[nt][0]), p01 = ex2(sv[nt][1] - mrun[nt][1]);
+                const float p10 = ex2(sv[nt][2] - mrun[nt][0]), p11 = ex2(sv[nt][3] - mrun[nt][1]);
+                lrun[nt][0] += p00 + p10;
+                lrun[nt][1] += p01 + p11;
                 float q00 = p00, q01 = p01, q10 = p10, q11 = p11;
                 if constexpr (T::KV == kFP8) {
                     q00 = v0 ? p00 * vs0 : 0.0f; q01 = v0 ? p01 * vs0 : 0.0f;
@@ -459,26 +638,25 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 pb[nt][1] = movmatrix_t(pack2<T::MMA_BF16>(q10, q11));
             }
 
-            // ---- O^T += V^T P^T  (D x 8*NT)
+            // ---- O^T += V^T P^T  (D x 8*NT); V rows are 16..31 of the tile
 #pragma unroll
             for (int mt = 0; mt < T::MT; ++mt) {
                 uint32_t a0, a1, a2, a3;
-                const uint32_t addr = vbase + (mt >> 2) * 2048 + v_tok * 128 +
+                const uint32_t addr = tbase + (mt >> 2) * 4096 + (16 + v_tok) * 128 +
                                       ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4);
                 ldsm_x4_t(addr, a0, a1, a2, a3);
 #pragma unroll
                 for (int nt = 0; nt < T::NT; ++nt)
                     mma_16816<T::MMA_BF16>(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
             }
+            __syncwarp();
             if constexpr (T::KV != kFP8) {
-                __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.empty[s]);
-            } else {
-                __syncwarp();
             }
         }
 
         // ---- merge the W warps' states for this segment
+        if (ctid == 0 && x + cnt >= end) VW_TRACE(5, globaltimer());
         if (!alive && lane == 0) sm.flag[1] = 1;  // abort marker, read by all warps below
         float* mo = sm.mo + warp * T::G * T::D;
 #pragma unroll
@@ -504,7 +682,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 sm.ml[warp * T::G + j0 + 1] = lrun[nt][1];
             }
         }
-        named_bar_sync(1, W * 32);
+        named_bar_sync(1, NTH);
         // every consumer warp reads the same marker after the barrier, so all of
         // them leave the segment loop together and no named barrier is orphaned
         const bool abort = sm.flag[1] != 0;
@@ -515,7 +693,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         const int slot = (x == begin) ? 0 : 1;
         float* po = p.part_o + ((size_t)blockIdx.x * 2 + slot) * T::G * T::D;
         float* pml = p.part_ml + ((size_t)blockIdx.x * 2 + slot) * T::G * 2;
-        for (int idx = ctid; idx < g * T::D && !abort; idx += W * 32) {
+        for (int idx = ctid; idx < g * T::D && !abort; idx += NTH) {
             const int j = idx / T::D, d = idx - j * T::D;
             float M = -INFINITY;
 #pragma unroll
@@ -523,12 +701,16 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             float Ls = 0.0f, Os = 0.0f;
 #pragma unroll
             for (int w = 0; w < W; ++w) {
-                const float f = ex2(sm.mm[w * T::G + j] - M);
-                Ls += sm.ml[w * T::G + j] * f;
-                Os += sm.mo[(w * T::G + j) * T::D + d] * f;
+                const float mw = sm.mm[w * T::G + j];
+                if (mw > -INFINITY) {                 // warps without pages here add nothing
+                    const float f = ex2(mw - M);
+                    Ls += sm.ml[w * T::G + j] * f;
+                    Os += sm.mo[(w * T::G + j) * T::D + d] * f;
+                }
             }
             if (complete) {
-                out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] = f32_to_io<T::IO>(Os / Ls);
+                out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
+                    f32_to_io<T::IO>(Os / Ls * T::VFOLD);
             } else {
                 po[j * T::D + d] = Os;
                 if (d == 0) { pml[j * 2] = M; pml[j * 2 + 1] = Ls; }
@@ -536,44 +718,78 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         }
         if (!complete && !abort) {
             __threadfence();
-            named_bar_sync(1, W * 32);
+            named_bar_sync(1, NTH);
             const int c0 = s_begin / per_cta, c1 = (s_begin + np - 1) / per_cta;
             if (ctid == 0) {
                 const uint32_t old = atomicAdd(p.counters + seg, 1u);
                 sm.flag[0] = old == (uint32_t)(c1 - c0);
             }
-            named_bar_sync(1, W * 32);
+            named_bar_sync(1, NTH);
             if (sm.flag[0]) {
+                // last piece in: merge every piece's (o, max, sum) from L2 with all
+                // loads of a group of pieces in flight at once
                 __threadfence();
-                for (int idx = ctid; idx < g * T::D; idx += W * 32) {
-                    const int j = idx / T::D, d = idx - j * T::D;
-                    float M = -INFINITY;
-                    for (int c = c0; c <= c1; ++c) {
-                        const int sl = (c == c0 && s_begin != c0 * per_cta) ? 1 : 0;
-                        M = fmaxf(M, __ldcg(p.part_ml + (((size_t)c * 2 + sl) * T::G + j) * 2));
+                float M[T::E], Ls[T::E], Os[T::E];
+#pragma unroll
+                for (int e = 0; e < T::E; ++e) { M[e] = -INFINITY; Ls[e] = 0.0f; Os[e] = 0.0f; }
+                for (int c = c0; c <= c1; c += T::CU) {
+                    float mv[T::CU][T::E], lv[T::CU][T::E], ov[T::CU][T::E];
+#pragma unroll
+                    for (int u = 0; u < T::CU; ++u) {
+                        const int cc = c + u;
+                        const int sl = (cc == c0 && s_begin != c0 * per_cta) ? 1 : 0;
+                        const size_t base = ((size_t)cc * 2 + sl) * T::G;
+#pragma unroll
+                        for (int e = 0; e < T::E; ++e) {
+                            const int idx = ctid + e * NTH;
+                            const int j = idx / T::D, d = idx - (idx / T::D) * T::D;
+                            if (cc <= c1 && idx < g * T::D) {
+                                mv[u][e] = __ldcg(p.part_ml + (base + j) * 2);
+                                lv[u][e] = __ldcg(p.part_ml + (base + j) * 2 + 1);
+                                ov[u][e] = __ldcg(p.part_o + (base + j) * T::D + d);
+                            } else {
+                                mv[u][e] = -INFINITY; lv[u][e] = 0.0f; ov[u][e] = 0.0f;
+                            }
+                        }
                     }
-                    float Ls = 0.0f, Os = 0.0f;
-                    for (int c = c0; c <= c1; ++c) {
-                        const int sl = (c == c0 && s_begin != c0 * per_cta) ? 1 : 0;
-                        const size_t base = ((size_t)c * 2 + sl) * T::G;
-                        const float f = ex2(__ldcg(p.part_ml + (base + j) * 2) - M);
-                        Ls += __ldcg(p.part_ml + (base + j) * 2 + 1) * f;
-                        Os += __ldcg(p.part_o + (base + j) * T::D + d) * f;
+#pragma unroll
+                    for (int u = 0; u < T::CU; ++u) {
+#pragma unroll
+                        for (int e = 0; e < T::E; ++e) {
+                            if (mv[u][e] > -INFINITY) {
+                                const float Mn = fmaxf(M[e], mv[u][e]);
+                                const float fo = ex2(M[e] - Mn), fn = ex2(mv[u][e] - Mn);
+                                Ls[e] = Ls[e] * fo + lv[u][e] * fn;
+                                Os[e] = Os[e] * fo + ov[u][e] * fn;
+                                M[e] = Mn;
+                            }
+                        }
                     }
-                    out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
-                        f32_to_io<T::IO>(Os / Ls);
+                }
+#pragma unroll
+                for (int e = 0; e < T::E; ++e) {
+                    const int idx = ctid + e * NTH;
+                    if (idx < g * T::D) {
+                        const int j = idx / T::D, d = idx - j * T::D;
+                        out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
+                            f32_to_io<T::IO>(Os[e] / Ls[e] * T::VFOLD);
+                    }
                 }
                 if (ctid == 0) p.counters[seg] = 0u;
+#ifdef VW_DECODE_TRACE
+                if (ctid == 0) g_vw_trace[blockIdx.x * 10 + 8] += 1;
+#endif
             }
         }
-        named_bar_sync(1, W * 32);
+        named_bar_sync(1, NTH);
         x += cnt;
         if (abort) break;
     }
+    if (ctid == 0) VW_TRACE(6, globaltimer());
 }
 
 template <class T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
 decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -581,18 +797,21 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     const Smem sm = carve<T>(base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t deadline = globaltimer() + kWaitDeadlineNs;
+    if (threadIdx.x == 0) VW_TRACE(0, globaltimer());
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::S; ++s) { mbar_init(&sm.full[s], 1); mbar_init(&sm.empty[s], 1); }
+        for (int s = 0; s < kQSlots; ++s) { mbar_init(&sm.qfull[s], 1); mbar_init(&sm.qempty[s], T::W); }
         fence_mbar_init();
         sm.flag[0] = 0;
         sm.flag[1] = 0;
     }
     if (warp == kProducerWarp) {
         if (lane == 0) prefetch_tensormap(&tmap);
-        // pages per sequence -> exclusive prefix (one warp, 32 sequences at a time)
-        int run = 0;
-        if (lane == 0) sm.pfx[0] = 0;
+        // pages per sequence -> exclusive prefixes of pages and of non-empty
+        // sequences (one warp, 32 sequences at a time)
+        int run = 0, run_nz = 0;
+        if (lane == 0) { sm.pfx[0] = 0; sm.nzp[0] = 0; }
         for (int base_b = 0; base_b < (int)p.B; base_b += 32) {
             const int b = base_b + lane;
             int np = 0;
@@ -604,17 +823,20 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
                     np = sl <= 0 ? 0 : (int)p.bt_stride;
                 }
             }
-            int incl = np;
+            int incl = np, incl_nz = np > 0 ? 1 : 0;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
                 const int v = __shfl_up_sync(0xffffffffu, incl, off);
-                if (lane >= off) incl += v;
+                const int vz = __shfl_up_sync(0xffffffffu, incl_nz, off);
+                if (lane >= off) { incl += v; incl_nz += vz; }
             }
-            if (b < (int)p.B) sm.pfx[b + 1] = run + incl;
+            if (b < (int)p.B) { sm.pfx[b + 1] = run + incl; sm.nzp[b + 1] = run_nz + incl_nz; }
             run += __shfl_sync(0xffffffffu, incl, 31);
+            run_nz += __shfl_sync(0xffffffffu, incl_nz, 31);
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0) VW_TRACE(1, globaltimer());
 
     const int total = (int)p.Hkv * sm.pfx[p.B];
     int per_cta = (total + (int)gridDim.x - 1) / (int)gridDim.x;
@@ -623,8 +845,15 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     const int end = min(total, begin + per_cta);
     if (begin >= end) return;
 
-    if (warp == kProducerWarp) producer<T>(&tmap, p, sm, begin, end - begin, deadline);
-    else consumer<T>(p, sm, begin, end, per_cta, deadline);
+    if (warp == kProducerWarp) {
+        // ordinal of the first segment of this range among non-empty segments
+        const int b0 = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, begin);
+        const int h0 = (begin - (int)p.Hkv * sm.pfx[b0]) / (sm.pfx[b0 + 1] - sm.pfx[b0]);
+        producer<T>(&tmap, p, sm, begin, end - begin, sm.nzp[b0] * (int)p.Hkv + h0, deadline);
+    } else {
+        consumer<T>(p, sm, begin, end, per_cta, deadline);
+    }
+    if (threadIdx.x == 0) VW_TRACE(7, globaltimer());
 }
 
 template <class T>
@@ -652,8 +881,20 @@ cudaError_t launch_d(const DecodeLaunch& L) {
 
 }  // namespace
 
+int decode_ctas_per_sm() { return kCtasPerSm; }
 size_t decode_scratch_floats_o(int grid, int head_dim) { return (size_t)grid * 2 * 16 * head_dim; }
 size_t decode_scratch_floats_ml(int grid) { return (size_t)grid * 2 * 16 * 2; }
+
+#ifdef VW_DECODE_TRACE
+extern "C" __attribute__((visibility("default"))) int vw_debug_trace(void* host, int reset) {
+    cudaMemcpyFromSymbol(host, g_vw_trace, sizeof(g_vw_trace));
+    if (reset) {
+        static unsigned long long zeros[1024 * 10];
+        cudaMemcpyToSymbol(g_vw_trace, zeros, sizeof(zeros));
+    }
+    return (int)cudaGetLastError();
+}
+#endif
 
 cudaError_t launch_paged_decode(const DecodeLaunch& L) {
     const uint32_t D = L.head_dim;

@@ -10,7 +10,7 @@ namespace vw {
 enum KvKind : uint32_t { kF16 = 0, kBF16 = 1, kFP8 = 2 };
 
 constexpr int kBlockSize = 16;          // tokens per page (engine/engine.bm:102)
-constexpr int kMaxBatchPerLaunch = 2048; // sequences per decode launch (prefix table in smem)
+constexpr int kMaxBatchPerLaunch = 1024; // sequences per decode launch (prefix tables in smem)
 constexpr int kMinPagesPerCta = 8;      // work quantum when the batch is tiny
 
 // Everything a decode launch needs besides the tensor map.
@@ -22,7 +22,7 @@ struct DecodeParams {
     const uint32_t* block_tables;   // [B][bt_stride]
     const uint32_t* seq_lens;       // [B], context length including the new token
     uint8_t* kv_data;           // pool pages (append writes)
-    float* kv_scales;           // FP8 scales [L][NB][2][Hkv][16]
+    float* kv_scales;           // FP8 scales [L][NB][Hkv][2][16]
     float* part_o;              // [grid][2][G][D] split-K partial outputs
     float* part_ml;             // [grid][2][G][2] (running max, sum)
     uint32_t* counters;         // [max_batch * Hkv] arrival counters, all zero between launches
@@ -42,6 +42,7 @@ struct DecodeLaunch {
 // Returns cudaSuccess or the launch error.  Unsupported shapes must have been
 // rejected by the caller.
 cudaError_t launch_paged_decode(const DecodeLaunch& L);
+int decode_ctas_per_sm();
 size_t decode_scratch_floats_o(int grid, int head_dim);
 size_t decode_scratch_floats_ml(int grid);
 

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(PoolGeom g, uint8_t* __r
         return;
     }
     const uint64_t blk = (uint64_t)slot / kBlockSize, t = (uint64_t)slot % kBlockSize;
-    const uint64_t row = ((((uint64_t)layer * g.num_blocks + blk) * 2 + kv) * g.num_kv_heads + h) *
+    const uint64_t row = ((((uint64_t)layer * g.num_blocks + blk) * g.num_kv_heads + h) * 2 + kv) *
                              kBlockSize + t;
     const uint16_t* src = (kv == 0 ? k_new : v_new) + ((uint64_t)i * g.num_kv_heads + h) * g.head_dim;
     if (g.kv_kind != kFP8) {
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256) kv_gather_kernel(PoolGeom g, const uint8_
         if (lane == 0) atomicOr(err, kDevErrBlockId);
         return;
     }
-    const uint64_t row = ((((uint64_t)layer * g.num_blocks + blk) * 2 + kv) * g.num_kv_heads + h) *
+    const uint64_t row = ((((uint64_t)layer * g.num_blocks + blk) * g.num_kv_heads + h) * 2 + kv) *
                              kBlockSize + p % kBlockSize;
     const uint64_t rb = (uint64_t)g.head_dim * elem_bytes(g.kv_kind);
     const uint64_t o = (uint64_t)h * seq_len + p;

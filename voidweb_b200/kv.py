@@ -54,7 +54,7 @@ _DT = {"f16": C.VW_F16, "bf16": C.VW_BF16, "fp8": C.VW_FP8_E4M3}
 
 
 class KvPool:
-    """A paged KV pool on one GPU: pages [L][NB][2][Hkv][16][D] (+ FP8 scales)."""
+    """A paged KV pool on one GPU: pages [L][NB][Hkv][2][16][D] (+ FP8 scales)."""
 
     def __init__(self, spec: PoolSpec, device: int | torch.device = 0,
                  data: torch.Tensor | None = None, scales: torch.Tensor | None = None):
@@ -96,7 +96,7 @@ class KvPool:
     @property
     def page_shape(self):
         s = self.spec
-        return (s.num_layers, s.num_blocks, 2, s.num_kv_heads, 16, s.head_dim)
+        return (s.num_layers, s.num_blocks, s.num_kv_heads, 2, 16, s.head_dim)
 
     # -- views of the library-owned pages (for tests and inspection) ----------
     def pages_u8(self) -> torch.Tensor:
