@@ -114,8 +114,18 @@ typedef struct {
     const void* k_new;             /* optional fused append: [num_seqs][num_kv_heads][head_dim] */
     const void* v_new;             /*   written at position seq_len-1 before attending */
     float scale;                   /* softmax scale; 0 means 1/sqrt(head_dim) (flash_attention.bm:187) */
-    uint32_t reserved;             /* must be 0 */
+    uint32_t flags;                /* VW_DECODE_* bits below, 0 for a plain launch */
 } vw_decode_args;
+
+/* Launch as a programmatic dependent of the previous kernel on the stream: the
+ * kernel may start while its predecessor drains and waits for it before
+ * reading q, k_new, v_new (and, without VW_DECODE_EARLY_PAGES, anything).  At
+ * most two consecutive decode launches of a pool overlap. */
+#define VW_DECODE_PDL 0x1u
+/* With VW_DECODE_PDL: the caller guarantees that the preceding kernel writes
+ * neither the block tables, nor seq_lens, nor this layer's pages, so the
+ * kernel starts streaming pages before the predecessor finishes. */
+#define VW_DECODE_EARLY_PAGES 0x2u
 
 /* Replaces: launch_paged_attn_decode (kernels/attention/flash_attention.bm:180-189,
  * kernel :113-162), generalised to GQA and split-K; with k_new/v_new set it is

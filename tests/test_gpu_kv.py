@@ -188,8 +188,8 @@ def test_gather_and_block_copy_bit_exact(dev, kv):
 
 def test_split_k_extremes(dev):
     """Very long and very short sequences in one batch: segments cut across many
-    CTAs and CTAs spanning many segments; repeated launches reuse the arrival
-    counters (they must reset to zero)."""
+    CTAs and CTAs spanning many segments, merged by the combine grid; repeated
+    launches alternate the two partial sets and must give identical results."""
     ctx = [1, 2, 15, 16, 17, 31, 32, 33, 9000, 3, 1, 4097, 64, 5, 12000]
     c = kvgen.make_case(99, 1, 2, 128, 14, len(ctx), 0, 0, BF16, BF16, ctx=ctx)
     pool = make_pool(c, dev)
@@ -232,6 +232,28 @@ def test_bad_block_id_and_seq_len_are_flagged(dev):
     pool.paged_decode(0, q, tu32(c.block_tables, dev), tu32(sl, dev), out)
     assert pool.check() & C.DEV_ERR_SEQ_LEN
     # untouched data outside the pool: the bad id was skipped, not written
+    pool.close()
+
+
+def test_seq_len_beyond_table_appends_nothing(dev):
+    """A seq_len longer than its block-table row is flagged; the kernel reads
+    the row's pages as full and must not append into a neighbouring row."""
+    from voidweb_b200 import _lib as C
+    c = kvgen.make_case(12, 1, 2, 128, 4, 3, 20, 60, BF16, BF16)
+    pool = make_pool(c, dev)
+    sl = c.seq_lens.copy()
+    sl[0] = c.block_tables.shape[1] * 16 + 5
+    q = t16(c.q[0], dev)
+    out = torch.zeros_like(q)
+    pool.paged_decode(0, q, tu32(c.block_tables, dev), tu32(sl, dev), out,
+                      k_new=t16(c.k_new[0], dev), v_new=t16(c.v_new[0], dev))
+    assert pool.check() & C.DEV_ERR_SEQ_LEN
+    data = c.data.copy()
+    slots = kvgen.new_token_slots(c)
+    slots[0] = -1                              # nothing written for sequence 0
+    oracle.kv_append(c.geom, data, None, 0, c.k_new[0], c.v_new[0], slots)
+    gdata, _ = download_pool(pool, c)
+    assert np.array_equal(gdata, data)
     pool.close()
 
 
@@ -285,4 +307,55 @@ def test_full_size_qwen_layer_sampled(dev):
     ref = oracle.paged_decode_f64(c.geom, data, None, 0, c.q[0], c.Hq, c.block_tables,
                                   c.seq_lens, 1.0 / np.sqrt(128))
     check_close(got, ref, BF16, "qwen full-size layer")
+    pool.close()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_pdl_layer_chain(dev, graph):
+    """Consecutive layers launched as programmatic dependents with early page
+    streaming (the flags a decode step uses), eagerly and inside a CUDA graph:
+    every layer's pages and outputs must match the oracle."""
+    from voidweb_b200 import _lib as C
+    c = kvgen.make_case(41, 6, 2, 128, 14, 9, 20, 2500, BF16, BF16)
+    pool = make_pool(c, dev)
+    bt, sl = tu32(c.block_tables, dev), tu32(c.seq_lens, dev)
+    qs = [t16(c.q[l], dev) for l in range(c.L)]
+    ks = [t16(c.k_new[l], dev) for l in range(c.L)]
+    vs = [t16(c.v_new[l], dev) for l in range(c.L)]
+    outs = [torch.zeros_like(qs[0]) for _ in range(c.L)]
+    flags = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
+    s = torch.cuda.Stream(device=dev)
+
+    def step(stream):
+        for l in range(c.L):
+            pool.paged_decode(l, qs[l], bt, sl, outs[l], k_new=ks[l], v_new=vs[l],
+                              stream=stream, flags=flags)
+
+    if graph:
+        with torch.cuda.stream(s):
+            step(s)                     # attribute set-up outside the capture
+        s.synchronize()
+        upload_pool(pool, c)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step(torch.cuda.current_stream())
+        for _ in range(3):              # replays re-append the same rows: idempotent
+            g.replay()
+        torch.cuda.synchronize()
+        del g
+    else:
+        with torch.cuda.stream(s):
+            step(s)
+        s.synchronize()
+    assert pool.check() == 0
+    data = c.data.copy()
+    slots = kvgen.new_token_slots(c)
+    for l in range(c.L):
+        oracle.kv_append(c.geom, data, None, l, c.k_new[l], c.v_new[l], slots)
+    gdata, _ = download_pool(pool, c)
+    assert np.array_equal(gdata, data)
+    for l in range(c.L):
+        ref = oracle.paged_decode_f64(c.geom, data, None, l, c.q[l], c.Hq, c.block_tables,
+                                      c.seq_lens, 1.0 / np.sqrt(128))
+        check_close(outs[l].cpu().numpy().view(np.uint16), ref, BF16, f"layer {l}")
     pool.close()

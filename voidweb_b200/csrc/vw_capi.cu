@@ -89,9 +89,12 @@ struct vw_pool {
     alignas(64) CUtensorMap tmap;
     float* part_o = nullptr;
     float* part_ml = nullptr;
-    uint32_t* counters = nullptr;
     uint32_t* err = nullptr;
     int grid = 0;
+    // split-K scratch: two sets, alternated per decode launch so that two
+    // overlapping launches (programmatic dependent launch) never share one
+    size_t scratch_o = 0, scratch_ml = 0;
+    uint64_t launches = 0;
     // staging for vw_decode_step_host (grow-only)
     uint8_t* stage = nullptr;
     size_t stage_bytes = 0;
@@ -107,7 +110,6 @@ void pool_free_all(vw_pool* p) {
     if (p->own_scales && p->scales) cudaFree(p->scales);
     if (p->part_o) cudaFree(p->part_o);
     if (p->part_ml) cudaFree(p->part_ml);
-    if (p->counters) cudaFree(p->counters);
     if (p->err) cudaFree(p->err);
     if (p->stage) cudaFree(p->stage);
     if (p->s_h2d) cudaStreamDestroy(p->s_h2d);
@@ -212,17 +214,16 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
     }
     const size_t n_o = decode_scratch_floats_o(p->grid, c.head_dim);
     const size_t n_ml = decode_scratch_floats_ml(p->grid);
-    const size_t n_ctr = (size_t)c.max_batch * c.num_kv_heads;
-    if ((e = cudaMalloc(&p->part_o, n_o * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&p->part_ml, n_ml * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&p->counters, n_ctr * 4)) != cudaSuccess ||
+    p->scratch_o = n_o;
+    p->scratch_ml = n_ml;
+    if ((e = cudaMalloc(&p->part_o, 2 * n_o * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&p->part_ml, 2 * n_ml * 4)) != cudaSuccess ||
         (e = cudaMalloc(&p->err, 4)) != cudaSuccess) {
         pool_free_all(p);
         delete p;
         return fail(VW_ERR_OOM, "vw_pool_create: scratch: %s", cudaGetErrorString(e));
     }
-    if ((e = cudaMemset(p->counters, 0, n_ctr * 4)) != cudaSuccess ||
-        (e = cudaMemset(p->err, 0, 4)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+    if ((e = cudaMemset(p->err, 0, 4)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
         pool_free_all(p);
         delete p;
         return cuda_fail(e, "vw_pool_create: memset");
@@ -290,7 +291,10 @@ int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const voi
 static int32_t decode_validate(const vw_pool* pool, const vw_decode_args* a) {
     if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: null argument");
     const PoolGeom& g = pool->geom;
-    if (a->reserved != 0) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: reserved must be 0");
+    if (a->flags & ~(uint32_t)(VW_DECODE_PDL | VW_DECODE_EARLY_PAGES))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: unknown flags 0x%x", a->flags);
+    if ((a->flags & VW_DECODE_EARLY_PAGES) && !(a->flags & VW_DECODE_PDL))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: VW_DECODE_EARLY_PAGES needs VW_DECODE_PDL");
     if (a->layer >= g.num_layers)
         return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: layer %u >= %u", a->layer, g.num_layers);
     if (a->num_seqs > pool->cfg.max_batch)
@@ -328,9 +332,10 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
     p.seq_lens = a->seq_lens;
     p.kv_data = pool->data;
     p.kv_scales = pool->scales;
-    p.part_o = pool->part_o;
-    p.part_ml = pool->part_ml;
-    p.counters = pool->counters;
+    const uint64_t set = pool->launches++ & 1;
+    p.part_o = pool->part_o + set * pool->scratch_o;
+    p.part_ml = pool->part_ml + set * pool->scratch_ml;
+    p.flags = a->flags;
     p.err = pool->err;
     p.B = a->num_seqs;
     p.Hq = a->num_q_heads;
@@ -468,6 +473,9 @@ int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* str
             da.k_new = d_k + l * kb;
             da.v_new = d_v + l * kb;
             da.scale = a->scale;
+            // consecutive layers of a chunk: the previous launch writes only its own
+            // layer's pages and outputs, so this one may stream pages early
+            if (l > l0) da.flags = VW_DECODE_PDL | VW_DECODE_EARLY_PAGES;
             rc = decode_validate(pool, &da);
             if (rc == VW_OK) rc = decode_launch(pool, &da, cs);
         }

@@ -13,8 +13,9 @@
 //    into equal contiguous ranges, one per CTA of a persistent grid of two CTAs
 //    per SM, so every CTA streams the same number of bytes whatever the context
 //    lengths (split-K over pages).  A segment cut by a range boundary leaves
-//    (o, max, sum) partials; the last CTA to finish a piece of it (an atomic
-//    arrival counter, no waiting) merges them.
+//    (o, max, sum) partials, which a small combine grid launched right behind
+//    the decode (programmatic dependent launch) merges; the decode CTAs
+//    themselves never wait for one another or take an atomic.
 //  * GQA.  The Hq/Hkv query heads that share a KV head are processed together:
 //    each page is read from HBM once per KV head, never once per query head.
 //  * Data movement.  A producer warp resolves block ids 32 pages at a time, one
@@ -73,8 +74,8 @@ namespace vw {
 // stamps of [start, prologue done, first load issued, first page ready, last
 // load issued, last page done, merges done, exit] and combines done, for the
 // most recent launch; read back with vw_debug_trace().
-__device__ unsigned long long g_vw_trace[1024 * 10];
-#define VW_TRACE(slot, val) (g_vw_trace[blockIdx.x * 10 + (slot)] = (val))
+__device__ unsigned long long g_vw_trace[1024 * 16];
+#define VW_TRACE(slot, val) (g_vw_trace[blockIdx.x * 16 + (slot)] = (val))
 #else
 #define VW_TRACE(slot, val) ((void)0)
 #endif
@@ -109,7 +110,7 @@ struct Traits {
     static constexpr int KT = D / 16;                        // k-steps of Q K^T
     static constexpr int MT = D / 16;                        // d-tiles of V^T P^T
     static constexpr int CTILE = KV == kFP8 ? 32 * D * 2 : 0;  // f16 page-head per warp
-    static constexpr int MERGE = W * G * (D + 2) * 4;
+    static constexpr int MERGE = W * G * (D + 2) * 4 + (W + 2) * G * 4;
     static constexpr int QTILE = G * D * 2;
     static constexpr int PFX = align_up_c(2 * (kMaxBatchPerLaunch + 1) * 4, 128);
     static constexpr int FIXED = W * CTILE + align_up_c(MERGE, 1024) +
@@ -131,8 +132,6 @@ struct Traits {
     // FP8: probabilities carry the V scale but not the 1/256 of the f16 code
     // expansion; the output is multiplied back by 256
     static constexpr float VFOLD = KV == kFP8 ? 256.0f : 1.0f;
-    static constexpr int E = (G * D + W * 32 - 1) / (W * 32);   // combine elements per thread
-    static constexpr int CU = E > 4 ? 2 : 4;                     // combine pieces loaded at once
     static_assert(CHUNKS >= 1, "row must be at least 128 bytes");
     static_assert(S >= 4, "too few pipeline stages");
     static_assert(S % W == 0 && S % kIssuers == 0, "stage ownership needs S % W == S % issuers == 0");
@@ -156,6 +155,7 @@ struct Smem {
     float* mo;           // [W][G][D]
     float* mm;           // [W][G]
     float* ml;           // [W][G]
+    float* mf;           // [W][G] warp weights, then [G] max, [G] sum
     uint8_t* qring;      // [kQSlots][G][D] io dtype
     int* pfx;            // [B+1] exclusive prefix of pages per sequence
     int* nzp;            // [B+1] exclusive prefix of sequences with pages
@@ -164,7 +164,7 @@ struct Smem {
     uint64_t* empty;     // [S]
     uint64_t* qfull;     // [kQSlots]
     uint64_t* qempty;    // [kQSlots]
-    int* flag;           // [0] last-arrival broadcast, [1] abort marker
+    int* flag;           // [1] abort marker ([0] unused)
 };
 
 template <class T>
@@ -177,6 +177,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     s.mo = reinterpret_cast<float*>(p);
     s.mm = s.mo + T::W * T::G * T::D;
     s.ml = s.mm + T::W * T::G;
+    s.mf = s.ml + T::W * T::G;
     p += align_up_c(T::MERGE, 1024);
     s.qring = p; p += align_up_c(kQSlots * T::QTILE, 1024);
     s.pfx = reinterpret_cast<int*>(p);
@@ -279,9 +280,49 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
         sm.pinfo[buf * 32 + lane] = pi;
     };
 
+    // Issue page ii (this lane owns its stage) into stage ii % S.
+    auto issue_page = [&](int ii, const PageInfo& pi) -> bool {
+        const int s = ii % T::S;
+        if (ii >= T::S && !mbar_wait(&sm.empty[s], ((ii / T::S) - 1) & 1, deadline)) return false;
+        if (ii == 0) VW_TRACE(2, globaltimer());
+        if (ii == n - 1) VW_TRACE(4, globaltimer());
+        uint8_t* st = sm.stages + s * T::STAGE;
+        if constexpr (T::KV == kFP8) {
+            float* sc = sm.scal + s * 32;
+            if (pi.row0 >= 0) {
+                // the page-head's K and V scales: 32 consecutive f32
+                mbar_arrive_expect_tx(&sm.full[s], T::STAGE + 128);
+                bulk_load(sc, p.kv_scales + pi.row0, 128, &sm.full[s]);
+            } else {
+                // invalid block id: zero scales with plain stores, ordered before
+                // the arrive and fenced against this slot's next bulk write
+                for (int k = 0; k < 32; ++k) sc[k] = 0.0f;
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
+            }
+        } else {
+            mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
+        }
+#pragma unroll
+        for (int c = 0; c < T::CHUNKS; ++c)
+            tma_load_2d(st + c * 4096, tmap, &sm.full[s], c * (128 / T::EB), pi.row0);
+        return true;
+    };
+
     Resolved cur = resolve_page(p, sm, begin, first_ord, lane, n);
     publish(cur, 0);
     __syncwarp();
+    // Early pages: the first S pages fill every stage once and need no empty
+    // wait.  With kDecodeEarlyPages they are issued before the predecessor
+    // grid has finished (the caller vouches that it writes neither the tables
+    // nor these pages); the query tiles wait for it.
+    const int early_n = (p.flags & kDecodeEarlyPages) ? min(T::S, n) : 0;
+    if (lane < kIssuers)
+        for (int j = lane; j < early_n; j += kIssuers) issue_page(j, sm.pinfo[j]);
+    if (p.flags & kDecodePdl) {
+        griddep_wait();
+        griddep_launch_dependents();
+    }
     int buf = 0;
     for (int i0 = 0; i0 < n; i0 += 32) {
         const Resolved nxt = resolve_page(p, sm, begin, first_ord, i0 + 32 + lane, n);
@@ -306,34 +347,11 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
                               &sm.qfull[qs]);
                     segs_issued = k + 1;
                 }
-                if ((j % kIssuers) != lane) continue;   // another lane's stage
-                const int s = ii % T::S;
-                if (ii >= T::S && !mbar_wait(&sm.empty[s], ((ii / T::S) - 1) & 1, deadline)) {
+                if ((j % kIssuers) != lane || ii < early_n) continue;   // another lane's stage
+                if (!issue_page(ii, pi)) {
                     ok = false;
                     break;
                 }
-                if (ii == 0) VW_TRACE(2, globaltimer());
-                if (ii == n - 1) VW_TRACE(4, globaltimer());
-                uint8_t* st = sm.stages + s * T::STAGE;
-                if constexpr (T::KV == kFP8) {
-                    float* sc = sm.scal + s * 32;
-                    if (pi.row0 >= 0) {
-                        // the page-head's K and V scales: 32 consecutive f32
-                        mbar_arrive_expect_tx(&sm.full[s], T::STAGE + 128);
-                        bulk_load(sc, p.kv_scales + pi.row0, 128, &sm.full[s]);
-                    } else {
-                        // invalid block id: zero scales with plain stores, ordered before
-                        // the arrive and fenced against this slot's next bulk write
-                        for (int k = 0; k < 32; ++k) sc[k] = 0.0f;
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
-                    }
-                } else {
-                    mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
-                }
-#pragma unroll
-                for (int c = 0; c < T::CHUNKS; ++c)
-                    tma_load_2d(st + c * 4096, tmap, &sm.full[s], c * (128 / T::EB), pi.row0);
             }
         }
         if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
@@ -498,7 +516,6 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         const int seg_start = Hkv * sm.pfx[b];
         const int r = x - seg_start;
         const int h = r / np, pg0 = r - h * np;
-        const int s_begin = seg_start + h * np;       // flat index of this segment's page 0
         const int cnt = min(np - pg0, end - x);
         const bool complete = pg0 == 0 && cnt == np;
         const int i_base = x - begin;
@@ -546,8 +563,12 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             if (i == 0 && lane == 0) VW_TRACE(3, globaltimer());
             int valid = 16;
             if (pg == np - 1) {
+                // a seq_len beyond the table (flagged in the prologue) reads its
+                // pages as full and appends nothing
                 valid = seq_len - pg * 16;
-                if (append) {
+                const bool in_page = valid <= 16;
+                if (!in_page) valid = 16;
+                if (append && in_page) {
                     const uint32_t blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg);
                     append_row<T>(p, st, sc, b, h, blk, valid - 1, lane);
                 }
@@ -686,99 +707,43 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         // every consumer warp reads the same marker after the barrier, so all of
         // them leave the segment loop together and no named barrier is orphaned
         const bool abort = sm.flag[1] != 0;
-
         const int g = (int)p.group;
-        const int seg = b * Hkv + h;
+        // per-head weights of the W warp states: max, sum, and one factor per
+        // warp (warps without pages in this segment carry -inf and get 0)
+        if (ctid < g) {
+            const int j = ctid;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < W; ++w) M = fmaxf(M, sm.mm[w * T::G + j]);
+            float Ls = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float mw = sm.mm[w * T::G + j];
+                const float f = mw > -INFINITY ? ex2(mw - M) : 0.0f;
+                Ls += sm.ml[w * T::G + j] * f;
+                sm.mf[w * T::G + j] = f;
+            }
+            sm.mf[W * T::G + j] = M;
+            sm.mf[(W + 1) * T::G + j] = Ls;
+        }
+        named_bar_sync(1, NTH);
+        // A segment wholly inside this range is written out here; a piece of a
+        // segment split across ranges leaves (o, max, sum) for the combine kernel.
         uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
         const int slot = (x == begin) ? 0 : 1;
         float* po = p.part_o + ((size_t)blockIdx.x * 2 + slot) * T::G * T::D;
         float* pml = p.part_ml + ((size_t)blockIdx.x * 2 + slot) * T::G * 2;
         for (int idx = ctid; idx < g * T::D && !abort; idx += NTH) {
             const int j = idx / T::D, d = idx - j * T::D;
-            float M = -INFINITY;
+            float Os = 0.0f;
 #pragma unroll
-            for (int w = 0; w < W; ++w) M = fmaxf(M, sm.mm[w * T::G + j]);
-            float Ls = 0.0f, Os = 0.0f;
-#pragma unroll
-            for (int w = 0; w < W; ++w) {
-                const float mw = sm.mm[w * T::G + j];
-                if (mw > -INFINITY) {                 // warps without pages here add nothing
-                    const float f = ex2(mw - M);
-                    Ls += sm.ml[w * T::G + j] * f;
-                    Os += sm.mo[(w * T::G + j) * T::D + d] * f;
-                }
-            }
+            for (int w = 0; w < W; ++w) Os += sm.mo[(w * T::G + j) * T::D + d] * sm.mf[w * T::G + j];
             if (complete) {
                 out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
-                    f32_to_io<T::IO>(Os / Ls * T::VFOLD);
+                    f32_to_io<T::IO>(Os / sm.mf[(W + 1) * T::G + j] * T::VFOLD);
             } else {
                 po[j * T::D + d] = Os;
-                if (d == 0) { pml[j * 2] = M; pml[j * 2 + 1] = Ls; }
-            }
-        }
-        if (!complete && !abort) {
-            __threadfence();
-            named_bar_sync(1, NTH);
-            const int c0 = s_begin / per_cta, c1 = (s_begin + np - 1) / per_cta;
-            if (ctid == 0) {
-                const uint32_t old = atomicAdd(p.counters + seg, 1u);
-                sm.flag[0] = old == (uint32_t)(c1 - c0);
-            }
-            named_bar_sync(1, NTH);
-            if (sm.flag[0]) {
-                // last piece in: merge every piece's (o, max, sum) from L2 with all
-                // loads of a group of pieces in flight at once
-                __threadfence();
-                float M[T::E], Ls[T::E], Os[T::E];
-#pragma unroll
-                for (int e = 0; e < T::E; ++e) { M[e] = -INFINITY; Ls[e] = 0.0f; Os[e] = 0.0f; }
-                for (int c = c0; c <= c1; c += T::CU) {
-                    float mv[T::CU][T::E], lv[T::CU][T::E], ov[T::CU][T::E];
-#pragma unroll
-                    for (int u = 0; u < T::CU; ++u) {
-                        const int cc = c + u;
-                        const int sl = (cc == c0 && s_begin != c0 * per_cta) ? 1 : 0;
-                        const size_t base = ((size_t)cc * 2 + sl) * T::G;
-#pragma unroll
-                        for (int e = 0; e < T::E; ++e) {
-                            const int idx = ctid + e * NTH;
-                            const int j = idx / T::D, d = idx - (idx / T::D) * T::D;
-                            if (cc <= c1 && idx < g * T::D) {
-                                mv[u][e] = __ldcg(p.part_ml + (base + j) * 2);
-                                lv[u][e] = __ldcg(p.part_ml + (base + j) * 2 + 1);
-                                ov[u][e] = __ldcg(p.part_o + (base + j) * T::D + d);
-                            } else {
-                                mv[u][e] = -INFINITY; lv[u][e] = 0.0f; ov[u][e] = 0.0f;
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < T::CU; ++u) {
-#pragma unroll
-                        for (int e = 0; e < T::E; ++e) {
-                            if (mv[u][e] > -INFINITY) {
-                                const float Mn = fmaxf(M[e], mv[u][e]);
-                                const float fo = ex2(M[e] - Mn), fn = ex2(mv[u][e] - Mn);
-                                Ls[e] = Ls[e] * fo + lv[u][e] * fn;
-                                Os[e] = Os[e] * fo + ov[u][e] * fn;
-                                M[e] = Mn;
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int e = 0; e < T::E; ++e) {
-                    const int idx = ctid + e * NTH;
-                    if (idx < g * T::D) {
-                        const int j = idx / T::D, d = idx - j * T::D;
-                        out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
-                            f32_to_io<T::IO>(Os[e] / Ls[e] * T::VFOLD);
-                    }
-                }
-                if (ctid == 0) p.counters[seg] = 0u;
-#ifdef VW_DECODE_TRACE
-                if (ctid == 0) g_vw_trace[blockIdx.x * 10 + 8] += 1;
-#endif
+                if (d == 0) { pml[j * 2] = sm.mf[W * T::G + j]; pml[j * 2 + 1] = sm.mf[(W + 1) * T::G + j]; }
             }
         }
         named_bar_sync(1, NTH);
@@ -805,6 +770,19 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         fence_mbar_init();
         sm.flag[0] = 0;
         sm.flag[1] = 0;
+    }
+    // Programmatic dependent launch: without early pages everything waits for
+    // the predecessor before the first global read; each thread lets the next
+    // grid launch only after its own wait, so at most two grids overlap.
+    const bool pdl = (p.flags & kDecodePdl) != 0;
+    const bool early = pdl && (p.flags & kDecodeEarlyPages) != 0;
+    if (pdl && !early) {
+        griddep_wait();
+        griddep_launch_dependents();
+    } else if (!pdl) {
+        // the successor is this launch's own combine grid, which waits for the
+        // whole of this grid before it reads anything this grid writes
+        griddep_launch_dependents();
     }
     if (warp == kProducerWarp) {
         if (lane == 0) prefetch_tensormap(&tmap);
@@ -849,11 +827,115 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         // ordinal of the first segment of this range among non-empty segments
         const int b0 = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, begin);
         const int h0 = (begin - (int)p.Hkv * sm.pfx[b0]) / (sm.pfx[b0 + 1] - sm.pfx[b0]);
-        producer<T>(&tmap, p, sm, begin, end - begin, sm.nzp[b0] * (int)p.Hkv + h0, deadline);
+        DecodeParams pp = p;
+        if (!early) pp.flags &= ~(kDecodePdl | kDecodeEarlyPages);   // already waited above
+        producer<T>(&tmap, pp, sm, begin, end - begin, sm.nzp[b0] * (int)p.Hkv + h0, deadline);
     } else {
+        if (early) {
+            griddep_wait();            // q, k_new, v_new may come from the predecessor
+            griddep_launch_dependents();
+        }
         consumer<T>(p, sm, begin, end, per_cta, deadline);
     }
     if (threadIdx.x == 0) VW_TRACE(7, globaltimer());
+}
+
+// ------------------------------------------------------------------ combine
+
+constexpr int kCombineThreads = 256;
+
+// Merge of the split-K partials, one CTA per (sequence, KV head) segment.  The
+// CTA recomputes the decode grid's page ranges from seq_lens (same clamping,
+// same per-CTA quantum), returns at once for a segment that one decode CTA
+// finished, and otherwise merges the pieces (o, max, sum) left by decode CTAs
+// c0..c1 with weights 2^(max_c - max) -- the merge rule of the online softmax
+// in flash_attention.bm:149-157, applied across pieces instead of tokens.
+// Launched as a programmatic dependent of its decode grid: the geometry is
+// computed while the decode still runs, the partials are read after
+// griddepcontrol.wait.  Each thread produces four consecutive output elements.
+template <int D, int G, int IO>
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeParams p, int dec_grid,
+                                                                  float vfold) {
+    __shared__ int red[kCombineThreads / 32][2];
+    // the next grid (the following layer's decode) may start its prologue now;
+    // it waits for this whole grid before it writes anything this grid reads
+    griddep_launch_dependents();
+    const int Hkv = (int)p.Hkv;
+    const int b = (int)blockIdx.x / Hkv, h = (int)blockIdx.x - b * Hkv;
+    auto pages = [&](int i) {
+        const int sl = (int)__ldcg(p.seq_lens + i);
+        const int np = (sl + 15) >> 4;
+        return sl <= 0 ? 0 : min(np, (int)p.bt_stride);
+    };
+    int before = 0, all = 0;
+    for (int i = threadIdx.x; i < (int)p.B; i += kCombineThreads) {
+        const int np = pages(i);
+        all += np;
+        if (i < b) before += np;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        before += __shfl_xor_sync(0xffffffffu, before, off);
+        all += __shfl_xor_sync(0xffffffffu, all, off);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { red[warp][0] = before; red[warp][1] = all; }
+    __syncthreads();
+    before = all = 0;
+#pragma unroll
+    for (int w = 0; w < kCombineThreads / 32; ++w) { before += red[w][0]; all += red[w][1]; }
+    const int np = pages(b);
+    if (np == 0) return;
+    const int total = Hkv * all;
+    int per_cta = (total + dec_grid - 1) / dec_grid;
+    if (per_cta < kMinPagesPerCta) per_cta = kMinPagesPerCta;
+    const int s_begin = Hkv * before + h * np;
+    const int c0 = s_begin / per_cta, c1 = (s_begin + np - 1) / per_cta;
+    if (c0 == c1) return;                      // written out by the decode CTA itself
+    // CTA c0 holds this segment in slot 0 when the segment starts its range,
+    // else in slot 1 (its last segment); every later CTA starts inside it
+    const int slot0 = s_begin == c0 * per_cta ? 0 : 1;
+    griddep_wait();
+    const int g = (int)p.group;
+    uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
+    for (int u = threadIdx.x; u < g * (D / 4); u += kCombineThreads) {
+        const int j = u / (D / 4), d = (u - j * (D / 4)) * 4;
+        float M = -INFINITY;
+#pragma unroll 4
+        for (int c = c0; c <= c1; ++c) {
+            const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
+            M = fmaxf(M, __ldcg(p.part_ml + piece * G * 2 + j * 2));
+        }
+        float Ls = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 4
+        for (int c = c0; c <= c1; ++c) {
+            const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
+            const float m = __ldcg(p.part_ml + piece * G * 2 + j * 2);
+            const float l = __ldcg(p.part_ml + piece * G * 2 + j * 2 + 1);
+            const float4 o = __ldcg(reinterpret_cast<const float4*>(p.part_o + (piece * G + j) * D + d));
+            const float w = m > -INFINITY ? ex2(m - M) : 0.0f;
+            Ls += l * w;
+            a0 += o.x * w; a1 += o.y * w; a2 += o.z * w; a3 += o.w * w;
+        }
+        const float r = vfold / Ls;
+        const uint32_t lo = (uint32_t)f32_to_io<IO>(a0 * r) | ((uint32_t)f32_to_io<IO>(a1 * r) << 16);
+        const uint32_t hi = (uint32_t)f32_to_io<IO>(a2 * r) | ((uint32_t)f32_to_io<IO>(a3 * r) << 16);
+        *reinterpret_cast<uint2*>(out + ((size_t)b * p.Hq + (size_t)h * g + j) * D + d) = make_uint2(lo, hi);
+    }
+}
+
+template <class T>
+cudaError_t launch_combine(const DecodeLaunch& L) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(L.p.B * L.p.Hkv);
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.stream = L.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, combine_kernel<T::D, T::G, T::IO>, L.p, L.grid, T::VFOLD);
 }
 
 template <class T>
@@ -869,8 +951,21 @@ cudaError_t launch_t(const DecodeLaunch& L) {
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    decode_kernel<T><<<L.grid, kThreads, T::SMEM, L.stream>>>(*L.tmap, L.p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(L.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = T::SMEM;
+    cfg.stream = L.stream;
+    cudaLaunchAttribute attr[1];
+    if (L.p.flags & kDecodePdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<T>, *L.tmap, L.p);
+    if (e != cudaSuccess) return e;
+    return launch_combine<T>(L);
 }
 
 template <int D, int KV, int IO>
@@ -889,7 +984,7 @@ size_t decode_scratch_floats_ml(int grid) { return (size_t)grid * 2 * 16 * 2; }
 extern "C" __attribute__((visibility("default"))) int vw_debug_trace(void* host, int reset) {
     cudaMemcpyFromSymbol(host, g_vw_trace, sizeof(g_vw_trace));
     if (reset) {
-        static unsigned long long zeros[1024 * 10];
+        static unsigned long long zeros[1024 * 16];
         cudaMemcpyToSymbol(g_vw_trace, zeros, sizeof(zeros));
     }
     return (int)cudaGetLastError();

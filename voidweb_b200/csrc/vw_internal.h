@@ -25,11 +25,14 @@ struct DecodeParams {
     float* kv_scales;           // FP8 scales [L][NB][Hkv][2][16]
     float* part_o;              // [grid][2][G][D] split-K partial outputs
     float* part_ml;             // [grid][2][G][2] (running max, sum)
-    uint32_t* counters;         // [max_batch * Hkv] arrival counters, all zero between launches
     uint32_t* err;              // device error word
     uint32_t B, Hq, Hkv, group, num_blocks, layer, bt_stride, fp8_ocp;
     float scale_log2;           // softmax scale * log2(e)
+    uint32_t flags;             // kDecodePdl | kDecodeEarlyPages
 };
+
+constexpr uint32_t kDecodePdl = 0x1u;
+constexpr uint32_t kDecodeEarlyPages = 0x2u;
 
 struct DecodeLaunch {
     DecodeParams p;

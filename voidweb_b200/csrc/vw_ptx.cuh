@@ -105,6 +105,18 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- programmatic dependent launch -------------------------------------------
+
+// Wait until the preceding grid on the stream has completed and its memory is
+// visible (no-op when the kernel was not launched as a programmatic dependent).
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Let the next programmatic dependent grid start launching.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- named barrier among a subset of warps ---------------------------------
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {

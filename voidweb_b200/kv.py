@@ -126,16 +126,17 @@ class KvPool:
 
     def paged_decode(self, layer: int, q: torch.Tensor, block_tables: torch.Tensor,
                      seq_lens: torch.Tensor, out: torch.Tensor, k_new=None, v_new=None,
-                     scale: float = 0.0, stream=None) -> torch.Tensor:
+                     scale: float = 0.0, stream=None, flags: int = 0) -> torch.Tensor:
         """o = softmax(q K^T * scale) V over each sequence's pages (GQA, split-K).
 
         With k_new/v_new given, the new token's rows are first written at
         position seq_len-1 (fused append).  q/out: [B][Hq][D]; block_tables:
         [B][stride] int32 ids; seq_lens: [B] int32 (including the new token).
+        flags: VW_DECODE_PDL / VW_DECODE_EARLY_PAGES (see include/voidweb_kv.h).
         """
         B, Hq, _ = q.shape
         a = C.DecodeArgs(layer, B, Hq, block_tables.shape[1], _ptr(q), _ptr(block_tables),
-                         _ptr(seq_lens), _ptr(out), _ptr(k_new), _ptr(v_new), scale, 0)
+                         _ptr(seq_lens), _ptr(out), _ptr(k_new), _ptr(v_new), scale, flags)
         C.check(C.lib().vw_paged_decode(self._h, ctypes.byref(a), _stream(stream)))
         return out
 
