@@ -479,7 +479,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,
-            "gpu_launches": args.steps * L,
+            # per layer: the fused append+decode grid and its split-K combine grid
+            "gpu_launches": args.steps * L * 2,
         }
         print(json.dumps(line), flush=True)
     del graph

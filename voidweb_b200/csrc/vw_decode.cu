@@ -843,6 +843,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
 // ------------------------------------------------------------------ combine
 
 constexpr int kCombineThreads = 256;
+constexpr int kCombineBatch = 8;       // pieces loaded per round trip
 
 // Merge of the split-K partials, one CTA per (sequence, KV head) segment.  The
 // CTA recomputes the decode grid's page ranges from seq_lens (same clamping,
@@ -897,25 +898,39 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodePa
     const int slot0 = s_begin == c0 * per_cta ? 0 : 1;
     griddep_wait();
     const int g = (int)p.group;
+    const int n = c1 - c0 + 1;
     uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
     for (int u = threadIdx.x; u < g * (D / 4); u += kCombineThreads) {
         const int j = u / (D / 4), d = (u - j * (D / 4)) * 4;
-        float M = -INFINITY;
-#pragma unroll 4
-        for (int c = c0; c <= c1; ++c) {
-            const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
-            M = fmaxf(M, __ldcg(p.part_ml + piece * G * 2 + j * 2));
-        }
-        float Ls = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 4
-        for (int c = c0; c <= c1; ++c) {
-            const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
-            const float m = __ldcg(p.part_ml + piece * G * 2 + j * 2);
-            const float l = __ldcg(p.part_ml + piece * G * 2 + j * 2 + 1);
-            const float4 o = __ldcg(reinterpret_cast<const float4*>(p.part_o + (piece * G + j) * D + d));
-            const float w = m > -INFINITY ? ex2(m - M) : 0.0f;
-            Ls += l * w;
-            a0 += o.x * w; a1 += o.y * w; a2 += o.z * w; a3 += o.w * w;
+        // up to kBatch pieces are loaded at once (one memory round trip); longer
+        // segments continue with a running rescale, batch by batch
+        float M = -INFINITY, Ls = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        for (int k0 = 0; k0 < n; k0 += kCombineBatch) {
+            float2 ml[kCombineBatch];
+            float4 o[kCombineBatch];
+#pragma unroll
+            for (int k = 0; k < kCombineBatch; ++k) {
+                ml[k] = make_float2(-INFINITY, 0.0f);
+                o[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (k0 + k < n) {
+                    const int c = c0 + k0 + k;
+                    const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
+                    ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (piece * G + j) * 2));
+                    o[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + (piece * G + j) * D + d));
+                }
+            }
+            float Mn = M;
+#pragma unroll
+            for (int k = 0; k < kCombineBatch; ++k) Mn = fmaxf(Mn, ml[k].x);
+            const float r = M > -INFINITY ? ex2(M - Mn) : 0.0f;
+            Ls *= r; a0 *= r; a1 *= r; a2 *= r; a3 *= r;
+#pragma unroll
+            for (int k = 0; k < kCombineBatch; ++k) {
+                const float w = ml[k].x > -INFINITY ? ex2(ml[k].x - Mn) : 0.0f;
+                Ls += ml[k].y * w;
+                a0 += o[k].x * w; a1 += o[k].y * w; a2 += o[k].z * w; a3 += o[k].w * w;
+            }
+            M = Mn;
         }
         const float r = vfold / Ls;
         const uint32_t lo = (uint32_t)f32_to_io<IO>(a0 * r) | ((uint32_t)f32_to_io<IO>(a1 * r) << 16);
