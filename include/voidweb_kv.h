@@ -134,6 +134,27 @@ typedef struct {
  * scratch is shared). */
 VW_API int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream);
 
+/* vw_paged_decode with its split-K scratch in a fixed array compiled into this
+ * library instead of in memory the pool allocated.  No counterpart in the
+ * reference: its single-CTA-per-sequence decode keeps no partials at all.
+ *
+ * For callers that cannot allocate device memory where they decode -- a
+ * serving loop that has handed all free HBM to its own caching allocator, or
+ * code that must not call cudaMalloc because it synchronises the device --
+ * and that want the decode to touch no library-allocated scratch: neither
+ * this call nor its one-time setup allocates anything.  Same arguments,
+ * results and flags as vw_paged_decode.
+ *
+ * Limit: the array holds the partials of a 296-CTA decode grid (148 SMs x 2,
+ * a B200) at head_dim <= 128 and up to 16 query heads per KV head, 4.9 MB per
+ * device; a pool whose grid needs more gets VW_ERR_UNSUPPORTED and should use
+ * vw_paged_decode.  The first call on each device looks the array's address
+ * up (cudaGetSymbolAddress); make that first call before any stream capture.
+ * There is one array per device, shared by every pool on it: calls on one
+ * stream are ordered and safe, but two calls whose kernels can run at the same
+ * time (different streams, or different pools on the same device) race. */
+VW_API int32_t vw_paged_decode_static(vw_pool* pool, const vw_decode_args* args, void* stream);
+
 /* Copy-on-write block copy / compaction move (no reference counterpart; the
  * decision point is the ref-count in engine/kv_cache.bm:94-113).  pairs:
  * device [num_pairs][2] uint32 (src, dst); every layer's K, V and scales of

@@ -79,6 +79,7 @@ SIGNATURES = {
     "vw_pool_check": (i32, [vp, ctypes.POINTER(u32)]),
     "vw_kv_append": (i32, [vp, u32, vp, vp, vp, u32, vp]),
     "vw_paged_decode": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
+    "vw_paged_decode_static": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
     "vw_block_copy": (i32, [vp, vp, u32, vp]),
     "vw_kv_gather": (i32, [vp, u32, vp, u32, vp, vp, vp, vp, vp]),
     "vw_decode_step_host": (i32, [vp, ctypes.POINTER(StepHostArgs), vp]),

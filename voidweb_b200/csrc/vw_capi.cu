@@ -590,3 +590,112 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ static scratch
+//
+// vw_paged_decode_static: the decode of vw_paged_decode with its split-K
+// partials in a fixed array compiled into this library instead of the pool's
+// scratch.  The array is sized for the decode grid of a B200 (148 SMs x 2 CTAs
+// = 296 CTAs), head_dim up to 128 and up to 16 query heads per KV head:
+// 296 * 2 * 16 * 128 f32 of partial outputs (4.85 MB) plus 296 * 2 * 16 * 2
+// f32 of (max, sum) (74 KB), one copy per device.  A launch whose grid needs
+// more is rejected.  The decode writes every partial that its combine grid
+// reads within the same call, so nothing in the array has to start at zero.
+
+namespace {
+
+constexpr size_t kStaticCtas = 296;
+constexpr size_t kStaticFloatsO = kStaticCtas * 2 * 16 * 128;
+constexpr size_t kStaticFloatsMl = kStaticCtas * 2 * 16 * 2;
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) float g_static_part_o[kStaticFloatsO];
+static __device__ __align__(256) float g_static_part_ml[kStaticFloatsMl];
+
+struct StaticScratch {
+    float* o = nullptr;
+    float* ml = nullptr;
+};
+
+// Device addresses of the two arrays, looked up once per device with that
+// device current (the caller's DeviceScope).
+int32_t static_scratch(int dev, StaticScratch* out) {
+    static std::mutex mu;
+    static StaticScratch addr[kStaticMaxDevices];
+    static bool ready[kStaticMaxDevices] = {};
+    if (dev < 0 || dev >= kStaticMaxDevices)
+        return fail(VW_ERR_UNSUPPORTED, "vw_paged_decode_static: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[dev]) {
+        void* po = nullptr;
+        void* pml = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&po, g_static_part_o);
+        if (e != cudaSuccess) return cuda_fail(e, "vw_paged_decode_static: cudaGetSymbolAddress (o)");
+        e = cudaGetSymbolAddress(&pml, g_static_part_ml);
+        if (e != cudaSuccess) return cuda_fail(e, "vw_paged_decode_static: cudaGetSymbolAddress (ml)");
+        addr[dev].o = static_cast<float*>(po);
+        addr[dev].ml = static_cast<float*>(pml);
+        ready[dev] = true;
+    }
+    *out = addr[dev];
+    return VW_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t vw_paged_decode_static(vw_pool* pool, const vw_decode_args* a, void* stream) {
+    int32_t rc = decode_validate(pool, a);
+    if (rc != VW_OK) return rc;
+    const PoolGeom& g = pool->geom;
+    const size_t need_o = decode_scratch_floats_o(pool->grid, g.head_dim);
+    const size_t need_ml = decode_scratch_floats_ml(pool->grid);
+    if (need_o > kStaticFloatsO || need_ml > kStaticFloatsMl)
+        return fail(VW_ERR_UNSUPPORTED,
+                    "vw_paged_decode_static: a %d-CTA decode grid at head_dim %u needs %zu + %zu "
+                    "floats of split-K scratch; the static array holds %zu + %zu (%zu CTAs at "
+                    "head_dim 128); use vw_paged_decode",
+                    pool->grid, g.head_dim, need_o, need_ml, kStaticFloatsO, kStaticFloatsMl,
+                    kStaticCtas);
+    if (a->num_seqs == 0) return VW_OK;
+    DeviceScope ds(pool->cfg.device);
+    if (!ds.ok) return fail(VW_ERR_CUDA, "vw_paged_decode_static: cannot select device %d", pool->cfg.device);
+    StaticScratch sc;
+    rc = static_scratch(pool->cfg.device, &sc);
+    if (rc != VW_OK) return rc;
+    DecodeLaunch L{};
+    DecodeParams& p = L.p;
+    p.q = a->q;
+    p.out = a->out;
+    p.k_new = a->k_new;
+    p.v_new = a->v_new;
+    p.block_tables = a->block_tables;
+    p.seq_lens = a->seq_lens;
+    p.kv_data = pool->data;
+    p.kv_scales = pool->scales;
+    p.part_o = sc.o;
+    p.part_ml = sc.ml;
+    p.flags = a->flags;
+    p.err = pool->err;
+    p.B = a->num_seqs;
+    p.Hq = a->num_q_heads;
+    p.Hkv = g.num_kv_heads;
+    p.group = a->num_q_heads / g.num_kv_heads;
+    p.num_blocks = g.num_blocks;
+    p.layer = a->layer;
+    p.bt_stride = a->block_table_stride;
+    p.fp8_ocp = g.fp8_ocp;
+    const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    L.tmap = &pool->tmap;
+    L.head_dim = g.head_dim;
+    L.kv_kind = g.kv_kind;
+    L.io_kind = g.io_kind;
+    L.grid = pool->grid;
+    L.stream = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_paged_decode(L);
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_paged_decode_static launch");
+}
+
+}  // extern "C"
