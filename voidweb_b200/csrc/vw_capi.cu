@@ -126,15 +126,19 @@ int32_t encode_pool_map(vw_pool* p) {
     const PoolGeom& g = p->geom;
     const uint64_t eb = elem_bytes(g.kv_kind);
     const uint64_t row = (uint64_t)g.head_dim * eb;
-    // 2-D view of the pool: rows of head_dim elements; one box = the 32 rows of a
-    // page-head (K rows then V rows) by 128 bytes, 128-B swizzled in smem
+    // View of the pool as 128-B columns of token rows: dimension 0 = the 128 bytes
+    // of one column, 1 = token rows (stride one row), 2 = the row's columns
+    // (stride 128 B; present when a row is 256 B).  One box = a whole page-head,
+    // its 32 rows (K rows then V rows) of every column, landing in smem as
+    // [column][32 rows][128 B] with the 128-B swizzle.
     const uint64_t rows = (uint64_t)g.num_layers * g.num_blocks * g.num_kv_heads * 32;
-    cuuint64_t dims[2] = {g.head_dim, rows};
-    cuuint64_t strides[1] = {row};
-    cuuint32_t box[2] = {(cuuint32_t)(128 / eb), 32};
-    cuuint32_t estr[2] = {1, 1};
+    const uint32_t cols = (uint32_t)(row / 128);
+    cuuint64_t dims[3] = {128 / eb, rows, cols};
+    cuuint64_t strides[2] = {row, 128};
+    cuuint32_t box[3] = {(cuuint32_t)(128 / eb), 32, cols};
+    cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(&p->tmap, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                    2, p->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    cols > 1 ? 3 : 2, p->data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(VW_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);

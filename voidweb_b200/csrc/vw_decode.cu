@@ -74,8 +74,12 @@ namespace vw {
 // stamps of [start, prologue done, first load issued, first page ready, last
 // load issued, last page done, merges done, exit] and combines done, for the
 // most recent launch; read back with vw_debug_trace().
-__device__ unsigned long long g_vw_trace[1024 * 16];
-#define VW_TRACE(slot, val) (g_vw_trace[blockIdx.x * 16 + (slot)] = (val))
+// Rows [layer & 1][blockIdx.x]: decode CTAs use slots 0-8, combine CTAs
+// 12-14 (start, partials visible, done), so two consecutive layers' decode and
+// combine grids can be read back together.
+__device__ unsigned long long g_vw_trace[2 * 1024 * 16];
+#define VW_TRACE(slot, val) \
+    (g_vw_trace[(((p.layer & 1u) * 1024u) + blockIdx.x) * 16 + (slot)] = (val))
 #else
 #define VW_TRACE(slot, val) ((void)0)
 #endif
@@ -112,9 +116,10 @@ struct Traits {
     static constexpr int CTILE = KV == kFP8 ? 32 * D * 2 : 0;  // f16 page-head per warp
     static constexpr int MERGE = W * G * (D + 2) * 4 + (W + 2) * G * 4;
     static constexpr int QTILE = G * D * 2;
+    static constexpr int QSLOT = QTILE + 2 * D * 2;          // + the new token's K and V rows
     static constexpr int PFX = align_up_c(2 * (kMaxBatchPerLaunch + 1) * 4, 128);
     static constexpr int FIXED = W * CTILE + align_up_c(MERGE, 1024) +
-                                 align_up_c(kQSlots * QTILE, 1024) + PFX + 2048;
+                                 align_up_c(kQSlots * QSLOT, 1024) + PFX + 2048;
     static constexpr int BUDGET = kSmemPerCta - 1024 /* base alignment slack */ -
                                   (SCAL ? 1024 : 0) /* scale ring alignment */;
     // Stage count: as many as fit, rounded down to a multiple of the consumer
@@ -140,12 +145,13 @@ struct Traits {
     static_assert(STAGE % 1024 == 0 && CTILE % 1024 == 0, "1024-B tile alignment");
 };
 
-// Page as the producer publishes it to its issuing lanes: KV head, TMA row of
-// its first K row (negative for an invalid block id: TMA zero-fills), and the
-// segment ordinal and first query row when the page starts a segment of this
-// CTA's range (else qseg = -1).
+// Page as the producer publishes it to its issuing lanes: TMA row of its first
+// K row (negative for an invalid block id: TMA zero-fills), and when the page
+// starts a segment of this CTA's range (else qseg = -1) the segment ordinal,
+// its first query row, and the row b*Hkv+h of the new K/V token when this CTA
+// also holds the segment's last page and appends it (else kvrow = -1).
 struct PageInfo {
-    int h, row0, qseg, qrow;
+    int kvrow, row0, qseg, qrow;
 };
 
 struct Smem {
@@ -156,7 +162,7 @@ struct Smem {
     float* mm;           // [W][G]
     float* ml;           // [W][G]
     float* mf;           // [W][G] warp weights, then [G] max, [G] sum
-    uint8_t* qring;      // [kQSlots][G][D] io dtype
+    uint8_t* qring;      // [kQSlots][QSLOT]: [G][D] query rows, then new K, new V rows (io dtype)
     int* pfx;            // [B+1] exclusive prefix of pages per sequence
     int* nzp;            // [B+1] exclusive prefix of sequences with pages
     PageInfo* pinfo;     // [2][32] producer batches
@@ -179,7 +185,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     s.ml = s.mm + T::W * T::G;
     s.mf = s.ml + T::W * T::G;
     p += align_up_c(T::MERGE, 1024);
-    s.qring = p; p += align_up_c(kQSlots * T::QTILE, 1024);
+    s.qring = p; p += align_up_c(kQSlots * T::QSLOT, 1024);
     s.pfx = reinterpret_cast<int*>(p);
     s.nzp = s.pfx + (kMaxBatchPerLaunch + 1);
     p += T::PFX;
@@ -228,7 +234,7 @@ __device__ __forceinline__ uint16_t f32_to_io(float f) {
 // ------------------------------------------------------------------ producer
 
 struct Resolved {
-    int h, qseg, qrow;
+    int h, qseg, qrow, kvrow;
     uint32_t blk;
     bool live;
 };
@@ -237,7 +243,7 @@ struct Resolved {
 // block id (the block-table load is consumed one batch later).
 __device__ __forceinline__ Resolved resolve_page(const DecodeParams& p, const Smem& sm, int begin,
                                                  int first_ord, int i, int n) {
-    Resolved r{0, -1, -1, 0xFFFFFFFFu, false};
+    Resolved r{0, -1, -1, -1, 0xFFFFFFFFu, false};
     if (i < n) {
         const long long x = (long long)begin + i;
         const int b = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, x);
@@ -250,6 +256,8 @@ __device__ __forceinline__ Resolved resolve_page(const DecodeParams& p, const Sm
         if (i == 0 || pg == 0) {
             r.qseg = sm.nzp[b] * (int)p.Hkv + h - first_ord;
             r.qrow = (int)(b * p.Hq + h * p.group);
+            // the segment's last page is page i + np-1-pg of this range
+            if (p.k_new != nullptr && i + (np - 1 - pg) < n) r.kvrow = (int)(b * p.Hkv + h);
         }
     }
     return r;
@@ -262,12 +270,14 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     const uint32_t Hkv = p.Hkv;
     const uint32_t qbytes = p.group * T::D * 2;
     const uint8_t* qbase = reinterpret_cast<const uint8_t*>(p.q);
+    const uint8_t* kbase = reinterpret_cast<const uint8_t*>(p.k_new);
+    const uint8_t* vbase = reinterpret_cast<const uint8_t*>(p.v_new);
     int segs_issued = 0;                             // highest segment ordinal issued + 1
     bool ok = true;
 
     auto publish = [&](const Resolved& r, int buf) {
         PageInfo pi;
-        pi.h = r.h;
+        pi.kvrow = r.kvrow;
         pi.qseg = r.qseg;
         pi.qrow = r.qrow;
         pi.row0 = -32;
@@ -303,9 +313,12 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
         } else {
             mbar_arrive_expect_tx(&sm.full[s], T::STAGE);
         }
-#pragma unroll
-        for (int c = 0; c < T::CHUNKS; ++c)
-            tma_load_2d(st + c * 4096, tmap, &sm.full[s], c * (128 / T::EB), pi.row0);
+        // one tensor copy per page-head: rows of one 128-B column, then the next
+        // column (the map's third dimension) when a row is 256 B
+        if constexpr (T::CHUNKS == 1)
+            tma_load_2d(st, tmap, &sm.full[s], 0, pi.row0);
+        else
+            tma_load_3d(st, tmap, &sm.full[s], 0, pi.row0, 0);
         return true;
     };
 
@@ -319,10 +332,20 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     const int early_n = (p.flags & kDecodeEarlyPages) ? min(T::S, n) : 0;
     if (lane < kIssuers)
         for (int j = lane; j < early_n; j += kIssuers) issue_page(j, sm.pinfo[j]);
-    if (p.flags & kDecodePdl) {
-        griddep_wait();
-        griddep_launch_dependents();
+    if (early_n > 0) {
+        // warm L2 with the query tiles (and new K/V rows) of the first batch's
+        // segments: the predecessor may still write them, but L2 is where that
+        // write lands, so the bulk copies after the wait find them there anyway
+        const PageInfo pi = sm.pinfo[lane];
+        if (lane < n && pi.qseg >= 0) {
+            bulk_prefetch_l2(qbase + (size_t)pi.qrow * T::D * 2, qbytes);
+            if (pi.kvrow >= 0) {
+                bulk_prefetch_l2(kbase + (size_t)pi.kvrow * T::D * 2, T::D * 2);
+                bulk_prefetch_l2(vbase + (size_t)pi.kvrow * T::D * 2, T::D * 2);
+            }
+        }
     }
+    if (p.flags & kDecodePdl) griddep_wait();
     int buf = 0;
     for (int i0 = 0; i0 < n; i0 += 32) {
         const Resolved nxt = resolve_page(p, sm, begin, first_ord, i0 + 32 + lane, n);
@@ -342,9 +365,16 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&sm.qfull[qs], qbytes);
-                    bulk_load(sm.qring + qs * T::QTILE, qbase + (size_t)pi.qrow * T::D * 2, qbytes,
-                              &sm.qfull[qs]);
+                    uint8_t* slot = sm.qring + qs * T::QSLOT;
+                    const bool nkv = pi.kvrow >= 0;
+                    mbar_arrive_expect_tx(&sm.qfull[qs], qbytes + (nkv ? 4 * T::D : 0));
+                    bulk_load(slot, qbase + (size_t)pi.qrow * T::D * 2, qbytes, &sm.qfull[qs]);
+                    if (nkv) {
+                        bulk_load(slot + T::QTILE, kbase + (size_t)pi.kvrow * T::D * 2, T::D * 2,
+                                  &sm.qfull[qs]);
+                        bulk_load(slot + T::QTILE + T::D * 2, vbase + (size_t)pi.kvrow * T::D * 2,
+                                  T::D * 2, &sm.qfull[qs]);
+                    }
                     segs_issued = k + 1;
                 }
                 if ((j % kIssuers) != lane || ii < early_n) continue;   // another lane's stage
@@ -361,6 +391,9 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
         __syncwarp();
     }
     if (!ok) set_err(p.err, kDevErrTimeout);
+    // every load of this range is issued: let the combine grid launch once all
+    // CTAs got here (consumer warps signal as they finish, below)
+    griddep_launch_dependents();
     // Drain: never leave the CTA while a TMA or bulk load may still write its smem.
     // lane 0 issued every query tile; share its count for the drain below
     segs_issued = __shfl_sync(0xffffffffu, segs_issued, 0);
@@ -378,6 +411,52 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
             }
         }
     }
+}
+
+// Merge of the split-K pieces of one segment (b, h) for query head j and
+// output elements d..d+3: the pieces (o, max, sum) left by decode CTAs
+// c0..c0+n-1 (CTA c0 in slot slot0, the others in slot 0) are weighted by
+// 2^(max_c - max), the online-softmax rule of flash_attention.bm:149-157
+// applied across pieces; up to kCombineBatch pieces per memory round trip.
+constexpr int kCombineBatch = 8;
+
+template <int D, int G, int IO>
+__device__ __forceinline__ void merge_unit(const DecodeParams& p, int b, int h, int j, int d, int c0,
+                                           int n, int slot0, float vfold) {
+    uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
+    const int g = (int)p.group;
+    float M = -INFINITY, Ls = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (int k0 = 0; k0 < n; k0 += kCombineBatch) {
+        float2 ml[kCombineBatch];
+        float4 o[kCombineBatch];
+#pragma unroll
+        for (int k = 0; k < kCombineBatch; ++k) {
+            ml[k] = make_float2(-INFINITY, 0.0f);
+            o[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (k0 + k < n) {
+                const int c = c0 + k0 + k;
+                const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
+                ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (piece * G + j) * 2));
+                o[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + (piece * G + j) * D + d));
+            }
+        }
+        float Mn = M;
+#pragma unroll
+        for (int k = 0; k < kCombineBatch; ++k) Mn = fmaxf(Mn, ml[k].x);
+        const float r = M > -INFINITY ? ex2(M - Mn) : 0.0f;
+        Ls *= r; a0 *= r; a1 *= r; a2 *= r; a3 *= r;
+#pragma unroll
+        for (int k = 0; k < kCombineBatch; ++k) {
+            const float w = ml[k].x > -INFINITY ? ex2(ml[k].x - Mn) : 0.0f;
+            Ls += ml[k].y * w;
+            a0 += o[k].x * w; a1 += o[k].y * w; a2 += o[k].z * w; a3 += o[k].w * w;
+        }
+        M = Mn;
+    }
+    const float r = vfold / Ls;
+    const uint32_t lo = (uint32_t)f32_to_io<IO>(a0 * r) | ((uint32_t)f32_to_io<IO>(a1 * r) << 16);
+    const uint32_t hi = (uint32_t)f32_to_io<IO>(a2 * r) | ((uint32_t)f32_to_io<IO>(a3 * r) << 16);
+    *reinterpret_cast<uint2*>(out + ((size_t)b * p.Hq + (size_t)h * g + j) * D + d) = make_uint2(lo, hi);
 }
 
 // ------------------------------------------------------------------ consumer
@@ -409,24 +488,22 @@ __device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qti
 
 // Write the new token's row (t = valid-1) of one KV head into HBM and into the
 // staged page-head (K at row t, V at row 16+t).  One warp; each lane owns D/32
-// consecutive elements.
+// consecutive elements, given in nkv[kv] (the rows the producer staged with the
+// segment's query tile).
 template <class T>
 __device__ __forceinline__ void append_row(const DecodeParams& p, uint8_t* stage, float* scal,
-                                           int b, int h, uint32_t blk, int t, int lane) {
+                                           int h, uint32_t blk, int t, int lane,
+                                           const uint32_t (&nkv)[2][2]) {
     constexpr int PER = T::D / 32;    // 2 (D=64) or 4 (D=128)
     const bool blk_ok = blk < p.num_blocks;
     if (!blk_ok && lane == 0) set_err(p.err, kDevErrBlockId);
 #pragma unroll
     for (int kv = 0; kv < 2; ++kv) {
-        const uint16_t* src = reinterpret_cast<const uint16_t*>(kv == 0 ? p.k_new : p.v_new) +
-                              ((size_t)b * p.Hkv + h) * T::D + lane * PER;
         // pool row of (layer, block, head, kv, t) in [L][NB][Hkv][2][16]
         const size_t prow = ((((size_t)p.layer * p.num_blocks + blk) * p.Hkv + h) * 2 + kv) * 16 + t;
         const int srow = kv * 16 + t;
         if constexpr (T::KV != kFP8) {
-            uint32_t w[PER / 2];
-#pragma unroll
-            for (int k = 0; k < PER / 2; ++k) w[k] = __ldg(reinterpret_cast<const uint32_t*>(src) + k);
+            const uint32_t* w = nkv[kv];
             uint8_t* gdst = p.kv_data + prow * T::ROW + lane * PER * 2;
             uint8_t* sdst = stage + swz16(srow, lane * PER);
             if constexpr (PER == 4) {
@@ -438,7 +515,7 @@ __device__ __forceinline__ void append_row(const DecodeParams& p, uint8_t* stage
             }
         } else {
             static_assert(T::D == 128, "FP8 pools need head_dim 128");
-            uint2 raw = __ldg(reinterpret_cast<const uint2*>(src));
+            const uint2 raw = make_uint2(nkv[kv][0], nkv[kv][1]);
             float v[4] = {io_to_f32<T::IO>(raw.x & 0xFFFFu), io_to_f32<T::IO>(raw.x >> 16),
                           io_to_f32<T::IO>(raw.y & 0xFFFFu), io_to_f32<T::IO>(raw.y >> 16)};
             float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
@@ -523,6 +600,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
 
         // query tile of this segment (staged by the producer)
         uint32_t qf[T::NT][T::KT][2];
+        uint32_t nkv[2][2] = {{0u, 0u}, {0u, 0u}};
         {
             const int qs = seg_k % kQSlots;
             // every lane waits, then the warp agrees (and reconverges) before the
@@ -532,7 +610,17 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 if (lane == 0) set_err(p.err, kDevErrTimeout);
                 alive = false;
             }
-            load_q<T>(p, sm.qring + qs * T::QTILE, lane, qf);
+            load_q<T>(p, sm.qring + qs * T::QSLOT, lane, qf);
+            if (append && pg0 + cnt == np) {
+                // this range holds the segment's last page: keep the staged new
+                // K/V row pieces of this lane for the append
+                const uint8_t* nrow = sm.qring + qs * T::QSLOT + T::QTILE + lane * (T::D / 32) * 2;
+#pragma unroll
+                for (int kv = 0; kv < 2; ++kv)
+#pragma unroll
+                    for (int k = 0; k < T::D / 64; ++k)
+                        nkv[kv][k] = reinterpret_cast<const uint32_t*>(nrow + kv * T::D * 2)[k];
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.qempty[qs]);
             ++seg_k;
@@ -570,7 +658,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 if (!in_page) valid = 16;
                 if (append && in_page) {
                     const uint32_t blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg);
-                    append_row<T>(p, st, sc, b, h, blk, valid - 1, lane);
+                    append_row<T>(p, st, sc, h, blk, valid - 1, lane, nkv);
                 }
                 if (valid < 16) zero_tail<T>(st, valid, lane);
                 // plain stores into a TMA-filled stage: order them before the stage's
@@ -763,6 +851,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t deadline = globaltimer() + kWaitDeadlineNs;
     if (threadIdx.x == 0) VW_TRACE(0, globaltimer());
+#ifdef VW_DECODE_TRACE
+    if (threadIdx.x == 0) {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        VW_TRACE(9, smid);
+    }
+#endif
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::S; ++s) { mbar_init(&sm.full[s], 1); mbar_init(&sm.empty[s], 1); }
@@ -772,18 +867,14 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         sm.flag[1] = 0;
     }
     // Programmatic dependent launch: without early pages everything waits for
-    // the predecessor before the first global read; each thread lets the next
-    // grid launch only after its own wait, so at most two grids overlap.
+    // the predecessor before the first global read.  The successor, the
+    // combine grid, is released only near the end (each CTA signals
+    // launch_dependents once its last loads are issued): launched at the start,
+    // combine CTAs would sit in their wait on the SMs that free up first, packed
+    // several to an SM, and keep the next layer's decode CTAs off those SMs.
     const bool pdl = (p.flags & kDecodePdl) != 0;
     const bool early = pdl && (p.flags & kDecodeEarlyPages) != 0;
-    if (pdl && !early) {
-        griddep_wait();
-        griddep_launch_dependents();
-    } else if (!pdl) {
-        // the successor is this launch's own combine grid, which waits for the
-        // whole of this grid before it reads anything this grid writes
-        griddep_launch_dependents();
-    }
+    if (pdl && !early) griddep_wait();
     if (warp == kProducerWarp) {
         if (lane == 0) prefetch_tensormap(&tmap);
         // pages per sequence -> exclusive prefixes of pages and of non-empty
@@ -833,17 +924,28 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     } else {
         if (early) {
             griddep_wait();            // q, k_new, v_new may come from the predecessor
-            griddep_launch_dependents();
+            if (threadIdx.x == 0) VW_TRACE(8, globaltimer());
         }
         consumer<T>(p, sm, begin, end, per_cta, deadline);
+        griddep_launch_dependents();
     }
     if (threadIdx.x == 0) VW_TRACE(7, globaltimer());
 }
 
 // ------------------------------------------------------------------ combine
 
-constexpr int kCombineThreads = 256;
-constexpr int kCombineBatch = 8;       // pieces loaded per round trip
+// The combine grid is resident next to the decode grids of this layer and the
+// next one (it launches before the decode grid ends and waits in
+// griddepcontrol.wait), so its CTAs must fit beside two decode CTAs.  The
+// register file is split over the SM's four sub-partitions (16,384 each) and
+// ten 168-register decode warps fill two of them (3 x 5,376 = 16,128), so a
+// combine CTA is a single warp of at most 80 registers (2,560), which fits in a
+// sub-partition holding two decode warps; it also runs with the decode's
+// shared-memory carveout.  CTA (segment, j) merges query head j of the
+// segment, four output elements per lane.
+constexpr int kCombineWarps = 1;
+constexpr int kCombineThreads = kCombineWarps * 32;
+constexpr int kCombineMinBlocks = 25;  // 65,536 / (32 x 25) -> a cap of 80 registers
 
 // Merge of the split-K partials, one CTA per (sequence, KV head) segment.  The
 // CTA recomputes the decode grid's page ranges from seq_lens (same clamping,
@@ -855,14 +957,16 @@ constexpr int kCombineBatch = 8;       // pieces loaded per round trip
 // computed while the decode still runs, the partials are read after
 // griddepcontrol.wait.  Each thread produces four consecutive output elements.
 template <int D, int G, int IO>
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeParams p, int dec_grid,
+__global__ void __launch_bounds__(kCombineThreads, kCombineMinBlocks) combine_kernel(const DecodeParams p, int dec_grid,
                                                                   float vfold) {
     __shared__ int red[kCombineThreads / 32][2];
+    if (threadIdx.x == 0) VW_TRACE(12, globaltimer());
     // the next grid (the following layer's decode) may start its prologue now;
     // it waits for this whole grid before it writes anything this grid reads
     griddep_launch_dependents();
     const int Hkv = (int)p.Hkv;
     const int b = (int)blockIdx.x / Hkv, h = (int)blockIdx.x - b * Hkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     auto pages = [&](int i) {
         const int sl = (int)__ldcg(p.seq_lens + i);
         const int np = (sl + 15) >> 4;
@@ -879,7 +983,6 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodePa
         before += __shfl_xor_sync(0xffffffffu, before, off);
         all += __shfl_xor_sync(0xffffffffu, all, off);
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) { red[warp][0] = before; red[warp][1] = all; }
     __syncthreads();
     before = all = 0;
@@ -897,52 +1000,18 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodePa
     // else in slot 1 (its last segment); every later CTA starts inside it
     const int slot0 = s_begin == c0 * per_cta ? 0 : 1;
     griddep_wait();
+    if (threadIdx.x == 0) VW_TRACE(13, globaltimer());
     const int g = (int)p.group;
     const int n = c1 - c0 + 1;
-    uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
-    for (int u = threadIdx.x; u < g * (D / 4); u += kCombineThreads) {
-        const int j = u / (D / 4), d = (u - j * (D / 4)) * 4;
-        // up to kBatch pieces are loaded at once (one memory round trip); longer
-        // segments continue with a running rescale, batch by batch
-        float M = -INFINITY, Ls = 0.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-        for (int k0 = 0; k0 < n; k0 += kCombineBatch) {
-            float2 ml[kCombineBatch];
-            float4 o[kCombineBatch];
-#pragma unroll
-            for (int k = 0; k < kCombineBatch; ++k) {
-                ml[k] = make_float2(-INFINITY, 0.0f);
-                o[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (k0 + k < n) {
-                    const int c = c0 + k0 + k;
-                    const size_t piece = (size_t)c * 2 + (c == c0 ? slot0 : 0);
-                    ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (piece * G + j) * 2));
-                    o[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + (piece * G + j) * D + d));
-                }
-            }
-            float Mn = M;
-#pragma unroll
-            for (int k = 0; k < kCombineBatch; ++k) Mn = fmaxf(Mn, ml[k].x);
-            const float r = M > -INFINITY ? ex2(M - Mn) : 0.0f;
-            Ls *= r; a0 *= r; a1 *= r; a2 *= r; a3 *= r;
-#pragma unroll
-            for (int k = 0; k < kCombineBatch; ++k) {
-                const float w = ml[k].x > -INFINITY ? ex2(ml[k].x - Mn) : 0.0f;
-                Ls += ml[k].y * w;
-                a0 += o[k].x * w; a1 += o[k].y * w; a2 += o[k].z * w; a3 += o[k].w * w;
-            }
-            M = Mn;
-        }
-        const float r = vfold / Ls;
-        const uint32_t lo = (uint32_t)f32_to_io<IO>(a0 * r) | ((uint32_t)f32_to_io<IO>(a1 * r) << 16);
-        const uint32_t hi = (uint32_t)f32_to_io<IO>(a2 * r) | ((uint32_t)f32_to_io<IO>(a3 * r) << 16);
-        *reinterpret_cast<uint2*>(out + ((size_t)b * p.Hq + (size_t)h * g + j) * D + d) = make_uint2(lo, hi);
-    }
+    const int j = (int)blockIdx.y * kCombineWarps + warp, d = lane * 4;
+    if (j < g && d < D) merge_unit<D, G, IO>(p, b, h, j, d, c0, n, slot0, vfold);
+    if (threadIdx.x == 0) VW_TRACE(14, globaltimer());
 }
 
 template <class T>
 cudaError_t launch_combine(const DecodeLaunch& L) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(L.p.B * L.p.Hkv);
+    cfg.gridDim = dim3(L.p.B * L.p.Hkv, (L.p.group + kCombineWarps - 1) / kCombineWarps);
     cfg.blockDim = dim3(kCombineThreads);
     cfg.stream = L.stream;
     cudaLaunchAttribute attr[1];
@@ -963,6 +1032,13 @@ cudaError_t launch_t(const DecodeLaunch& L) {
     if (!(configured.load() & bit)) {
         cudaError_t e = cudaFuncSetAttribute(decode_kernel<T>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(combine_kernel<T::D, T::G, T::IO>,
+                                     cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
@@ -999,7 +1075,7 @@ size_t decode_scratch_floats_ml(int grid) { return (size_t)grid * 2 * 16 * 2; }
 extern "C" __attribute__((visibility("default"))) int vw_debug_trace(void* host, int reset) {
     cudaMemcpyFromSymbol(host, g_vw_trace, sizeof(g_vw_trace));
     if (reset) {
-        static unsigned long long zeros[1024 * 16];
+        static unsigned long long zeros[2 * 1024 * 16];
         cudaMemcpyToSymbol(g_vw_trace, zeros, sizeof(zeros));
     }
     return (int)cudaGetLastError();
