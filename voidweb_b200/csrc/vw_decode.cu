@@ -137,6 +137,11 @@ struct Traits {
     // FP8: probabilities carry the V scale but not the 1/256 of the f16 code
     // expansion; the output is multiplied back by 256
     static constexpr float VFOLD = KV == kFP8 ? 256.0f : 1.0f;
+    // Register budget: the f16/bf16 kernels with one query-head tile fit in 128
+    // registers (the bound of 3 CTAs' worth of threads), which leaves every SM
+    // sub-partition room for the single-warp combine CTAs that wait beside the
+    // decode CTAs; the others keep 168 (2 CTAs' worth) to avoid spills.
+    static constexpr int MIN_CTAS = (NT == 1 && KV != kFP8) ? 3 : 2;
     static_assert(CHUNKS >= 1, "row must be at least 128 bytes");
     static_assert(S >= 4, "too few pipeline stages");
     static_assert(S % W == 0 && S % kIssuers == 0, "stage ownership needs S % W == S % issuers == 0");
@@ -218,6 +223,51 @@ __device__ __forceinline__ int find_seq(const int* pfx, int B, int Hkv, long lon
         if ((long long)Hkv * pfx[mid] <= x) lo = mid; else hi = mid - 1;
     }
     return lo;
+}
+
+// Page ranges of the decode CTAs.  The (sequence b, KV head h) segments,
+// ordered by (b, h), lie end to end.  A CTA that crosses a segment boundary
+// pays for a second query tile, a merge of its warps' states and a partial
+// write, and it is the one that finishes last; so each segment is followed by
+// a gap of kSegmentCost virtual pages and the virtual line is cut into equal
+// lengths vper.  12 was the best gap in a sweep of 0-20 on the Qwen2.5-7B
+// batch-16 decode (30 pages per CTA).  Page x of the segment with ordinal k
+// (among segments with pages) sits at v(x) = x + kSegmentCost * k; CTA c takes
+// the pages whose v falls in [c * vper, (c + 1) * vper), so the CTA holding
+// page x is v(x) / vper.  With kSegmentCost = 0 this is the plain equal split.
+#ifndef VW_SEGMENT_COST
+#define VW_SEGMENT_COST 12
+#endif
+constexpr int kSegmentCost = VW_SEGMENT_COST;
+
+// Virtual positions stay far below 2^31: a launch covers fewer than 2^26 pages
+// (the pool's rows are checked against 2^31 at creation) plus kSegmentCost per
+// segment.
+__host__ __device__ __forceinline__ int virtual_total(int total_pages, int segments) {
+    return total_pages + kSegmentCost * segments;
+}
+__host__ __device__ __forceinline__ int virtual_per_cta(int vtotal, int grid) {
+    const int v = (vtotal + grid - 1) / grid;
+    return v < kMinPagesPerCta ? kMinPagesPerCta : v;
+}
+
+// First page x with v(x) >= t (total when there is none), from the exclusive
+// prefixes of pages (pfx) and of sequences with pages (nzp) over B sequences.
+__device__ __forceinline__ int range_start(const int* pfx, const int* nzp, int B, int Hkv, int t) {
+    const int total = Hkv * pfx[B];
+    if (t >= virtual_total(total, Hkv * nzp[B])) return total;
+    // largest b whose first virtual position is <= t (always a sequence with pages)
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (virtual_total(Hkv * pfx[mid], Hkv * nzp[mid]) <= t) lo = mid; else hi = mid - 1;
+    }
+    const int np = pfx[lo + 1] - pfx[lo];
+    const int r = t - virtual_total(Hkv * pfx[lo], Hkv * nzp[lo]);
+    const int h = r / (np + kSegmentCost);
+    const int off = r - h * (np + kSegmentCost);
+    // inside the gap after segment h: the range starts at the next segment
+    return Hkv * pfx[lo] + h * np + (off < np ? off : np);
 }
 
 __device__ __forceinline__ void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
@@ -322,9 +372,11 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
         return true;
     };
 
+    if (lane == 0) VW_TRACE(10, globaltimer());
     Resolved cur = resolve_page(p, sm, begin, first_ord, lane, n);
     publish(cur, 0);
     __syncwarp();
+    if (lane == 0) VW_TRACE(11, globaltimer());
     // Early pages: the first S pages fill every stage once and need no empty
     // wait.  With kDecodeEarlyPages they are issued before the predecessor
     // grid has finished (the caller vouches that it writes neither the tables
@@ -567,7 +619,7 @@ __device__ __forceinline__ void dequant_page(const uint8_t* stage, uint8_t* ctil
 }
 
 template <class T>
-__device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int end, int per_cta,
+__device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int end,
                          uint64_t deadline) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ctid = threadIdx.x;                     // 0 .. W*32-1
@@ -842,7 +894,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
 }
 
 template <class T>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+__global__ void __launch_bounds__(kThreads, T::MIN_CTAS)
 decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -908,13 +960,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     if (threadIdx.x == 0) VW_TRACE(1, globaltimer());
 
     const int total = (int)p.Hkv * sm.pfx[p.B];
-    int per_cta = (total + (int)gridDim.x - 1) / (int)gridDim.x;
-    if (per_cta < kMinPagesPerCta) per_cta = kMinPagesPerCta;
-    const int begin = (int)blockIdx.x * per_cta;
-    const int end = min(total, begin + per_cta);
+    const int vper = virtual_per_cta(virtual_total(total, (int)p.Hkv * sm.nzp[p.B]), (int)gridDim.x);
+    const int begin = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, (int)blockIdx.x * vper);
+    const int end = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, ((int)blockIdx.x + 1) * vper);
     if (begin >= end) return;
 
     if (warp == kProducerWarp) {
+        if (lane == 0) VW_TRACE(15, globaltimer());
         // ordinal of the first segment of this range among non-empty segments
         const int b0 = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, begin);
         const int h0 = (begin - (int)p.Hkv * sm.pfx[b0]) / (sm.pfx[b0 + 1] - sm.pfx[b0]);
@@ -926,7 +978,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
             griddep_wait();            // q, k_new, v_new may come from the predecessor
             if (threadIdx.x == 0) VW_TRACE(8, globaltimer());
         }
-        consumer<T>(p, sm, begin, end, per_cta, deadline);
+        consumer<T>(p, sm, begin, end, deadline);
         griddep_launch_dependents();
     }
     if (threadIdx.x == 0) VW_TRACE(7, globaltimer());
@@ -937,11 +989,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
 // The combine grid is resident next to the decode grids of this layer and the
 // next one (it launches before the decode grid ends and waits in
 // griddepcontrol.wait), so its CTAs must fit beside two decode CTAs.  The
-// register file is split over the SM's four sub-partitions (16,384 each) and
-// ten 168-register decode warps fill two of them (3 x 5,376 = 16,128), so a
-// combine CTA is a single warp of at most 80 registers (2,560), which fits in a
-// sub-partition holding two decode warps; it also runs with the decode's
-// shared-memory carveout.  CTA (segment, j) merges query head j of the
+// register file is split over the SM's four sub-partitions (16,384 each); ten
+// 128-register decode warps leave 4,096 in a sub-partition holding three of
+// them, so a combine CTA is a single warp of at most 80 registers (2,560),
+// and it runs with the decode's shared-memory carveout.  CTA (segment, j) merges query head j of the
 // segment, four output elements per lane.
 constexpr int kCombineWarps = 1;
 constexpr int kCombineThreads = kCombineWarps * 32;
@@ -959,7 +1010,7 @@ constexpr int kCombineMinBlocks = 25;  // 65,536 / (32 x 25) -> a cap of 80 regi
 template <int D, int G, int IO>
 __global__ void __launch_bounds__(kCombineThreads, kCombineMinBlocks) combine_kernel(const DecodeParams p, int dec_grid,
                                                                   float vfold) {
-    __shared__ int red[kCombineThreads / 32][2];
+    __shared__ int red[kCombineThreads / 32][4];
     if (threadIdx.x == 0) VW_TRACE(12, globaltimer());
     // the next grid (the following layer's decode) may start its prologue now;
     // it waits for this whole grid before it writes anything this grid reads
@@ -972,33 +1023,40 @@ __global__ void __launch_bounds__(kCombineThreads, kCombineMinBlocks) combine_ke
         const int np = (sl + 15) >> 4;
         return sl <= 0 ? 0 : min(np, (int)p.bt_stride);
     };
-    int before = 0, all = 0;
+    // pages and sequences with pages, before b and in all (the decode's prefixes)
+    int before = 0, all = 0, nz_before = 0, nz_all = 0;
     for (int i = threadIdx.x; i < (int)p.B; i += kCombineThreads) {
         const int np = pages(i);
         all += np;
-        if (i < b) before += np;
+        nz_all += np > 0;
+        if (i < b) { before += np; nz_before += np > 0; }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         before += __shfl_xor_sync(0xffffffffu, before, off);
         all += __shfl_xor_sync(0xffffffffu, all, off);
+        nz_before += __shfl_xor_sync(0xffffffffu, nz_before, off);
+        nz_all += __shfl_xor_sync(0xffffffffu, nz_all, off);
     }
-    if (lane == 0) { red[warp][0] = before; red[warp][1] = all; }
+    if (lane == 0) { red[warp][0] = before; red[warp][1] = all; red[warp][2] = nz_before; red[warp][3] = nz_all; }
     __syncthreads();
-    before = all = 0;
+    before = all = nz_before = nz_all = 0;
 #pragma unroll
-    for (int w = 0; w < kCombineThreads / 32; ++w) { before += red[w][0]; all += red[w][1]; }
+    for (int w = 0; w < kCombineThreads / 32; ++w) {
+        before += red[w][0]; all += red[w][1]; nz_before += red[w][2]; nz_all += red[w][3];
+    }
     const int np = pages(b);
     if (np == 0) return;
-    const int total = Hkv * all;
-    int per_cta = (total + dec_grid - 1) / dec_grid;
-    if (per_cta < kMinPagesPerCta) per_cta = kMinPagesPerCta;
+    const int vper = virtual_per_cta(virtual_total(Hkv * all, Hkv * nz_all), dec_grid);
     const int s_begin = Hkv * before + h * np;
-    const int c0 = s_begin / per_cta, c1 = (s_begin + np - 1) / per_cta;
+    const int k = Hkv * nz_before + h;        // segment ordinal
+    const int v0 = s_begin + kSegmentCost * k;
+    const int c0 = v0 / vper, c1 = (v0 + np - 1) / vper;
     if (c0 == c1) return;                      // written out by the decode CTA itself
-    // CTA c0 holds this segment in slot 0 when the segment starts its range,
-    // else in slot 1 (its last segment); every later CTA starts inside it
-    const int slot0 = s_begin == c0 * per_cta ? 0 : 1;
+    // CTA c0 holds this segment in slot 0 when the segment starts its range
+    // (the page before it, of segment k-1, lies in an earlier CTA), else in
+    // slot 1 (its last segment); every later CTA starts inside it
+    const int slot0 = (k == 0 || (s_begin - 1) + kSegmentCost * (k - 1) < c0 * vper) ? 0 : 1;
     griddep_wait();
     if (threadIdx.x == 0) VW_TRACE(13, globaltimer());
     const int g = (int)p.group;
