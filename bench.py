@@ -69,6 +69,12 @@ def algorithmic_bytes_per_launch(w, seq_lens):
     return int(per.sum())
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch of the
+# default workload, from one ncu --set full capture of that launch; ncu cannot
+# run inside the timed bench, so the figure is carried here.
+NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 70_964_480}
+
+
 def hbm_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -471,7 +477,8 @@ def main():
             "tok_per_s": round(tok_s, 1),
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
                          "peak_kind": peak_kind, "launch_us_in_region": round(launch_us, 3),
                          "kernel_us_event_median": round(kernel_us, 3),
                          "kernel_only_frac": round(bytes_launch / (kernel_us * 1e-6) / 1e9 / peak, 4),
