@@ -113,7 +113,11 @@ struct Traits {
     static constexpr bool MMA_BF16 = KV == kBF16;            // FP8 pages compute in f16
     static constexpr int KT = D / 16;                        // k-steps of Q K^T
     static constexpr int MT = D / 16;                        // d-tiles of V^T P^T
-    static constexpr int CTILE = KV == kFP8 ? 32 * D * 2 : 0;  // f16 page-head per warp
+    // FP8: per-warp f16 tile of half a page-head (16 rows: K, then V), laid out
+    // [2 columns][16 rows][128 B]; 2-byte pages are read in place from the stage
+    static constexpr int CTILE = KV == kFP8 ? 16 * D * 2 : 0;
+    static constexpr int TCOL = KV == kFP8 ? 2048 : 4096;    // column stride of the MMA tile
+    static constexpr int VROW = KV == kFP8 ? 0 : 16;         // first V row in the MMA tile
     static constexpr int MERGE = W * G * (D + 2) * 4 + (W + 2) * G * 4;
     static constexpr int QTILE = G * D * 2;
     static constexpr int QSLOT = QTILE + 2 * D * 2;          // + the new token's K and V rows
@@ -600,21 +604,25 @@ __device__ __forceinline__ void zero_tail(uint8_t* stage, int valid, int lane) {
     }
 }
 
-// FP8: expand the staged page-head of codes [32 rows][128 B] into this warp's
-// f16 tile [2][32 rows][128 B] (same swizzled layout as a 2-byte stage).
+// FP8: expand rows row0..row0+15 of the staged page-head of codes [32 rows]
+// [128 B] (K: row0 = 0, V: row0 = 16) into this warp's f16 tile [2 columns]
+// [16 rows][128 B], 128-B swizzled like a 2-byte stage.
 template <class T>
-__device__ __forceinline__ void dequant_page(const uint8_t* stage, uint8_t* ctile, int lane) {
+__device__ __forceinline__ void dequant_half(const uint8_t* stage, uint8_t* ctile, int row0, int lane) {
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int row = it * 4 + (lane >> 3), c16 = lane & 7;
+    for (int it = 0; it < 4; ++it) {
+        const int r = it * 4 + (lane >> 3), row = row0 + r, c16 = lane & 7;
         const uint4 w = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c16 ^ (row & 7)) << 4));
         uint4 lo, hi;
         lo.x = fp8x2_to_f16x2_scaled(w.x, 0); lo.y = fp8x2_to_f16x2_scaled(w.x, 1);
         lo.z = fp8x2_to_f16x2_scaled(w.y, 0); lo.w = fp8x2_to_f16x2_scaled(w.y, 1);
         hi.x = fp8x2_to_f16x2_scaled(w.z, 0); hi.y = fp8x2_to_f16x2_scaled(w.z, 1);
         hi.z = fp8x2_to_f16x2_scaled(w.w, 0); hi.w = fp8x2_to_f16x2_scaled(w.w, 1);
-        *reinterpret_cast<uint4*>(ctile + swz16(row, c16 * 16)) = lo;
-        *reinterpret_cast<uint4*>(ctile + swz16(row, c16 * 16 + 8)) = hi;
+        // codes c16*16 .. +15 are f16 elements of column c16/4, 16-B units 2*(c16%4), +1
+        uint8_t* base = ctile + (c16 >> 2) * 2048 + r * 128;
+        const int u = (c16 & 3) * 2;
+        *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4*>(base + (((u + 1) ^ (r & 7)) << 4)) = hi;
     }
 }
 
@@ -723,9 +731,8 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             if constexpr (T::KV == kFP8) {
                 ks0 = sc[t0] * 256.0f; ks1 = sc[t1] * 256.0f;
                 vs0 = sc[16 + t0]; vs1 = sc[16 + t1];
-                dequant_page<T>(st, my_ctile, lane);
+                dequant_half<T>(st, my_ctile, 0, lane);      // K rows
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.empty[s]);   // stage no longer needed
                 tbase = smem_u32(my_ctile);
             } else {
                 tbase = smem_u32(st);
@@ -740,7 +747,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
 #pragma unroll
             for (int kt = 0; kt < T::KT; ++kt) {
                 uint32_t a0, a1, a2, a3;
-                const uint32_t addr = tbase + (kt >> 2) * 4096 + k_tok * 128 +
+                const uint32_t addr = tbase + (kt >> 2) * T::TCOL + k_tok * 128 +
                                       ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4);
                 ldsm_x4(addr, a0, a1, a2, a3);
 #pragma unroll
@@ -748,6 +755,14 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                     if (kt & 1) mma_16816<T::MMA_BF16>(sb[nt], a0, a1, a2, a3, qf[nt][kt][0], qf[nt][kt][1]);
                     else mma_16816<T::MMA_BF16>(sa[nt], a0, a1, a2, a3, qf[nt][kt][0], qf[nt][kt][1]);
                 }
+            }
+
+            if constexpr (T::KV == kFP8) {
+                // the K half is in registers now: expand the V half into the tile
+                __syncwarp();
+                dequant_half<T>(st, my_ctile, 16, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.empty[s]);   // stage no longer needed
             }
 
             // ---- online softmax (log2 domain) with a lazily raised maximum
@@ -799,11 +814,11 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 pb[nt][1] = movmatrix_t(pack2<T::MMA_BF16>(q10, q11));
             }
 
-            // ---- O^T += V^T P^T  (D x 8*NT); V rows are 16..31 of the tile
+            // ---- O^T += V^T P^T  (D x 8*NT); V rows start at row VROW of the tile
 #pragma unroll
             for (int mt = 0; mt < T::MT; ++mt) {
                 uint32_t a0, a1, a2, a3;
-                const uint32_t addr = tbase + (mt >> 2) * 4096 + (16 + v_tok) * 128 +
+                const uint32_t addr = tbase + (mt >> 2) * T::TCOL + (T::VROW + v_tok) * 128 +
                                       ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4);
                 ldsm_x4_t(addr, a0, a1, a2, a3);
 #pragma unroll
