@@ -119,8 +119,9 @@ typedef struct {
 
 /* Launch as a programmatic dependent of the previous kernel on the stream: the
  * kernel may start while its predecessor drains and waits for it before
- * reading q, k_new, v_new (and, without VW_DECODE_EARLY_PAGES, anything).  At
- * most two consecutive decode launches of a pool overlap. */
+ * reading q, k_new, v_new (and, without VW_DECODE_EARLY_PAGES, anything).
+ * Each call is a decode grid followed by a small combine grid on the same
+ * stream; consecutive calls on one stream may overlap and stay correct. */
 #define VW_DECODE_PDL 0x1u
 /* With VW_DECODE_PDL: the caller guarantees that the preceding kernel writes
  * neither the block tables, nor seq_lens, nor this layer's pages, so the
@@ -130,8 +131,9 @@ typedef struct {
 /* Replaces: launch_paged_attn_decode (kernels/attention/flash_attention.bm:180-189,
  * kernel :113-162), generalised to GQA and split-K; with k_new/v_new set it is
  * also the append of the step's token (one launch per layer).  Device pointers;
- * all of them 16-byte aligned.  One decode at a time per pool (its split-K
- * scratch is shared). */
+ * all of them 16-byte aligned.  Calls on one stream are ordered; calls of one
+ * pool on different streams must not run at the same time (they share the
+ * pool's split-K scratch). */
 VW_API int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream);
 
 /* vw_paged_decode with its split-K scratch in a fixed array compiled into this

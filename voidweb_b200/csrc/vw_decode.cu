@@ -447,9 +447,6 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
         __syncwarp();
     }
     if (!ok) set_err(p.err, kDevErrTimeout);
-    // every load of this range is issued: let the combine grid launch once all
-    // CTAs got here (consumer warps signal as they finish, below)
-    griddep_launch_dependents();
     // Drain: never leave the CTA while a TMA or bulk load may still write its smem.
     // lane 0 issued every query tile; share its count for the drain below
     segs_issued = __shfl_sync(0xffffffffu, segs_issued, 0);
@@ -934,14 +931,18 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         sm.flag[1] = 0;
     }
     // Programmatic dependent launch: without early pages everything waits for
-    // the predecessor before the first global read.  The successor, the
-    // combine grid, is released only near the end (each CTA signals
-    // launch_dependents once its last loads are issued): launched at the start,
-    // combine CTAs would sit in their wait on the SMs that free up first, packed
-    // several to an SM, and keep the next layer's decode CTAs off those SMs.
+    // the predecessor before the first global read.  The successor, this
+    // launch's combine grid, may launch at once: its single-warp CTAs wait in
+    // griddepcontrol.wait and fit beside two decode CTAs, and its own early
+    // signal lets the next layer's decode launch and stream its first pages
+    // while this grid drains.  Three grids can be in flight (this decode, its
+    // combine, the next decode); the next decode writes partials only after
+    // its own wait, when this grid and its combine are complete, so two
+    // alternating partial sets suffice.
     const bool pdl = (p.flags & kDecodePdl) != 0;
     const bool early = pdl && (p.flags & kDecodeEarlyPages) != 0;
     if (pdl && !early) griddep_wait();
+    griddep_launch_dependents();
     if (warp == kProducerWarp) {
         if (lane == 0) prefetch_tensormap(&tmap);
         // pages per sequence -> exclusive prefixes of pages and of non-empty
@@ -994,7 +995,6 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
             if (threadIdx.x == 0) VW_TRACE(8, globaltimer());
         }
         consumer<T>(p, sm, begin, end, deadline);
-        griddep_launch_dependents();
     }
     if (threadIdx.x == 0) VW_TRACE(7, globaltimer());
 }
