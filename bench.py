@@ -322,7 +322,10 @@ def main():
     q = torch.randn((L, B, Hq, D), device=dev, generator=gen, dtype=torch.float32).to(iod)
     kn = torch.randn((L, B, Hkv, D), device=dev, generator=gen, dtype=torch.float32).to(iod)
     vn = torch.randn((L, B, Hkv, D), device=dev, generator=gen, dtype=torch.float32).to(iod)
-    out = torch.zeros((L, B, Hq, D), device=dev, dtype=iod)
+    # two output buffers: with N GPUs the all-gather of one step's outputs runs on
+    # a side stream while the next step writes the other buffer
+    outs = [torch.zeros((L, B, Hq, D), device=dev, dtype=iod) for _ in range(2)]
+    out = outs[0]
     bt_d = torch.from_numpy(bt).to(dev)
     sl_d = torch.from_numpy(seq_lens.astype(np.int32)).to(dev)
     torch.cuda.synchronize()
@@ -334,29 +337,53 @@ def main():
     # stream its pages early (the previous launch writes only its own layer)
     flags = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
 
-    def step(s):
+    def step(s, o):
         for layer in range(L):
-            pool.paged_decode(layer, q[layer], bt_d, sl_d, out[layer], k_new=kn[layer],
+            pool.paged_decode(layer, q[layer], bt_d, sl_d, o[layer], k_new=kn[layer],
                               v_new=vn[layer], stream=s, flags=flags)
 
     # first launches outside capture (per-device kernel attribute set-up)
     with torch.cuda.stream(stream):
-        step(stream)
+        step(stream, outs[0])
     stream.synchronize()
     assert pool.check() == 0, "device bounds check tripped"
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step(torch.cuda.current_stream())
-    gathered = torch.empty((world, L, B, Hq, D), device=dev, dtype=iod) if world > 1 else None
+    graphs = []
+    for o in outs:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(torch.cuda.current_stream(), o)
+        graphs.append(g)
+    gathered = [torch.empty((world, L, B, Hq, D), device=dev, dtype=iod) for _ in range(2)] \
+        if world > 1 else None
+    gather_stream = torch.cuda.Stream(device=dev) if world > 1 else None
+    gather_done = [torch.cuda.Event(), torch.cuda.Event()]
+    pending = [False, False]
+    step_no = [0]
 
     def run_step():
-        graph.replay()
+        i = step_no[0] % 2
+        step_no[0] += 1
+        if pending[i]:
+            stream.wait_event(gather_done[i])    # the gather reading outs[i] has finished
+        graphs[i].replay()
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            ready = torch.cuda.Event()
+            ready.record(stream)
+            gather_stream.wait_event(ready)
+            with torch.cuda.stream(gather_stream):
+                dist.all_gather_into_tensor(gathered[i], outs[i])
+            gather_done[i].record(gather_stream)
+            pending[i] = True
+
+    def join_gathers():
+        for i in range(2):
+            if pending[i]:
+                stream.wait_event(gather_done[i])
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             run_step()
+        join_gathers()
     stream.synchronize()
     if world > 1:
         dist.barrier()
@@ -370,6 +397,7 @@ def main():
         t0.record(stream)
         for _ in range(args.steps):
             run_step()
+        join_gathers()                  # every step's gather ends inside the timed region
         t1.record(stream)
     stream.synchronize()
     torch.cuda.synchronize()
@@ -473,7 +501,9 @@ def main():
                        "l2": f"inputs larger than L2 ({bytes_launch * L / 1e9:.2f} GB of KV "
                              f"per step per GPU vs {L2_BYTES / 1e6:.0f} MB L2)",
                        "graph": "one CUDA graph per step: one fused append+decode launch per layer, "
-                                "programmatic dependent launches with early page streaming"},
+                                "programmatic dependent launches with early page streaming",
+                       "gather": (f"NCCL all-gather of each step's outputs on a side stream, overlapping "
+                                  f"the next step (double-buffered outputs)") if world > 1 else None},
             "tok_per_s": round(tok_s, 1),
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
@@ -490,7 +520,7 @@ def main():
             "gpu_launches": args.steps * L * 2,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    del graphs
     pool.close()
     if world > 1:
         dist.barrier()
