@@ -281,6 +281,9 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        # the per-step output all-gather overlaps the next step's decode: two
+        # NCCL channels move 3 MB per rank in time and leave the SMs to the decode
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
