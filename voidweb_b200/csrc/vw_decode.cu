@@ -385,7 +385,8 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     // wait.  With kDecodeEarlyPages they are issued before the predecessor
     // grid has finished (the caller vouches that it writes neither the tables
     // nor these pages); the query tiles wait for it.
-    const int early_n = (p.flags & kDecodeEarlyPages) ? min(T::S, n) : 0;
+    // (at most the first batch: only its 32 page records are published yet)
+    const int early_n = (p.flags & kDecodeEarlyPages) ? min(min(T::S, 32), n) : 0;
     if (lane < kIssuers)
         for (int j = lane; j < early_n; j += kIssuers) issue_page(j, sm.pinfo[j]);
     if (early_n > 0) {
