@@ -128,6 +128,13 @@ typedef struct {
  * kernel starts streaming pages before the predecessor finishes. */
 #define VW_DECODE_EARLY_PAGES 0x2u
 
+/* With a plan (vw_decode_plan) of the same block tables, seq_lens, num_seqs,
+ * stride and query heads: the launch takes its page assignment from the plan
+ * instead of computing it.  With VW_DECODE_EARLY_PAGES the plan is read before
+ * the predecessor finishes, so the predecessor must not be the plan launch
+ * itself (launch the step's first layer without VW_DECODE_EARLY_PAGES). */
+#define VW_DECODE_PLANNED 0x4u
+
 /* Replaces: launch_paged_attn_decode (kernels/attention/flash_attention.bm:180-189,
  * kernel :113-162), generalised to GQA and split-K; with k_new/v_new set it is
  * also the append of the step's token (one launch per layer).  Device pointers;
@@ -135,6 +142,19 @@ typedef struct {
  * pool on different streams must not run at the same time (they share the
  * pool's split-K scratch). */
 VW_API int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream);
+
+/* Page assignment of a decode batch, computed once and reused by every layer's
+ * vw_paged_decode with VW_DECODE_PLANNED (no counterpart in the reference,
+ * whose decode has one CTA per sequence): each decode CTA's range of pages, its
+ * first page records and the batch prefixes, in pool memory.  block_tables and
+ * seq_lens are the device arrays the decodes will pass; their contents must not
+ * change until the next plan.  One plan per pool: a new plan replaces it, in
+ * stream order.  On the 28-layer Qwen2.5-7B batch-16 step the plan launch
+ * costs more than it saves (early page streaming already hides the decode's
+ * own prologue behind the previous layer), so it is an option, not a default. */
+VW_API int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32_t* seq_lens,
+                              uint32_t num_seqs, uint32_t block_table_stride, uint32_t num_q_heads,
+                              void* stream);
 
 /* vw_paged_decode with its split-K scratch in a fixed array compiled into this
  * library instead of in memory the pool allocated.  No counterpart in the

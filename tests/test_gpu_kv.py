@@ -310,11 +310,13 @@ def test_full_size_qwen_layer_sampled(dev):
     pool.close()
 
 
-@pytest.mark.parametrize("graph", [False, True])
-def test_pdl_layer_chain(dev, graph):
+@pytest.mark.parametrize("graph,planned", [(False, False), (True, False), (False, True),
+                                           (True, True)])
+def test_pdl_layer_chain(dev, graph, planned):
     """Consecutive layers launched as programmatic dependents with early page
-    streaming (the flags a decode step uses), eagerly and inside a CUDA graph:
-    every layer's pages and outputs must match the oracle."""
+    streaming (the flags a decode step uses), eagerly and inside a CUDA graph,
+    with and without a decode plan made at the start of the step: every layer's
+    pages and outputs must match the oracle."""
     from voidweb_b200 import _lib as C
     c = kvgen.make_case(41, 6, 2, 128, 14, 9, 20, 2500, BF16, BF16)
     pool = make_pool(c, dev)
@@ -323,11 +325,15 @@ def test_pdl_layer_chain(dev, graph):
     ks = [t16(c.k_new[l], dev) for l in range(c.L)]
     vs = [t16(c.v_new[l], dev) for l in range(c.L)]
     outs = [torch.zeros_like(qs[0]) for _ in range(c.L)]
-    flags = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
+    chain = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
     s = torch.cuda.Stream(device=dev)
 
     def step(stream):
+        if planned:
+            pool.plan(bt, sl, c.Hq, stream=stream)
         for l in range(c.L):
+            # the layer right after the plan launch waits for it in stream order
+            flags = (C.VW_DECODE_PLANNED | (chain if l > 0 else 0)) if planned else chain
             pool.paged_decode(l, qs[l], bt, sl, outs[l], k_new=ks[l], v_new=vs[l],
                               stream=stream, flags=flags)
 
@@ -358,4 +364,26 @@ def test_pdl_layer_chain(dev, graph):
         ref = oracle.paged_decode_f64(c.geom, data, None, l, c.q[l], c.Hq, c.block_tables,
                                       c.seq_lens, 1.0 / np.sqrt(128))
         check_close(outs[l].cpu().numpy().view(np.uint16), ref, BF16, f"layer {l}")
+    pool.close()
+
+
+def test_planned_decode_is_bit_identical(dev):
+    """A planned launch uses the same page split and arithmetic as a plain one:
+    on the split-K extremes batch the outputs match bit for bit."""
+    from voidweb_b200 import _lib as C
+    ctx = [1, 2, 15, 16, 17, 31, 32, 33, 9000, 3, 1, 4097, 64, 5, 12000]
+    c = kvgen.make_case(98, 1, 2, 128, 14, len(ctx), 0, 0, BF16, BF16, ctx=ctx)
+    pool = make_pool(c, dev)
+    q, bt, sl = t16(c.q[0], dev), tu32(c.block_tables, dev), tu32(c.seq_lens, dev)
+    plain, planned = torch.zeros_like(q), torch.zeros_like(q)
+    pool.paged_decode(0, q, bt, sl, plain)
+    pool.plan(bt, sl, c.Hq)
+    pool.paged_decode(0, q, bt, sl, planned, flags=C.VW_DECODE_PLANNED)
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert torch.equal(plain, planned)
+    # a plan of other tables is refused, not used
+    other = bt.clone()
+    with pytest.raises(C.VoidwebError):
+        pool.paged_decode(0, q, other, sl, planned, flags=C.VW_DECODE_PLANNED)
     pool.close()

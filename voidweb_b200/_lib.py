@@ -25,7 +25,7 @@ VW_ERR_DEVICE_CHECK = 5
 
 VW_F16, VW_BF16, VW_FP8_E4M3 = 0, 1, 2
 VW_FP8_REFERENCE, VW_FP8_OCP = 0, 1
-VW_DECODE_PDL, VW_DECODE_EARLY_PAGES = 0x1, 0x2
+VW_DECODE_PDL, VW_DECODE_EARLY_PAGES, VW_DECODE_PLANNED = 0x1, 0x2, 0x4
 
 DEV_ERR_BLOCK_ID, DEV_ERR_SEQ_LEN, DEV_ERR_TIMEOUT, DEV_ERR_SLOT = 1, 2, 4, 8
 
@@ -79,6 +79,7 @@ SIGNATURES = {
     "vw_pool_check": (i32, [vp, ctypes.POINTER(u32)]),
     "vw_kv_append": (i32, [vp, u32, vp, vp, vp, u32, vp]),
     "vw_paged_decode": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
+    "vw_decode_plan": (i32, [vp, vp, vp, u32, u32, u32, vp]),
     "vw_paged_decode_static": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
     "vw_block_copy": (i32, [vp, vp, u32, vp]),
     "vw_kv_gather": (i32, [vp, u32, vp, u32, vp, vp, vp, vp, vp]),

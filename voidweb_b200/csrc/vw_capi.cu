@@ -95,6 +95,12 @@ struct vw_pool {
     // overlapping launches (programmatic dependent launch) never share one
     size_t scratch_o = 0, scratch_ml = 0;
     uint64_t launches = 0;
+    // decode plan (vw_decode_plan) and the batch it was made for
+    int* plan = nullptr;
+    bool plan_ready = false;
+    const void* plan_tables = nullptr;
+    const void* plan_lens = nullptr;
+    uint32_t plan_seqs = 0, plan_stride = 0, plan_q_heads = 0;
     // staging for vw_decode_step_host (grow-only)
     uint8_t* stage = nullptr;
     size_t stage_bytes = 0;
@@ -110,6 +116,7 @@ void pool_free_all(vw_pool* p) {
     if (p->own_scales && p->scales) cudaFree(p->scales);
     if (p->part_o) cudaFree(p->part_o);
     if (p->part_ml) cudaFree(p->part_ml);
+    if (p->plan) cudaFree(p->plan);
     if (p->err) cudaFree(p->err);
     if (p->stage) cudaFree(p->stage);
     if (p->s_h2d) cudaStreamDestroy(p->s_h2d);
@@ -222,6 +229,7 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
     p->scratch_ml = n_ml;
     if ((e = cudaMalloc(&p->part_o, 2 * n_o * 4)) != cudaSuccess ||
         (e = cudaMalloc(&p->part_ml, 2 * n_ml * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&p->plan, plan_ints(p->grid) * 4)) != cudaSuccess ||
         (e = cudaMalloc(&p->err, 4)) != cudaSuccess) {
         pool_free_all(p);
         delete p;
@@ -295,8 +303,15 @@ int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const voi
 static int32_t decode_validate(const vw_pool* pool, const vw_decode_args* a) {
     if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: null argument");
     const PoolGeom& g = pool->geom;
-    if (a->flags & ~(uint32_t)(VW_DECODE_PDL | VW_DECODE_EARLY_PAGES))
+    if (a->flags & ~(uint32_t)(VW_DECODE_PDL | VW_DECODE_EARLY_PAGES | VW_DECODE_PLANNED))
         return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: unknown flags 0x%x", a->flags);
+    if ((a->flags & VW_DECODE_PLANNED) &&
+        (!pool->plan_ready || pool->plan_tables != a->block_tables || pool->plan_lens != a->seq_lens ||
+         pool->plan_seqs != a->num_seqs || pool->plan_stride != a->block_table_stride ||
+         pool->plan_q_heads != a->num_q_heads))
+        return fail(VW_ERR_INVALID_ARG,
+                    "vw_paged_decode: VW_DECODE_PLANNED without a vw_decode_plan of the same "
+                    "block tables, seq_lens, num_seqs, stride and query heads");
     if ((a->flags & VW_DECODE_EARLY_PAGES) && !(a->flags & VW_DECODE_PDL))
         return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: VW_DECODE_EARLY_PAGES needs VW_DECODE_PDL");
     if (a->layer >= g.num_layers)
@@ -340,6 +355,7 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
     p.part_o = pool->part_o + set * pool->scratch_o;
     p.part_ml = pool->part_ml + set * pool->scratch_ml;
     p.flags = a->flags;
+    p.plan = (a->flags & VW_DECODE_PLANNED) ? pool->plan : nullptr;
     p.err = pool->err;
     p.B = a->num_seqs;
     p.Hq = a->num_q_heads;
@@ -368,6 +384,43 @@ int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream)
     if (args->num_seqs == 0) return VW_OK;
     DeviceScope ds(pool->cfg.device);
     return decode_launch(pool, args, static_cast<cudaStream_t>(stream));
+}
+
+int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32_t* seq_lens,
+                       uint32_t num_seqs, uint32_t block_table_stride, uint32_t num_q_heads,
+                       void* stream) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_decode_plan: null pool");
+    const PoolGeom& g = pool->geom;
+    if (num_seqs == 0 || num_seqs > pool->cfg.max_batch)
+        return fail(VW_ERR_INVALID_ARG, "vw_decode_plan: num_seqs %u not in 1..%u", num_seqs,
+                    pool->cfg.max_batch);
+    if (!block_tables || !seq_lens || !aligned(block_tables, 4) || !aligned(seq_lens, 4))
+        return fail(VW_ERR_INVALID_ARG, "vw_decode_plan: bad block_tables / seq_lens pointer");
+    if (block_table_stride == 0)
+        return fail(VW_ERR_INVALID_ARG, "vw_decode_plan: block_table_stride must be > 0");
+    if (num_q_heads == 0 || num_q_heads % g.num_kv_heads != 0 || num_q_heads / g.num_kv_heads > 16)
+        return fail(VW_ERR_INVALID_ARG, "vw_decode_plan: num_q_heads %u does not fit %u KV heads",
+                    num_q_heads, g.num_kv_heads);
+    DeviceScope ds(pool->cfg.device);
+    DecodeParams p{};
+    p.block_tables = block_tables;
+    p.seq_lens = seq_lens;
+    p.err = pool->err;
+    p.B = num_seqs;
+    p.Hq = num_q_heads;
+    p.Hkv = g.num_kv_heads;
+    p.group = num_q_heads / g.num_kv_heads;
+    p.num_blocks = g.num_blocks;
+    p.bt_stride = block_table_stride;
+    cudaError_t e = launch_decode_plan(p, pool->grid, pool->plan, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "vw_decode_plan launch");
+    pool->plan_ready = true;
+    pool->plan_tables = block_tables;
+    pool->plan_lens = seq_lens;
+    pool->plan_seqs = num_seqs;
+    pool->plan_stride = block_table_stride;
+    pool->plan_q_heads = num_q_heads;
+    return VW_OK;
 }
 
 int32_t vw_block_copy(vw_pool* pool, const uint32_t* pairs, uint32_t num_pairs, void* stream) {

@@ -179,7 +179,7 @@ struct Smem {
     uint64_t* empty;     // [S]
     uint64_t* qfull;     // [kQSlots]
     uint64_t* qempty;    // [kQSlots]
-    int* flag;           // [1] abort marker ([0] unused)
+    int* flag;           // [1] abort marker, [2..4] planned begin, end, first ordinal
 };
 
 template <class T>
@@ -275,6 +275,39 @@ __device__ __forceinline__ int range_start(const int* pfx, const int* nzp, int B
 }
 
 __device__ __forceinline__ void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
+
+// Pages per sequence -> exclusive prefixes of pages (pfx) and of sequences with
+// pages (nzp), by one warp, 32 sequences at a time.  A seq_len of 0 gives no
+// pages and one longer than its block-table row is clamped to the row; both
+// are flagged when `report`.
+__device__ __forceinline__ void warp_prefixes(const uint32_t* seq_lens, int B, int bt_stride,
+                                              uint32_t* err, bool report, int* pfx, int* nzp,
+                                              int lane) {
+    int run = 0, run_nz = 0;
+    if (lane == 0) { pfx[0] = 0; nzp[0] = 0; }
+    for (int base_b = 0; base_b < B; base_b += 32) {
+        const int b = base_b + lane;
+        int np = 0;
+        if (b < B) {
+            const int sl = (int)__ldg(seq_lens + b);
+            np = (sl + 15) >> 4;
+            if (sl <= 0 || np > bt_stride) {
+                if (report) set_err(err, kDevErrSeqLen);
+                np = sl <= 0 ? 0 : bt_stride;
+            }
+        }
+        int incl = np, incl_nz = np > 0 ? 1 : 0;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, off);
+            const int vz = __shfl_up_sync(0xffffffffu, incl_nz, off);
+            if (lane >= off) { incl += v; incl_nz += vz; }
+        }
+        if (b < B) { pfx[b + 1] = run + incl; nzp[b + 1] = run_nz + incl_nz; }
+        run += __shfl_sync(0xffffffffu, incl, 31);
+        run_nz += __shfl_sync(0xffffffffu, incl_nz, 31);
+    }
+}
 
 template <int IO>
 __device__ __forceinline__ float io_to_f32(uint32_t h) {
@@ -377,8 +410,10 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     };
 
     if (lane == 0) VW_TRACE(10, globaltimer());
-    Resolved cur = resolve_page(p, sm, begin, first_ord, lane, n);
-    publish(cur, 0);
+    if (p.plan == nullptr) {                        // else batch 0 came with the plan
+        Resolved cur = resolve_page(p, sm, begin, first_ord, lane, n);
+        publish(cur, 0);
+    }
     __syncwarp();
     if (lane == 0) VW_TRACE(11, globaltimer());
     // Early pages: the first S pages fill every stage once and need no empty
@@ -616,11 +651,17 @@ __device__ __forceinline__ void dequant_half(const uint8_t* stage, uint8_t* ctil
         lo.z = fp8x2_to_f16x2_scaled(w.y, 0); lo.w = fp8x2_to_f16x2_scaled(w.y, 1);
         hi.x = fp8x2_to_f16x2_scaled(w.z, 0); hi.y = fp8x2_to_f16x2_scaled(w.z, 1);
         hi.z = fp8x2_to_f16x2_scaled(w.w, 0); hi.w = fp8x2_to_f16x2_scaled(w.w, 1);
-        // codes c16*16 .. +15 are f16 elements of column c16/4, 16-B units 2*(c16%4), +1
+        // codes c16*16 .. +15 are f16 elements of column c16/4, 16-B units 2*(c16%4), +1.
+        // The 8 lanes of a row (one quarter-warp per store) cover both columns;
+        // column-1 lanes store their odd unit first so that each store touches 8
+        // different 16-B bank groups.
         uint8_t* base = ctile + (c16 >> 2) * 2048 + r * 128;
         const int u = (c16 & 3) * 2;
-        *reinterpret_cast<uint4*>(base + ((u ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4*>(base + (((u + 1) ^ (r & 7)) << 4)) = hi;
+        const bool odd_first = (c16 >> 2) != 0;
+        const uint4 first = odd_first ? hi : lo, second = odd_first ? lo : hi;
+        const int u1 = odd_first ? u + 1 : u, u2 = odd_first ? u : u + 1;
+        *reinterpret_cast<uint4*>(base + ((u1 ^ (r & 7)) << 4)) = first;
+        *reinterpret_cast<uint4*>(base + ((u2 ^ (r & 7)) << 4)) = second;
     }
 }
 
@@ -944,52 +985,61 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     const bool early = pdl && (p.flags & kDecodeEarlyPages) != 0;
     if (pdl && !early) griddep_wait();
     griddep_launch_dependents();
-    if (warp == kProducerWarp) {
-        if (lane == 0) prefetch_tensormap(&tmap);
-        // pages per sequence -> exclusive prefixes of pages and of non-empty
-        // sequences (one warp, 32 sequences at a time)
-        int run = 0, run_nz = 0;
-        if (lane == 0) { sm.pfx[0] = 0; sm.nzp[0] = 0; }
-        for (int base_b = 0; base_b < (int)p.B; base_b += 32) {
-            const int b = base_b + lane;
-            int np = 0;
-            if (b < (int)p.B) {
-                const int sl = (int)__ldg(p.seq_lens + b);
-                np = (sl + 15) >> 4;
-                if (sl <= 0 || np > (int)p.bt_stride) {
-                    if (blockIdx.x == 0) set_err(p.err, kDevErrSeqLen);
-                    np = sl <= 0 ? 0 : (int)p.bt_stride;
-                }
-            }
-            int incl = np, incl_nz = np > 0 ? 1 : 0;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, incl, off);
-                const int vz = __shfl_up_sync(0xffffffffu, incl_nz, off);
-                if (lane >= off) { incl += v; incl_nz += vz; }
-            }
-            if (b < (int)p.B) { sm.pfx[b + 1] = run + incl; sm.nzp[b + 1] = run_nz + incl_nz; }
-            run += __shfl_sync(0xffffffffu, incl, 31);
-            run_nz += __shfl_sync(0xffffffffu, incl_nz, 31);
+    // The page assignment: from the plan (one round trip for the prefixes,
+    // this CTA's range and its first 32 page records), or computed here.
+    const bool planned = p.plan != nullptr;
+    if (planned) {
+        const int* entry = p.plan + kPlanCta + (size_t)blockIdx.x * kPlanCtaInts;
+        // (L2 reads: the plan is rewritten by later plan launches)
+        for (int i = threadIdx.x; i <= (int)p.B; i += kThreads) {
+            sm.pfx[i] = __ldcg(p.plan + kPlanPfx + i);
+            sm.nzp[i] = __ldcg(p.plan + kPlanNzp + i);
         }
+        if (warp == kProducerWarp) {
+            if (lane == 0) prefetch_tensormap(&tmap);
+            if (lane < 3) sm.flag[2 + lane] = __ldcg(entry + lane);
+            const int4 rec = __ldcg(reinterpret_cast<const int4*>(entry + 4) + lane);
+            PageInfo pi;
+            pi.kvrow = p.k_new != nullptr ? rec.x : -1;
+            pi.row0 = rec.y >= 0 ? rec.y + (int)(p.layer * p.num_blocks * p.Hkv * 32u) : rec.y;
+            pi.qseg = rec.z;
+            pi.qrow = rec.w;
+            sm.pinfo[lane] = pi;
+        }
+    } else if (warp == kProducerWarp) {
+        if (lane == 0) prefetch_tensormap(&tmap);
+        warp_prefixes(p.seq_lens, (int)p.B, (int)p.bt_stride, p.err, blockIdx.x == 0, sm.pfx, sm.nzp,
+                      lane);
     }
     __syncthreads();
     if (threadIdx.x == 0) VW_TRACE(1, globaltimer());
 
-    const int total = (int)p.Hkv * sm.pfx[p.B];
-    const int vper = virtual_per_cta(virtual_total(total, (int)p.Hkv * sm.nzp[p.B]), (int)gridDim.x);
-    const int begin = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, (int)blockIdx.x * vper);
-    const int end = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, ((int)blockIdx.x + 1) * vper);
+    int begin, end;
+    if (planned) {
+        begin = sm.flag[2];
+        end = sm.flag[3];
+    } else {
+        const int total = (int)p.Hkv * sm.pfx[p.B];
+        const int vper = virtual_per_cta(virtual_total(total, (int)p.Hkv * sm.nzp[p.B]), (int)gridDim.x);
+        begin = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, (int)blockIdx.x * vper);
+        end = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, ((int)blockIdx.x + 1) * vper);
+    }
     if (begin >= end) return;
 
     if (warp == kProducerWarp) {
         if (lane == 0) VW_TRACE(15, globaltimer());
         // ordinal of the first segment of this range among non-empty segments
-        const int b0 = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, begin);
-        const int h0 = (begin - (int)p.Hkv * sm.pfx[b0]) / (sm.pfx[b0 + 1] - sm.pfx[b0]);
+        int first_ord;
+        if (planned) {
+            first_ord = sm.flag[4];
+        } else {
+            const int b0 = find_seq(sm.pfx, (int)p.B, (int)p.Hkv, begin);
+            const int h0 = (begin - (int)p.Hkv * sm.pfx[b0]) / (sm.pfx[b0 + 1] - sm.pfx[b0]);
+            first_ord = sm.nzp[b0] * (int)p.Hkv + h0;
+        }
         DecodeParams pp = p;
         if (!early) pp.flags &= ~(kDecodePdl | kDecodeEarlyPages);   // already waited above
-        producer<T>(&tmap, pp, sm, begin, end - begin, sm.nzp[b0] * (int)p.Hkv + h0, deadline);
+        producer<T>(&tmap, pp, sm, begin, end - begin, first_ord, deadline);
     } else {
         if (early) {
             griddep_wait();            // q, k_new, v_new may come from the predecessor
@@ -1081,6 +1131,67 @@ __global__ void __launch_bounds__(kCombineThreads, kCombineMinBlocks) combine_ke
     if (j < g && d < D) merge_unit<D, G, IO>(p, b, h, j, d, c0, n, slot0, vfold);
     if (threadIdx.x == 0) VW_TRACE(14, globaltimer());
 }
+
+
+// ------------------------------------------------------------------ plan
+
+// One warp per decode CTA: the same prefixes, range and first-batch page
+// records the decode prologue computes, written once for all the layers of a
+// step.  Page records are resolved as for an appending decode (kvrow set when
+// the range holds the segment's last page); a decode without new rows ignores
+// kvrow.
+__global__ void __launch_bounds__(32) plan_kernel(const DecodeParams p, int* plan) {
+    __shared__ int pfx[kMaxBatchPerLaunch + 1], nzp[kMaxBatchPerLaunch + 1];
+    const int lane = threadIdx.x;
+    const int B = (int)p.B, Hkv = (int)p.Hkv;
+    warp_prefixes(p.seq_lens, B, (int)p.bt_stride, p.err, blockIdx.x == 0, pfx, nzp, lane);
+    __syncwarp();
+    if (blockIdx.x == 0) {
+        if (lane == 0) {
+            plan[0] = B; plan[1] = (int)p.bt_stride; plan[2] = (int)gridDim.x; plan[3] = Hkv;
+        }
+        for (int i = lane; i <= B; i += 32) { plan[kPlanPfx + i] = pfx[i]; plan[kPlanNzp + i] = nzp[i]; }
+    }
+    const int total = Hkv * pfx[B];
+    const int vper = virtual_per_cta(virtual_total(total, Hkv * nzp[B]), (int)gridDim.x);
+    const int begin = range_start(pfx, nzp, B, Hkv, (int)blockIdx.x * vper);
+    const int end = range_start(pfx, nzp, B, Hkv, ((int)blockIdx.x + 1) * vper);
+    int* entry = plan + kPlanCta + (size_t)blockIdx.x * kPlanCtaInts;
+    int first_ord = 0;
+    if (begin < end) {
+        const int b0 = find_seq(pfx, B, Hkv, begin);
+        const int h0 = (begin - Hkv * pfx[b0]) / (pfx[b0 + 1] - pfx[b0]);
+        first_ord = nzp[b0] * Hkv + h0;
+    }
+    if (lane == 0) { entry[0] = begin; entry[1] = end; entry[2] = first_ord; entry[3] = 0; }
+    int4 rec = make_int4(-1, -32, -1, -1);
+    const int n = end - begin, i = lane;
+    if (i < n) {
+        const int x = begin + i;
+        const int b = find_seq(pfx, B, Hkv, x);
+        const int np = pfx[b + 1] - pfx[b];
+        const int rr = x - Hkv * pfx[b];
+        const int h = rr / np, pg = rr - h * np;
+        const uint32_t blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg);
+        if (blk < p.num_blocks) rec.y = (int)((blk * (uint32_t)Hkv + (uint32_t)h) * 32u);
+        else set_err(p.err, kDevErrBlockId);
+        if (i == 0 || pg == 0) {
+            rec.z = nzp[b] * Hkv + h - first_ord;
+            rec.w = (int)(b * p.Hq + h * p.group);
+            if (i + (np - 1 - pg) < n) rec.x = b * Hkv + h;
+        }
+    }
+    reinterpret_cast<int4*>(entry + 4)[lane] = rec;
+}
+
+}  // namespace
+
+cudaError_t launch_decode_plan(const DecodeParams& p, int grid, int* plan, cudaStream_t s) {
+    plan_kernel<<<grid, 32, 0, s>>>(p, plan);
+    return cudaGetLastError();
+}
+
+namespace {
 
 template <class T>
 cudaError_t launch_combine(const DecodeLaunch& L) {

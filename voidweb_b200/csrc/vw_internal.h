@@ -26,13 +26,28 @@ struct DecodeParams {
     float* part_o;              // [grid][2][G][D] split-K partial outputs
     float* part_ml;             // [grid][2][G][2] (running max, sum)
     uint32_t* err;              // device error word
+    const int* plan;            // page assignment written by the plan kernel (kDecodePlanned)
     uint32_t B, Hq, Hkv, group, num_blocks, layer, bt_stride, fp8_ocp;
     float scale_log2;           // softmax scale * log2(e)
-    uint32_t flags;             // kDecodePdl | kDecodeEarlyPages
+    uint32_t flags;             // kDecodePdl | kDecodeEarlyPages | kDecodePlanned
 };
 
 constexpr uint32_t kDecodePdl = 0x1u;
 constexpr uint32_t kDecodeEarlyPages = 0x2u;
+constexpr uint32_t kDecodePlanned = 0x4u;
+
+// Decode plan (int32 words): a header {B, bt_stride, grid, Hkv}, the exclusive
+// prefixes of pages and of sequences with pages over the batch, then one entry
+// per decode CTA: {begin, end, first segment ordinal, 0} and the 32 page records
+// of its first batch ({kvrow, row0 without the layer offset, qseg, qrow}).
+constexpr int kPlanPfx = 4;
+constexpr int kPlanNzp = kPlanPfx + kMaxBatchPerLaunch + 1;
+constexpr int kPlanCta = (kPlanNzp + kMaxBatchPerLaunch + 1 + 3) / 4 * 4;
+constexpr int kPlanCtaInts = 4 + 32 * 4;
+inline size_t plan_ints(int grid) { return (size_t)kPlanCta + (size_t)grid * kPlanCtaInts; }
+// p carries the batch (B, Hq, Hkv, group, bt_stride, num_blocks, tables,
+// seq_lens, err); plan receives plan_ints(grid) words.
+cudaError_t launch_decode_plan(const DecodeParams& p, int grid, int* plan, cudaStream_t s);
 
 struct DecodeLaunch {
     DecodeParams p;

@@ -140,6 +140,15 @@ class KvPool:
         C.check(C.lib().vw_paged_decode(self._h, ctypes.byref(a), _stream(stream)))
         return out
 
+    def plan(self, block_tables: torch.Tensor, seq_lens: torch.Tensor, num_q_heads: int,
+             stream=None) -> None:
+        """Page assignment of a decode batch for every layer's paged_decode with
+        VW_DECODE_PLANNED (same block_tables / seq_lens tensors, unchanged until
+        the next plan)."""
+        C.check(C.lib().vw_decode_plan(self._h, _ptr(block_tables), _ptr(seq_lens),
+                                       block_tables.shape[0], block_tables.shape[1], num_q_heads,
+                                       _stream(stream)))
+
     def block_copy(self, pairs: torch.Tensor, stream=None) -> None:
         """Copy-on-write / compaction copy of whole blocks: pairs [n][2] (src, dst)."""
         C.check(C.lib().vw_block_copy(self._h, _ptr(pairs), pairs.shape[0], _stream(stream)))
