@@ -955,7 +955,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Smem sm = carve<T>(base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t deadline = globaltimer() + kWaitDeadlineNs;
+    const uint64_t deadline = cycles() + kWaitDeadlineCycles;
     if (threadIdx.x == 0) VW_TRACE(0, globaltimer());
 #ifdef VW_DECODE_TRACE
     if (threadIdx.x == 0) {

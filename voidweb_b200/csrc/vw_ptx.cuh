@@ -1,8 +1,8 @@
 // vw_ptx.cuh -- thin inline-PTX helpers for sm_100a: mbarriers, TMA tensor
 // and bulk copies, warp-level tensor-core fragments (ldmatrix / movmatrix /
 // mma.sync), and bounded waits.  Every wait here gives up after a deadline on
-// %globaltimer so that no kernel can hang a GPU; the caller records the
-// failure in the pool's device error word and unwinds.
+// the SM's cycle counter so that no kernel can hang a GPU; the caller records
+// the failure in the pool's device error word and unwinds.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -17,7 +17,17 @@ enum : uint32_t {
     kDevErrSlot = 1u << 3,        // append slot outside the pool
 };
 
-constexpr uint64_t kWaitDeadlineNs = 2000000000ull;   // 2 s: kernels run for microseconds
+// Wait deadline in SM cycles: 4e9 cycles is about 2 s at the 1965 MHz maximum
+// clock and at most about 4 s at any clock the part runs a kernel at; kernels
+// here run for microseconds.  The cycle counter is read in a few cycles, unlike
+// %globaltimer, so polling it does not delay the waiter's wake-up.
+constexpr uint64_t kWaitDeadlineCycles = 4000000000ull;
+
+__device__ __forceinline__ uint64_t cycles() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
@@ -68,12 +78,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed, or until the
-// deadline passes.  Returns false on timeout.
+// deadline (cycles(), see kWaitDeadlineCycles) passes.  Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline) {
     if (mbar_try_wait(bar, parity)) return true;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() > deadline) return false;
+        if (cycles() > deadline) return false;
     }
 }
 
