@@ -115,7 +115,16 @@ typedef struct {
     const void* v_new;             /*   written at position seq_len-1 before attending */
     float scale;                   /* softmax scale; 0 means 1/sqrt(head_dim) (flash_attention.bm:187) */
     uint32_t flags;                /* VW_DECODE_* bits below, 0 for a plain launch */
+    float rope_theta;              /* with VW_DECODE_ROPE: the RoPE base (ModelConfig rope_theta) */
+    uint32_t reserved;             /* must be 0 */
 } vw_decode_args;
+
+/* Rotary position embedding fused into the decode (kernels/rope/rope.bm:22-52,
+ * rotate-half pairs (d, d + head_dim/2), theta_d = rope_theta^(-2d/head_dim)):
+ * q of every query head and the new K row (with k_new) are rotated to position
+ * seq_len-1 and rounded to the io type before use, as a separate RoPE pass
+ * over q and k would leave them; the pool stores rotated K.  V is unchanged. */
+#define VW_DECODE_ROPE 0x8u
 
 /* Launch as a programmatic dependent of the previous kernel on the stream: the
  * kernel may start while its predecessor drains and waits for it before
@@ -205,7 +214,7 @@ typedef struct {
     const uint32_t* seq_lens;      /* host [num_seqs] (including the new token) */
     void* out;                     /* host [L][num_seqs][num_q_heads][head_dim] */
     float scale;
-    uint32_t reserved2;
+    float rope_theta;              /* > 0: fused RoPE on q and the new K rows (VW_DECODE_ROPE) */
 } vw_step_host_args;
 VW_API int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* args, void* stream);
 

@@ -58,6 +58,7 @@ def lib() -> ctypes.CDLL:
                                            ctypes.c_int]),
             "vwo_paged_decode_f64": (i32, [vp, vp, vp, u32, vp, u32, vp, u32, vp, u32, f64, vp,
                                            ctypes.c_int]),
+            "vwo_rope_apply": (None, [vp, u32, u32, u32, vp, f32, u32]),
             "vwo_rolling_hash": (u64, [u64, vp, u32]),
             "vwo_bm_new": (vp, [u32, u32]), "vwo_bm_delete": (None, [vp]),
             "vwo_bm_capacity": (u32, [vp]), "vwo_bm_free_count": (u32, [vp]),
@@ -147,6 +148,16 @@ def fp8_quant_row(x: np.ndarray, mode: int = FP8_REFERENCE):
 def pool_shape(g: Geom):
     """[L][NB][Hkv][2][16][D]: per head, a page is K rows then V rows."""
     return (g.num_layers, g.num_blocks, g.num_kv_heads, 2, 16, g.head_dim)
+
+
+def rope_apply(x: np.ndarray, pos, theta: float, io_dtype: int) -> np.ndarray:
+    """kernels/rope/rope.bm:22-52 on a copy of x [n][H][D] (io dtype bits),
+    token i at position pos[i]."""
+    y = np.array(x, dtype=np.uint16, copy=True, order="C")
+    n, H, D = y.shape
+    p = np.ascontiguousarray(pos, dtype=np.uint32)
+    lib().vwo_rope_apply(_p(y), n, H, D, _p(p), theta, io_dtype)
+    return y
 
 
 def kv_append(g: Geom, data: np.ndarray, scales, layer: int, k_new: np.ndarray,

@@ -402,6 +402,27 @@ struct OBlockManager {
 
 // kv_cache.bm:157-164 rolling_hash: h = prev + len*P, then h = h*P + t
 // (wrapping u64), P = 0x9e3779b97f4a7c15.
+// Rotary position embedding in place on x [n][H][D] (io dtype bits), token i at
+// position pos[i]: kernels/rope/rope.bm:22-52.  For each pair (d, d + D/2):
+// freq = 1 / theta^(2d / D), angle = freq * pos, (x_r, x_i) ->
+// (x_r cos - x_i sin, x_r sin + x_i cos) in f32 (no contraction: this file is
+// built with -ffp-contract=off), stored back rounded to the io type (:48-49).
+void vwo_rope_apply(void* x, uint32_t n, uint32_t H, uint32_t D, const uint32_t* pos,
+                    float theta, uint32_t io) {
+    const uint32_t half = D / 2;
+    for (uint32_t i = 0; i < n; ++i)
+        for (uint32_t h = 0; h < H; ++h)
+            for (uint32_t d = 0; d < half; ++d) {
+                const float freq = 1.0f / std::pow(theta, 2.0f * (float)d / (float)D);
+                const float angle = freq * (float)pos[i];
+                const float s = std::sin(angle), c = std::cos(angle);
+                const size_t base = ((size_t)i * H + h) * D;
+                const float xr = io_to_f32(x, base + d, io), xi = io_to_f32(x, base + d + half, io);
+                static_cast<uint16_t*>(x)[base + d] = f32_to_io(xr * c - xi * s, io);
+                static_cast<uint16_t*>(x)[base + d + half] = f32_to_io(xr * s + xi * c, io);
+            }
+}
+
 uint64_t vwo_rolling_hash(uint64_t prev, const uint32_t* tokens, uint32_t n) {
     const uint64_t P = 0x9e3779b97f4a7c15ull;
     uint64_t h = prev + (uint64_t)n * P;

@@ -44,7 +44,7 @@ def test_packed_struct_sizes_match_engine():
 _Static_assert(sizeof(SeqDescriptor) == 33, "SeqDescriptor");
 _Static_assert(sizeof(ForwardArgs) == 52, "ForwardArgs");
 _Static_assert(offsetof(ForwardArgs, logits_out) == 44, "logits_out");
-_Static_assert(sizeof(vw_decode_args) == 72, "vw_decode_args");
+_Static_assert(sizeof(vw_decode_args) == 80, "vw_decode_args");
 _Static_assert(sizeof(vw_pool_config) == 56, "vw_pool_config");
 int main(void) { return 0; }
 '''
@@ -53,7 +53,7 @@ int main(void) { return 0; }
         open(f, "w").write(code)
         subprocess.run(["gcc", "-std=c11", "-I", os.path.dirname(HEADER), f, "-o",
                         os.path.join(d, "t")], check=True)
-    assert ctypes.sizeof(C.DecodeArgs) == 72
+    assert ctypes.sizeof(C.DecodeArgs) == 80
     assert ctypes.sizeof(C.PoolConfig) == 56
 
 

@@ -67,13 +67,13 @@ def check_close(got_bits, ref64, io, what=""):
                            f"max err {err.max():.3g} (worst ratio {(err / bound).max():.3g})")
 
 
-def run_decode(pool, c, layer, dev, fused=False):
+def run_decode(pool, c, layer, dev, fused=False, rope_theta=0.0):
     q = t16(c.q[layer], dev)
     out = torch.zeros_like(q)
     bt, sl = tu32(c.block_tables, dev), tu32(c.seq_lens, dev)
     kn = t16(c.k_new[layer], dev) if fused else None
     vn = t16(c.v_new[layer], dev) if fused else None
-    pool.paged_decode(layer, q, bt, sl, out, k_new=kn, v_new=vn)
+    pool.paged_decode(layer, q, bt, sl, out, k_new=kn, v_new=vn, rope_theta=rope_theta)
     torch.cuda.synchronize()
     return out.cpu().numpy().view(np.uint16)
 
@@ -262,7 +262,10 @@ def test_host_step_and_forward_pass_match_device_path(dev):
     from voidweb_b200 import _lib as C
     c = kvgen.make_case(12, 3, 2, 128, 8, 4, 5, 200, BF16, BF16)
     pool = make_pool(c, dev)
-    dev_out = [run_decode(pool, c, layer, dev, fused=True) for layer in range(c.L)]
+    # the engine passes its model's rope_theta (ForwardArgs); the shim applies it
+    theta = 10000.0
+    dev_out = [run_decode(pool, c, layer, dev, fused=True, rope_theta=theta)
+               for layer in range(c.L)]
     upload_pool(pool, c)
     out = np.zeros_like(c.q)
     pool.decode_step_host(torch.from_numpy(c.q.view(np.int16)),
@@ -270,7 +273,7 @@ def test_host_step_and_forward_pass_match_device_path(dev):
                           torch.from_numpy(c.v_new.view(np.int16)),
                           torch.from_numpy(c.block_tables.astype(np.int32)),
                           torch.from_numpy(c.seq_lens.astype(np.int32)),
-                          torch.from_numpy(out.view(np.int16)))
+                          torch.from_numpy(out.view(np.int16)), rope_theta=theta)
     for layer in range(c.L):
         assert np.array_equal(out[layer], dev_out[layer])
     # the engine-facing symbol: same step through voidweb_forward_pass
@@ -284,8 +287,8 @@ def test_host_step_and_forward_pass_match_device_path(dev):
     kl = KernelLib.open(C.LIB_PATH)
     seqs = [(1000 + b, 7, c.block_tables[b, : (int(c.seq_lens[b]) + 15) // 16])
             for b in range(c.B)]
-    kl.forward_pass(dict(num_heads=c.Hq, num_kv_heads=c.Hkv, num_layers=c.L, head_dim=c.D),
-                    seqs)
+    kl.forward_pass(dict(num_heads=c.Hq, num_kv_heads=c.Hkv, num_layers=c.L, head_dim=c.D,
+                         rope_theta=theta), seqs)
     for layer in range(c.L):
         assert np.array_equal(out2[layer], dev_out[layer])
     for b in range(c.B):
@@ -386,4 +389,49 @@ def test_planned_decode_is_bit_identical(dev):
     other = bt.clone()
     with pytest.raises(C.VoidwebError):
         pool.paged_decode(0, q, other, sl, planned, flags=C.VW_DECODE_PLANNED)
+    pool.close()
+
+
+@pytest.mark.parametrize("kv,io,D", [(BF16, BF16, 128), (F16, F16, 64), (FP8, BF16, 128)])
+def test_fused_rope_append_decode(dev, kv, io, D):
+    """RoPE fused into the decode (kernels/rope/rope.bm:22-52): q and the new K
+    row are rotated to position seq_len-1.  The appended K rows match the
+    oracle's rotation within one unit in the last place of the io type (f32
+    sin/cos may round differently); V rows and, for FP8, their codes are exact;
+    outputs are within the attention tolerance of the fp64 oracle run on the
+    rotated q and the device's own pages."""
+    theta = 1000000.0 if D == 128 else 10000.0
+    c = kvgen.make_case(60 + kv + D, 1, 2, D, 8, 6, 1, 3000, kv, io)
+    pool = make_pool(c, dev)
+    got = run_decode(pool, c, 0, dev, fused=True, rope_theta=theta)
+    assert pool.check() == 0
+    pos = c.seq_lens.astype(np.int64) - 1
+    q_rot = oracle.rope_apply(c.q[0], pos, theta, io)
+    k_rot = oracle.rope_apply(c.k_new[0], pos, theta, io)
+    gdata, gscales = download_pool(pool, c)
+    slots = kvgen.new_token_slots(c)
+    if kv != FP8:
+        want = c.data.copy()
+        oracle.kv_append(c.geom, want, None, 0, k_rot, c.v_new[0], slots)
+        rel = 2.0 ** -7 if io == BF16 else 2.0 ** -10
+        exact = 0
+        for s in slots:
+            blk, t = int(s) // 16, int(s) % 16
+            # V rows are untouched by the rotation: bit for bit
+            assert np.array_equal(gdata[0, blk, :, 1, t], want[0, blk, :, 1, t])
+            # rotated K rows: two last places of an f32 angle below 2^12 rad
+            # (< 2.5e-4 rad each) times |x_r| + |x_i| < 8, plus one io rounding
+            g = oracle.io_bits_to_f32(gdata[0, blk, :, 0, t], io)
+            w = oracle.io_bits_to_f32(want[0, blk, :, 0, t], io)
+            assert (np.abs(g - w) <= 8e-3 + rel * np.abs(w)).all(), "rotated K row"
+            exact += np.sum(gdata[0, blk, :, 0, t] == want[0, blk, :, 0, t])
+        assert exact >= 0.9 * len(slots) * c.Hkv * D
+        # and nothing else in the pool moved
+        mask = np.ones(gdata.shape, dtype=bool)
+        for s in slots:
+            mask[0, int(s) // 16, :, :, int(s) % 16] = False
+        assert np.array_equal(gdata[mask], want[mask])
+    ref = oracle.paged_decode_f64(c.geom, gdata, gscales, 0, q_rot, c.Hq, c.block_tables,
+                                  c.seq_lens, 1.0 / np.sqrt(D))
+    check_close(got, ref, io, f"rope {kv}/{io}/D{D}")
     pool.close()

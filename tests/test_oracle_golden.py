@@ -181,3 +181,38 @@ def test_block_copy_snapshot_semantics():
     assert (data[:, 2] == before[:, 1]).all() and (data[:, 4] == before[:, 2]).all()
     assert (scales[:, 4] == sbefore[:, 2]).all()
     assert (data[:, [0, 1, 3, 5]] == before[:, [0, 1, 3, 5]]).all()
+
+
+@pytest.mark.parametrize("io", [oracle.BF16, oracle.F16])
+def test_rope_matches_numpy_restatement(io):
+    """kernels/rope/rope.bm:22-52 in the oracle against an independent numpy
+    restatement with the same f32 steps (freq = 1 / theta^(2d/D), angle =
+    freq * pos, rotate, round to the io type): the two sides use different pow
+    / sin / cos implementations, so they may differ by two last places of the
+    f32 angle (large at large positions) plus one rounding to the io type.
+    Position 0 is exact."""
+    rng = np.random.default_rng(11)
+    n, H, D, theta = 37, 3, 128, 10000.0
+    x = oracle.f32_to_io_bits(rng.standard_normal((n, H, D)).astype(np.float32), io)
+    pos = rng.integers(0, 32768, n)
+    pos[0] = 0
+    got = oracle.rope_apply(x, pos, theta, io)
+    f32 = np.float32
+    xf = oracle.io_bits_to_f32(x, io)
+    d = np.arange(D // 2, dtype=np.float32)
+    freq = f32(1.0) / np.power(f32(theta), (f32(2.0) * d) / f32(D)).astype(np.float32)
+    ang = (freq[None, :] * pos[:, None].astype(np.float32)).astype(np.float32)
+    c = np.cos(ang.astype(np.float64)).astype(np.float32)[:, None, :]
+    s = np.sin(ang.astype(np.float64)).astype(np.float32)[:, None, :]
+    xr, xi = xf[..., : D // 2], xf[..., D // 2:]
+    want = np.concatenate([xr * c - xi * s, xr * s + xi * c], axis=-1).astype(np.float32)
+    want_bits = oracle.f32_to_io_bits(want, io)
+    assert np.array_equal(got[0], x[0])
+    g = oracle.io_bits_to_f32(got, io)
+    rel = 2.0 ** -7 if io == oracle.BF16 else 2.0 ** -10
+    # a last-place difference of freq plus one of the product: two ulps of the
+    # angle, each moving the rotated pair by at most ulp * (|x_r| + |x_i|)
+    amp = (np.abs(xr) + np.abs(xi)) * 2.0 * np.spacing(ang)[:, None, :]
+    bound = np.concatenate([amp, amp], axis=-1) + rel * np.abs(want) + 1e-6
+    assert (np.abs(g - want) <= bound).all()
+    assert np.mean(got == want_bits) > 0.97

@@ -25,7 +25,7 @@ VW_ERR_DEVICE_CHECK = 5
 
 VW_F16, VW_BF16, VW_FP8_E4M3 = 0, 1, 2
 VW_FP8_REFERENCE, VW_FP8_OCP = 0, 1
-VW_DECODE_PDL, VW_DECODE_EARLY_PAGES, VW_DECODE_PLANNED = 0x1, 0x2, 0x4
+VW_DECODE_PDL, VW_DECODE_EARLY_PAGES, VW_DECODE_PLANNED, VW_DECODE_ROPE = 0x1, 0x2, 0x4, 0x8
 
 DEV_ERR_BLOCK_ID, DEV_ERR_SEQ_LEN, DEV_ERR_TIMEOUT, DEV_ERR_SLOT = 1, 2, 4, 8
 
@@ -44,14 +44,15 @@ class PoolConfig(ctypes.Structure):
 class DecodeArgs(ctypes.Structure):
     _fields_ = [("layer", u32), ("num_seqs", u32), ("num_q_heads", u32),
                 ("block_table_stride", u32), ("q", vp), ("block_tables", vp), ("seq_lens", vp),
-                ("out", vp), ("k_new", vp), ("v_new", vp), ("scale", f32), ("flags", u32)]
+                ("out", vp), ("k_new", vp), ("v_new", vp), ("scale", f32), ("flags", u32),
+                ("rope_theta", f32), ("reserved", u32)]
 
 
 class StepHostArgs(ctypes.Structure):
     _fields_ = [("num_seqs", u32), ("num_q_heads", u32), ("block_table_stride", u32),
                 ("reserved", u32), ("q", vp), ("k_new", vp), ("v_new", vp),
                 ("block_tables", vp), ("seq_lens", vp), ("out", vp), ("scale", f32),
-                ("reserved2", u32)]
+                ("rope_theta", f32)]
 
 
 class SeqDescriptor(ctypes.Structure):

@@ -303,8 +303,11 @@ int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const voi
 static int32_t decode_validate(const vw_pool* pool, const vw_decode_args* a) {
     if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: null argument");
     const PoolGeom& g = pool->geom;
-    if (a->flags & ~(uint32_t)(VW_DECODE_PDL | VW_DECODE_EARLY_PAGES | VW_DECODE_PLANNED))
+    if (a->flags & ~(uint32_t)(VW_DECODE_PDL | VW_DECODE_EARLY_PAGES | VW_DECODE_PLANNED | VW_DECODE_ROPE))
         return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: unknown flags 0x%x", a->flags);
+    if (a->reserved != 0) return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: reserved must be 0");
+    if ((a->flags & VW_DECODE_ROPE) && !(a->rope_theta > 1.0f && std::isfinite(a->rope_theta)))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_decode: VW_DECODE_ROPE needs a finite rope_theta > 1");
     if ((a->flags & VW_DECODE_PLANNED) &&
         (!pool->plan_ready || pool->plan_tables != a->block_tables || pool->plan_lens != a->seq_lens ||
          pool->plan_seqs != a->num_seqs || pool->plan_stride != a->block_table_stride ||
@@ -368,6 +371,7 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
     // reference scale: 1.0 / (HEAD_DIM as f32).sqrt() (flash_attention.bm:187)
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
+    p.rope_theta = (a->flags & VW_DECODE_ROPE) ? a->rope_theta : 0.0f;
     L.tmap = &pool->tmap;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;
@@ -458,7 +462,9 @@ int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block_table,
 
 int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* stream) {
     if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: null argument");
-    if (a->reserved || a->reserved2) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: reserved");
+    if (a->reserved) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: reserved");
+    if (a->rope_theta != 0.0f && !(a->rope_theta > 1.0f && std::isfinite(a->rope_theta)))
+        return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: rope_theta must be 0 or a finite value > 1");
     const PoolGeom& g = pool->geom;
     const uint32_t B = a->num_seqs, Hq = a->num_q_heads, L = g.num_layers, D = g.head_dim;
     if (B == 0) return VW_OK;
@@ -533,6 +539,10 @@ int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* str
             // consecutive layers of a chunk: the previous launch writes only its own
             // layer's pages and outputs, so this one may stream pages early
             if (l > l0) da.flags = VW_DECODE_PDL | VW_DECODE_EARLY_PAGES;
+            if (a->rope_theta > 0.0f) {
+                da.flags |= VW_DECODE_ROPE;
+                da.rope_theta = a->rope_theta;
+            }
             rc = decode_validate(pool, &da);
             if (rc == VW_OK) rc = decode_launch(pool, &da, cs);
         }
@@ -640,6 +650,9 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
     st.seq_lens = lens.data();
     st.out = s.out;
     st.scale = 0.0f;
+    // ModelConfig.rope_theta (engine/ffi.bm:37): q and the new K rows are rotated
+    // in the decode, as the engine's own kernels would before attention
+    st.rope_theta = a.rope_theta > 1.0f ? a.rope_theta : 0.0f;
     int32_t rc = vw_decode_step_host(s.pool, &st, nullptr);
     if (rc != VW_OK) return rc;
     for (uint32_t i = 0; i < a.num_seqs; ++i) s.seq_len[d[i].seq_id] = lens[i];
@@ -745,6 +758,7 @@ int32_t vw_paged_decode_static(vw_pool* pool, const vw_decode_args* a, void* str
     p.fp8_ocp = g.fp8_ocp;
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
+    p.rope_theta = (a->flags & VW_DECODE_ROPE) ? a->rope_theta : 0.0f;
     L.tmap = &pool->tmap;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;

@@ -550,27 +550,64 @@ __device__ __forceinline__ void merge_unit(const DecodeParams& p, int b, int h, 
 
 // ------------------------------------------------------------------ consumer
 
-// Query fragments (B operand of S^T = K Q^T) from the staged query tile.
+// Rotary position embedding of one pair (x[d], x[d + D/2]) at position pos,
+// kernels/rope/rope.bm:22-52: theta_d = 1 / theta^(2d/D), angle = theta_d * pos,
+// (x_r, x_i) -> (x_r cos - x_i sin, x_r sin + x_i cos), all in f32 with no
+// fused multiply-adds, the result rounded to the io type by the caller.
+__device__ __forceinline__ void rope_pair(float& xr, float& xi, int d, int D, float theta, float pos) {
+    const float freq = __fdiv_rn(1.0f, powf(theta, __fdiv_rn(2.0f * (float)d, (float)D)));
+    float s, c;
+    sincosf(__fmul_rn(freq, pos), &s, &c);
+    const float r = __fsub_rn(__fmul_rn(xr, c), __fmul_rn(xi, s));
+    const float i = __fadd_rn(__fmul_rn(xr, s), __fmul_rn(xi, c));
+    xr = r;
+    xi = i;
+}
+
+// Query fragments (B operand of S^T = K Q^T) from the staged query tile.  A
+// lane's fragments hold elements d and d + D/2 (k-steps kt and kt + KT/2), so
+// with rope_theta > 0 the rotation of the query heads at position pos happens
+// here in registers, rounded to the io type as a separate RoPE pass would.
 template <class T>
 __device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qtile, int lane,
-                                       uint32_t (&qf)[T::NT][T::KT][2]) {
+                                       float pos, uint32_t (&qf)[T::NT][T::KT][2]) {
 #pragma unroll
     for (int nt = 0; nt < T::NT; ++nt) {
         const int j = nt * 8 + (lane >> 2);
         const bool live = j < (int)p.group;
         const uint8_t* row = qtile + (live ? j : 0) * T::D * 2;
 #pragma unroll
-        for (int kt = 0; kt < T::KT; ++kt) {
+        for (int kt = 0; kt < T::KT; ++kt)
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
-                uint32_t v = live ? *reinterpret_cast<const uint32_t*>(row + d * 2) : 0u;
-                if constexpr (T::KV == kFP8 && T::IO == kBF16) {
-                    // pages compute in f16: convert the bf16 query pair
-                    v = pack2<false>(bf16_bits_to_f32(v & 0xFFFFu), bf16_bits_to_f32(v >> 16));
-                }
-                qf[nt][kt][hf] = v;
+                qf[nt][kt][hf] = live ? *reinterpret_cast<const uint32_t*>(row + d * 2) : 0u;
             }
+        if (p.rope_theta > 0.0f) {
+#pragma unroll
+            for (int kt = 0; kt < T::KT / 2; ++kt)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
+                    uint32_t& a = qf[nt][kt][hf];
+                    uint32_t& b = qf[nt][kt + T::KT / 2][hf];
+                    float ar = io_to_f32<T::IO>(a & 0xFFFFu), ai = io_to_f32<T::IO>(b & 0xFFFFu);
+                    float br = io_to_f32<T::IO>(a >> 16), bi = io_to_f32<T::IO>(b >> 16);
+                    rope_pair(ar, ai, d, T::D, p.rope_theta, pos);
+                    rope_pair(br, bi, d + 1, T::D, p.rope_theta, pos);
+                    a = (uint32_t)f32_to_io<T::IO>(ar) | ((uint32_t)f32_to_io<T::IO>(br) << 16);
+                    b = (uint32_t)f32_to_io<T::IO>(ai) | ((uint32_t)f32_to_io<T::IO>(bi) << 16);
+                }
+        }
+        if constexpr (T::KV == kFP8 && T::IO == kBF16) {
+            // pages compute in f16: convert the bf16 query pairs
+#pragma unroll
+            for (int kt = 0; kt < T::KT; ++kt)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const uint32_t v = qf[nt][kt][hf];
+                    qf[nt][kt][hf] = pack2<false>(bf16_bits_to_f32(v & 0xFFFFu), bf16_bits_to_f32(v >> 16));
+                }
         }
     }
 }
@@ -709,7 +746,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 if (lane == 0) set_err(p.err, kDevErrTimeout);
                 alive = false;
             }
-            load_q<T>(p, sm.qring + qs * T::QSLOT, lane, qf);
+            load_q<T>(p, sm.qring + qs * T::QSLOT, lane, (float)(seq_len - 1), qf);
             if (append && pg0 + cnt == np) {
                 // this range holds the segment's last page: keep the staged new
                 // K/V row pieces of this lane for the append
@@ -719,6 +756,25 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
 #pragma unroll
                     for (int k = 0; k < T::D / 64; ++k)
                         nkv[kv][k] = reinterpret_cast<const uint32_t*>(nrow + kv * T::D * 2)[k];
+                if (p.rope_theta > 0.0f) {
+                    // the new K row at position seq_len-1: lane l holds elements
+                    // l*D/32 .. +D/32-1, whose partners (d +- D/2) lane l ^ 16 holds
+                    const bool lo = lane < 16;
+                    const float pos = (float)(seq_len - 1);
+#pragma unroll
+                    for (int k = 0; k < T::D / 64; ++k) {
+                        const uint32_t own = nkv[0][k];
+                        const uint32_t other = __shfl_xor_sync(0xffffffffu, own, 16);
+                        const uint32_t rw = lo ? own : other, iw = lo ? other : own;
+                        float r0 = io_to_f32<T::IO>(rw & 0xFFFFu), i0 = io_to_f32<T::IO>(iw & 0xFFFFu);
+                        float r1 = io_to_f32<T::IO>(rw >> 16), i1 = io_to_f32<T::IO>(iw >> 16);
+                        const int d = (lane & 15) * (T::D / 32) + 2 * k;
+                        rope_pair(r0, i0, d, T::D, p.rope_theta, pos);
+                        rope_pair(r1, i1, d + 1, T::D, p.rope_theta, pos);
+                        nkv[0][k] = lo ? ((uint32_t)f32_to_io<T::IO>(r0) | ((uint32_t)f32_to_io<T::IO>(r1) << 16))
+                                       : ((uint32_t)f32_to_io<T::IO>(i0) | ((uint32_t)f32_to_io<T::IO>(i1) << 16));
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.qempty[qs]);

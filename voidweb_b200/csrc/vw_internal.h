@@ -29,6 +29,7 @@ struct DecodeParams {
     const int* plan;            // page assignment written by the plan kernel (kDecodePlanned)
     uint32_t B, Hq, Hkv, group, num_blocks, layer, bt_stride, fp8_ocp;
     float scale_log2;           // softmax scale * log2(e)
+    float rope_theta;           // > 0: rotate q and the new K row (RoPE) at position seq_len-1
     uint32_t flags;             // kDecodePdl | kDecodeEarlyPages | kDecodePlanned
 };
 

@@ -126,17 +126,23 @@ class KvPool:
 
     def paged_decode(self, layer: int, q: torch.Tensor, block_tables: torch.Tensor,
                      seq_lens: torch.Tensor, out: torch.Tensor, k_new=None, v_new=None,
-                     scale: float = 0.0, stream=None, flags: int = 0) -> torch.Tensor:
+                     scale: float = 0.0, stream=None, flags: int = 0,
+                     rope_theta: float = 0.0) -> torch.Tensor:
         """o = softmax(q K^T * scale) V over each sequence's pages (GQA, split-K).
 
         With k_new/v_new given, the new token's rows are first written at
         position seq_len-1 (fused append).  q/out: [B][Hq][D]; block_tables:
         [B][stride] int32 ids; seq_lens: [B] int32 (including the new token).
-        flags: VW_DECODE_PDL / VW_DECODE_EARLY_PAGES (see include/voidweb_kv.h).
+        flags: VW_DECODE_PDL / VW_DECODE_EARLY_PAGES / VW_DECODE_PLANNED (see
+        include/voidweb_kv.h).  rope_theta > 0 rotates q and the new K row at
+        position seq_len-1 first (VW_DECODE_ROPE).
         """
         B, Hq, _ = q.shape
+        if rope_theta > 0.0:
+            flags |= C.VW_DECODE_ROPE
         a = C.DecodeArgs(layer, B, Hq, block_tables.shape[1], _ptr(q), _ptr(block_tables),
-                         _ptr(seq_lens), _ptr(out), _ptr(k_new), _ptr(v_new), scale, flags)
+                         _ptr(seq_lens), _ptr(out), _ptr(k_new), _ptr(v_new), scale, flags,
+                         rope_theta, 0)
         C.check(C.lib().vw_paged_decode(self._h, ctypes.byref(a), _stream(stream)))
         return out
 
@@ -168,11 +174,11 @@ class KvPool:
         return ok, ov, ks, vs
 
     def decode_step_host(self, q, k_new, v_new, block_tables, seq_lens, out,
-                         scale: float = 0.0, stream=None) -> None:
+                         scale: float = 0.0, stream=None, rope_theta: float = 0.0) -> None:
         """One step over all layers with host (CPU, ideally pinned) tensors."""
         B, Hq = q.shape[1], q.shape[2]
         a = C.StepHostArgs(B, Hq, block_tables.shape[1], 0, _ptr(q), _ptr(k_new), _ptr(v_new),
-                           _ptr(block_tables), _ptr(seq_lens), _ptr(out), scale, 0)
+                           _ptr(block_tables), _ptr(seq_lens), _ptr(out), scale, rope_theta)
         C.check(C.lib().vw_decode_step_host(self._h, ctypes.byref(a), _stream(stream)))
 
 
