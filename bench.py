@@ -264,8 +264,13 @@ def main():
     ap.add_argument("--workload", default=DEFAULT, choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="run only this many layers of the workload (a small case for ncu "
+                         "captures; the JSON line's config.layers says so)")
     args = ap.parse_args()
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.layers > 0:
+        w["L"] = min(args.layers, w["L"])
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

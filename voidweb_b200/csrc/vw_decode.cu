@@ -40,8 +40,11 @@
 //    page writes the new token's K/V row (quantised for FP8 pools) to its slot
 //    block_table[p/16]*16 + p%16, p = seq_len-1, in HBM and into the staged page.
 //  * FP8 pools.  Pages hold E4M3 codes plus one f32 scale per token per head;
-//    the consumer warp expands a page into binary16 tiles in shared memory and
-//    folds the scales into the scores and the probabilities.
+//    each lane of a consumer warp reads its share of the page's codes from the
+//    stage into registers and expands them into binary16 MMA fragments (the
+//    d order permuted so that a lane's fragments are runs of adjacent codes,
+//    V transposed with movmatrix); the scales fold into the scores and the
+//    probabilities.
 //
 // Every wait is bounded (vw_ptx.cuh); on timeout the kernel records
 // kDevErrTimeout and unwinds after draining its outstanding TMA loads.
@@ -62,6 +65,12 @@
 #endif
 #ifndef VW_DECODE_ISSUERS
 #define VW_DECODE_ISSUERS 4
+#endif
+#ifndef VW_DECODE_FP8_PRODUCERS
+#define VW_DECODE_FP8_PRODUCERS 2
+#endif
+#ifndef VW_DECODE_FP8_ISSUERS
+#define VW_DECODE_FP8_ISSUERS 1
 #endif
 #ifndef VW_DECODE_MAX_STAGES
 #define VW_DECODE_MAX_STAGES 16
@@ -88,13 +97,20 @@ namespace {
 
 constexpr int kConsumerWarps = VW_DECODE_WARPS;
 constexpr int kCtasPerSm = VW_DECODE_CTAS_PER_SM;
-constexpr int kIssuers = VW_DECODE_ISSUERS;           // producer lanes issuing loads
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kProducerWarp = kConsumerWarps;
+// Issuing lanes per producer warp, and producer warps.  The lanes of one warp
+// that issue copies with different operands run them one after another, so an
+// FP8 page-head (a tensor copy and a scale copy) issues faster from one lane in
+// each of two warps than from four lanes of one warp.
+constexpr int kIssuers = VW_DECODE_ISSUERS;
+constexpr int kFp8ProducerWarps = VW_DECODE_FP8_PRODUCERS;
+constexpr int kFp8Issuers = VW_DECODE_FP8_ISSUERS;
 constexpr int kQSlots = 4;                            // query tiles in flight (one per segment)
 constexpr int kMaxStages = VW_DECODE_MAX_STAGES;
 // per-CTA shared memory: an SM holds 228 KB and reserves 1 KB per resident CTA
 constexpr int kSmemPerCta = (233472 / kCtasPerSm) - 1024;
+// 2-byte pages feed ldmatrix in place from the stage, [CHUNKS][32 rows][128 B]
+// (column stride 4096 B); FP8 pages are read as codes straight into registers
+constexpr int kStageColumn = 4096;
 constexpr float kRescaleThreshold = 8.0f;             // log2 units: p <= 2^8 vs a stale max
 
 __host__ __device__ constexpr int align_up_c(int x, int a) { return (x + a - 1) / a * a; }
@@ -104,6 +120,10 @@ template <int D_, int NT_, int KV_, int IO_>
 struct Traits {
     static constexpr int D = D_, NT = NT_, KV = KV_, IO = IO_;
     static constexpr int W = kConsumerWarps;
+    static constexpr int PW = KV_ == kFP8 ? kFp8ProducerWarps : 1;   // producer warps W..W+PW-1
+    static constexpr int IPW = KV_ == kFP8 ? kFp8Issuers : kIssuers;  // issuing lanes per producer warp
+    static constexpr int NI = PW * IPW;                               // issuers in all
+    static constexpr int THREADS = (W + PW) * 32;
     static constexpr int G = 8 * NT;                         // padded query heads per KV head
     static constexpr int EB = KV == kFP8 ? 1 : 2;            // pool element bytes
     static constexpr int ROW = D * EB;                       // bytes of one token row
@@ -113,27 +133,27 @@ struct Traits {
     static constexpr bool MMA_BF16 = KV == kBF16;            // FP8 pages compute in f16
     static constexpr int KT = D / 16;                        // k-steps of Q K^T
     static constexpr int MT = D / 16;                        // d-tiles of V^T P^T
-    // FP8: per-warp f16 tile of half a page-head (16 rows: K, then V), laid out
-    // [2 columns][16 rows][128 B]; 2-byte pages are read in place from the stage
-    static constexpr int CTILE = KV == kFP8 ? 16 * D * 2 : 0;
-    static constexpr int TCOL = KV == kFP8 ? 2048 : 4096;    // column stride of the MMA tile
-    static constexpr int VROW = KV == kFP8 ? 0 : 16;         // first V row in the MMA tile
-    static constexpr int MERGE = W * G * (D + 2) * 4 + (W + 2) * G * 4;
+    // FP8 merge rows of D + 4 floats: a warp's stores of its O^T fragments
+    // (lanes 4g+c hold query heads 2c, 2c+1, d values 32 apart) then fall on 32
+    // different banks.  2-byte pages keep rows of D (a 4-way conflict measured
+    // cheaper than the padded rows).
+    static constexpr int MROW = KV == kFP8 ? D + 4 : D;
+    static constexpr int MERGE = W * G * (MROW + 2) * 4 + (W + 2) * G * 4;
     static constexpr int QTILE = G * D * 2;
     static constexpr int QSLOT = QTILE + 2 * D * 2;          // + the new token's K and V rows
     static constexpr int PFX = align_up_c(2 * (kMaxBatchPerLaunch + 1) * 4, 128);
-    static constexpr int FIXED = W * CTILE + align_up_c(MERGE, 1024) +
-                                 align_up_c(kQSlots * QSLOT, 1024) + PFX + 2048;
+    static constexpr int FIXED = align_up_c(MERGE, 1024) +
+                                 align_up_c(kQSlots * QSLOT, 1024) + PFX + PW * 1024 + 1024;
     static constexpr int BUDGET = kSmemPerCta - 1024 /* base alignment slack */ -
                                   (SCAL ? 1024 : 0) /* scale ring alignment */;
     // Stage count: as many as fit, rounded down to a multiple of the consumer
-    // warps and of the issuing lanes.  Page i lives in stage i % S, is issued by
-    // lane i % kIssuers and consumed by warp i % W; with S a multiple of both,
-    // every stage is filled by one lane and drained by one warp, each in page
-    // order.  That is what the mbarrier parity waits require: a parity wait can
-    // only tell the current phase from the one before it, so no waiter may ever
-    // run two phases ahead of a barrier.
-    static constexpr int LCM_WI = W * kIssuers / gcd_c(W, kIssuers);
+    // warps and of the issuers.  Page i lives in stage i % S, is issued by
+    // issuer i % NI (lane k / PW of producer warp k % PW) and consumed by warp
+    // i % W; with S a multiple of both, every stage is filled by one lane and
+    // drained by one warp, each in page order.  That is what the mbarrier parity
+    // waits require: a parity wait can only tell the current phase from the one
+    // before it, so no waiter may ever run two phases ahead of a barrier.
+    static constexpr int LCM_WI = W * NI / gcd_c(W, NI);
     static constexpr int S_FIT = (BUDGET - FIXED) / (STAGE + SCAL) > kMaxStages
                                      ? kMaxStages : (BUDGET - FIXED) / (STAGE + SCAL);
     static constexpr int S = S_FIT / LCM_WI * LCM_WI;
@@ -148,10 +168,10 @@ struct Traits {
     static constexpr int MIN_CTAS = (NT == 1 && KV != kFP8) ? 3 : 2;
     static_assert(CHUNKS >= 1, "row must be at least 128 bytes");
     static_assert(S >= 4, "too few pipeline stages");
-    static_assert(S % W == 0 && S % kIssuers == 0, "stage ownership needs S % W == S % issuers == 0");
-    static_assert(32 % kIssuers == 0, "issuing lanes must divide the 32-page batch");
+    static_assert(S % W == 0 && S % NI == 0, "stage ownership needs S % W == S % issuers == 0");
+    static_assert(32 % NI == 0 && IPW <= 32, "issuers must divide the 32-page batch");
     static_assert(SMEM <= kSmemPerCta, "shared memory over the per-CTA limit");
-    static_assert(STAGE % 1024 == 0 && CTILE % 1024 == 0, "1024-B tile alignment");
+    static_assert(STAGE % 1024 == 0, "1024-B tile alignment");
 };
 
 // Page as the producer publishes it to its issuing lanes: TMA row of its first
@@ -166,15 +186,14 @@ struct PageInfo {
 struct Smem {
     uint8_t* stages;     // [S][STAGE]
     float* scal;         // [S][32] FP8 scales (K 16, V 16)
-    uint8_t* ctile;      // FP8 only: [W][CTILE]
-    float* mo;           // [W][G][D]
+    float* mo;           // [W][G][MROW]
     float* mm;           // [W][G]
     float* ml;           // [W][G]
     float* mf;           // [W][G] warp weights, then [G] max, [G] sum
     uint8_t* qring;      // [kQSlots][QSLOT]: [G][D] query rows, then new K, new V rows (io dtype)
     int* pfx;            // [B+1] exclusive prefix of pages per sequence
     int* nzp;            // [B+1] exclusive prefix of sequences with pages
-    PageInfo* pinfo;     // [2][32] producer batches
+    PageInfo* pinfo;     // [PW][2][32] producer batches, one pair per producer warp
     uint64_t* full;      // [S]
     uint64_t* empty;     // [S]
     uint64_t* qfull;     // [kQSlots]
@@ -188,9 +207,8 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     uint8_t* p = base;
     s.stages = p; p += T::S * T::STAGE;
     s.scal = reinterpret_cast<float*>(p); p += align_up_c(T::S * T::SCAL, 1024);
-    s.ctile = p; p += T::W * T::CTILE;
     s.mo = reinterpret_cast<float*>(p);
-    s.mm = s.mo + T::W * T::G * T::D;
+    s.mm = s.mo + T::W * T::G * T::MROW;
     s.ml = s.mm + T::W * T::G;
     s.mf = s.ml + T::W * T::G;
     p += align_up_c(T::MERGE, 1024);
@@ -198,7 +216,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     s.pfx = reinterpret_cast<int*>(p);
     s.nzp = s.pfx + (kMaxBatchPerLaunch + 1);
     p += T::PFX;
-    s.pinfo = reinterpret_cast<PageInfo*>(p); p += 1024;
+    s.pinfo = reinterpret_cast<PageInfo*>(p); p += T::PW * 1024;
     s.full = reinterpret_cast<uint64_t*>(p);
     s.empty = s.full + T::S;
     s.qfull = s.empty + T::S;
@@ -350,10 +368,17 @@ __device__ __forceinline__ Resolved resolve_page(const DecodeParams& p, const Sm
     return r;
 }
 
+// Producer warp pw (0 .. PW-1): resolves every page of the range into its own
+// record buffer, and its lanes 0 .. IPW-1 issue the pages of issuers
+// lane * PW + pw.  Lane 0 of warp 0 also issues the query tiles, in segment
+// order.
 template <class T>
 __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const Smem& sm,
-                         int begin, int n, int first_ord, uint64_t deadline) {
+                         int begin, int n, int first_ord, int pw, uint64_t deadline) {
     const int lane = threadIdx.x & 31;
+    PageInfo* const mine = sm.pinfo + pw * 64;
+    const int k_me = lane * T::PW + pw;             // issuer number (lane < IPW)
+    const bool qlane = pw == 0 && lane == 0;         // issues the query tiles
     const uint32_t Hkv = p.Hkv;
     const uint32_t qbytes = p.group * T::D * 2;
     const uint8_t* qbase = reinterpret_cast<const uint8_t*>(p.q);
@@ -374,7 +399,7 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
             else
                 set_err(p.err, kDevErrBlockId);     // negative row: TMA zero-fills the tile
         }
-        sm.pinfo[buf * 32 + lane] = pi;
+        mine[buf * 32 + lane] = pi;
     };
 
     // Issue page ii (this lane owns its stage) into stage ii % S.
@@ -422,13 +447,13 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     // nor these pages); the query tiles wait for it.
     // (at most the first batch: only its 32 page records are published yet)
     const int early_n = (p.flags & kDecodeEarlyPages) ? min(min(T::S, 32), n) : 0;
-    if (lane < kIssuers)
-        for (int j = lane; j < early_n; j += kIssuers) issue_page(j, sm.pinfo[j]);
-    if (early_n > 0) {
+    if (lane < T::IPW)
+        for (int j = k_me; j < early_n; j += T::NI) issue_page(j, mine[j]);
+    if (early_n > 0 && pw == 0) {
         // warm L2 with the query tiles (and new K/V rows) of the first batch's
         // segments: the predecessor may still write them, but L2 is where that
         // write lands, so the bulk copies after the wait find them there anyway
-        const PageInfo pi = sm.pinfo[lane];
+        const PageInfo pi = mine[lane];
         if (lane < n && pi.qseg >= 0) {
             bulk_prefetch_l2(qbase + (size_t)pi.qrow * T::D * 2, qbytes);
             if (pi.kvrow >= 0) {
@@ -442,14 +467,15 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     for (int i0 = 0; i0 < n; i0 += 32) {
         const Resolved nxt = resolve_page(p, sm, begin, first_ord, i0 + 32 + lane, n);
         const int m = min(32, n - i0);
-        if (lane < kIssuers) {
-            // lane 0 scans every page of the batch for segment starts so that query
-            // tiles are issued in segment order by one thread (the query ring's
-            // parity waits need that); each lane issues the pages of its own stages
-            for (int j = lane == 0 ? 0 : lane; j < m && ok; j += lane == 0 ? 1 : kIssuers) {
+        if (lane < T::IPW) {
+            // the query lane scans every page of the batch for segment starts so
+            // that query tiles are issued in segment order by one thread (the query
+            // ring's parity waits need that); each issuer issues the pages of its
+            // own stages
+            for (int j = qlane ? 0 : k_me; j < m && ok; j += qlane ? 1 : T::NI) {
                 const int ii = i0 + j;
-                const PageInfo pi = sm.pinfo[buf * 32 + j];
-                if (lane == 0 && pi.qseg >= 0) {
+                const PageInfo pi = mine[buf * 32 + j];
+                if (qlane && pi.qseg >= 0) {
                     // a new segment starts here: its query tile
                     const int k = pi.qseg, qs = k % kQSlots;
                     if (k >= kQSlots &&
@@ -469,7 +495,7 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
                     }
                     segs_issued = k + 1;
                 }
-                if ((j % kIssuers) != lane || ii < early_n) continue;   // another lane's stage
+                if ((j % T::NI) != k_me || ii < early_n) continue;   // another issuer's stage
                 if (!issue_page(ii, pi)) {
                     ok = false;
                     break;
@@ -484,16 +510,17 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     }
     if (!ok) set_err(p.err, kDevErrTimeout);
     // Drain: never leave the CTA while a TMA or bulk load may still write its smem.
-    // lane 0 issued every query tile; share its count for the drain below
-    segs_issued = __shfl_sync(0xffffffffu, segs_issued, 0);
+    // (each warp waits for the pages its own lanes issued; the query lane for the
+    // query tiles)
     if (lane == 0) {
         for (int ii = n > T::S ? n - T::S : 0; ii < n; ++ii) {
+            if ((ii % T::NI) % T::PW != pw) continue;
             if (!mbar_wait(&sm.full[ii % T::S], (ii / T::S) & 1, deadline)) {
                 set_err(p.err, kDevErrTimeout);
                 break;
             }
         }
-        for (int k = segs_issued > kQSlots ? segs_issued - kQSlots : 0; k < segs_issued; ++k) {
+        for (int k = segs_issued > kQSlots ? segs_issued - kQSlots : 0; qlane && k < segs_issued; ++k) {
             if (!mbar_wait(&sm.qfull[k % kQSlots], (k / kQSlots) & 1, deadline)) {
                 set_err(p.err, kDevErrTimeout);
                 break;
@@ -564,10 +591,13 @@ __device__ __forceinline__ void rope_pair(float& xr, float& xi, int d, int D, fl
     xi = i;
 }
 
-// Query fragments (B operand of S^T = K Q^T) from the staged query tile.  A
-// lane's fragments hold elements d and d + D/2 (k-steps kt and kt + KT/2), so
-// with rope_theta > 0 the rotation of the query heads at position pos happens
-// here in registers, rounded to the io type as a separate RoPE pass would.
+// Query fragments (B operand of S^T = K Q^T) from the staged query tile.
+// 2-byte pages: a lane's fragments hold elements d and d + D/2 (k-steps kt and
+// kt + KT/2), so with rope_theta > 0 the rotation of the query heads at
+// position pos happens here in registers, rounded to the io type as a separate
+// RoPE pass would.  FP8 pages: k-step kt of lane c = lane%4 holds elements
+// 32c+4kt .. 32c+4kt+3 (the order of the K fragments, see Fp8Codes), so the
+// RoPE partner d +- D/2 of an element is in lane c ^ 2.
 template <class T>
 __device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qtile, int lane,
                                        float pos, uint32_t (&qf)[T::NT][T::KT][2]) {
@@ -576,38 +606,60 @@ __device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qti
         const int j = nt * 8 + (lane >> 2);
         const bool live = j < (int)p.group;
         const uint8_t* row = qtile + (live ? j : 0) * T::D * 2;
+        if constexpr (T::KV == kFP8) {
+            const int c = lane & 3;
+            uint32_t w[16];
 #pragma unroll
-        for (int kt = 0; kt < T::KT; ++kt)
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
-                qf[nt][kt][hf] = live ? *reinterpret_cast<const uint32_t*>(row + d * 2) : 0u;
+            for (int u = 0; u < 4; ++u) {
+                const uint4 v = live ? *reinterpret_cast<const uint4*>(row + c * 64 + u * 16)
+                                     : make_uint4(0, 0, 0, 0);
+                w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
             }
-        if (p.rope_theta > 0.0f) {
+            if (p.rope_theta > 0.0f) {
+                const bool lo = c < 2;                  // elements below D/2
 #pragma unroll
-            for (int kt = 0; kt < T::KT / 2; ++kt)
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
-                    uint32_t& a = qf[nt][kt][hf];
-                    uint32_t& b = qf[nt][kt + T::KT / 2][hf];
-                    float ar = io_to_f32<T::IO>(a & 0xFFFFu), ai = io_to_f32<T::IO>(b & 0xFFFFu);
-                    float br = io_to_f32<T::IO>(a >> 16), bi = io_to_f32<T::IO>(b >> 16);
-                    rope_pair(ar, ai, d, T::D, p.rope_theta, pos);
-                    rope_pair(br, bi, d + 1, T::D, p.rope_theta, pos);
-                    a = (uint32_t)f32_to_io<T::IO>(ar) | ((uint32_t)f32_to_io<T::IO>(br) << 16);
-                    b = (uint32_t)f32_to_io<T::IO>(ai) | ((uint32_t)f32_to_io<T::IO>(bi) << 16);
+                for (int m = 0; m < 16; ++m) {
+                    const uint32_t other = __shfl_xor_sync(0xffffffffu, w[m], 2);
+                    const uint32_t rw = lo ? w[m] : other, iw = lo ? other : w[m];
+                    float r0 = io_to_f32<T::IO>(rw & 0xFFFFu), i0 = io_to_f32<T::IO>(iw & 0xFFFFu);
+                    float r1 = io_to_f32<T::IO>(rw >> 16), i1 = io_to_f32<T::IO>(iw >> 16);
+                    const int d = (c & 1) * 32 + 2 * m;   // index of the lower element
+                    rope_pair(r0, i0, d, T::D, p.rope_theta, pos);
+                    rope_pair(r1, i1, d + 1, T::D, p.rope_theta, pos);
+                    w[m] = lo ? ((uint32_t)f32_to_io<T::IO>(r0) | ((uint32_t)f32_to_io<T::IO>(r1) << 16))
+                              : ((uint32_t)f32_to_io<T::IO>(i0) | ((uint32_t)f32_to_io<T::IO>(i1) << 16));
                 }
-        }
-        if constexpr (T::KV == kFP8 && T::IO == kBF16) {
-            // pages compute in f16: convert the bf16 query pairs
+            }
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+                if constexpr (T::IO == kBF16)       // pages compute in f16
+                    w[m] = pack2<false>(bf16_bits_to_f32(w[m] & 0xFFFFu), bf16_bits_to_f32(w[m] >> 16));
+                qf[nt][m >> 1][m & 1] = w[m];
+            }
+        } else {
 #pragma unroll
             for (int kt = 0; kt < T::KT; ++kt)
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
-                    const uint32_t v = qf[nt][kt][hf];
-                    qf[nt][kt][hf] = pack2<false>(bf16_bits_to_f32(v & 0xFFFFu), bf16_bits_to_f32(v >> 16));
+                    const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
+                    qf[nt][kt][hf] = live ? *reinterpret_cast<const uint32_t*>(row + d * 2) : 0u;
                 }
+            if (p.rope_theta > 0.0f) {
+#pragma unroll
+                for (int kt = 0; kt < T::KT / 2; ++kt)
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const int d = kt * 16 + hf * 8 + 2 * (lane & 3);
+                        uint32_t& a = qf[nt][kt][hf];
+                        uint32_t& b = qf[nt][kt + T::KT / 2][hf];
+                        float ar = io_to_f32<T::IO>(a & 0xFFFFu), ai = io_to_f32<T::IO>(b & 0xFFFFu);
+                        float br = io_to_f32<T::IO>(a >> 16), bi = io_to_f32<T::IO>(b >> 16);
+                        rope_pair(ar, ai, d, T::D, p.rope_theta, pos);
+                        rope_pair(br, bi, d + 1, T::D, p.rope_theta, pos);
+                        a = (uint32_t)f32_to_io<T::IO>(ar) | ((uint32_t)f32_to_io<T::IO>(br) << 16);
+                        b = (uint32_t)f32_to_io<T::IO>(ai) | ((uint32_t)f32_to_io<T::IO>(bi) << 16);
+                    }
+            }
         }
     }
 }
@@ -674,32 +726,49 @@ __device__ __forceinline__ void zero_tail(uint8_t* stage, int valid, int lane) {
     }
 }
 
-// FP8: expand rows row0..row0+15 of the staged page-head of codes [32 rows]
-// [128 B] (K: row0 = 0, V: row0 = 16) into this warp's f16 tile [2 columns]
-// [16 rows][128 B], 128-B swizzled like a 2-byte stage.
-template <class T>
-__device__ __forceinline__ void dequant_half(const uint8_t* stage, uint8_t* ctile, int row0, int lane) {
+// FP8 page-head fragments, read as codes straight from the stage.  Lane
+// (g = lane/4, c = lane%4) takes the 32 codes 32c .. 32c+31 of token rows g and
+// g+8 of K (stage rows 0-15) and of V (rows 16-31): two 16-B units per row,
+// 128-B swizzled.  The order of the reduction over d inside a k-step of
+// S^T = K Q^T is free, so k-step kt uses codes 4kt .. 4kt+3 of each lane's run
+// (fragment columns 2c+e and 2c+8+e hold d = 32c+4kt+e and 32c+4kt+2+e) and
+// load_q orders the query pairs the same way.  For O^T = V^T P^T the output
+// rows are permuted instead: the code pair j (d = 32c+2j, +1) of rows g and
+// g+8 forms 8x8 blocks that movmatrix transposes into V^T fragments, so row r
+// of d-tile mt of O^T is d = 32*(r%8/2) + 4*mt + 2*(r/8) + r%2 (fp8_out_d).
+struct Fp8Codes {
+    uint4 k[2][2], v[2][2];     // [token row g, g+8][16-B unit]
+};
+
+__device__ __forceinline__ void load_fp8_codes(const uint8_t* st, int lane, Fp8Codes& f) {
+    const int g = lane >> 2, c = lane & 3;
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-        const int r = it * 4 + (lane >> 3), row = row0 + r, c16 = lane & 7;
-        const uint4 w = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c16 ^ (row & 7)) << 4));
-        uint4 lo, hi;
-        lo.x = fp8x2_to_f16x2_scaled(w.x, 0); lo.y = fp8x2_to_f16x2_scaled(w.x, 1);
-        lo.z = fp8x2_to_f16x2_scaled(w.y, 0); lo.w = fp8x2_to_f16x2_scaled(w.y, 1);
-        hi.x = fp8x2_to_f16x2_scaled(w.z, 0); hi.y = fp8x2_to_f16x2_scaled(w.z, 1);
-        hi.z = fp8x2_to_f16x2_scaled(w.w, 0); hi.w = fp8x2_to_f16x2_scaled(w.w, 1);
-        // codes c16*16 .. +15 are f16 elements of column c16/4, 16-B units 2*(c16%4), +1.
-        // The 8 lanes of a row (one quarter-warp per store) cover both columns;
-        // column-1 lanes store their odd unit first so that each store touches 8
-        // different 16-B bank groups.
-        uint8_t* base = ctile + (c16 >> 2) * 2048 + r * 128;
-        const int u = (c16 & 3) * 2;
-        const bool odd_first = (c16 >> 2) != 0;
-        const uint4 first = odd_first ? hi : lo, second = odd_first ? lo : hi;
-        const int u1 = odd_first ? u + 1 : u, u2 = odd_first ? u : u + 1;
-        *reinterpret_cast<uint4*>(base + ((u1 ^ (r & 7)) << 4)) = first;
-        *reinterpret_cast<uint4*>(base + ((u2 ^ (r & 7)) << 4)) = second;
-    }
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int off = (g + 8 * rr) * 128 + (((2 * c + hh) ^ g) << 4);
+            f.k[rr][hh] = *reinterpret_cast<const uint4*>(st + off);
+            f.v[rr][hh] = *reinterpret_cast<const uint4*>(st + 16 * 128 + off);
+        }
+}
+
+// Word i (0..7) of a lane's 32-byte run held as two uint4.
+__device__ __forceinline__ uint32_t run_word(const uint4 (&u)[2], int i) {
+    const uint4& h = u[i >> 2];
+    const int k = i & 3;
+    return k == 0 ? h.x : k == 1 ? h.y : k == 2 ? h.z : h.w;
+}
+
+__host__ __device__ __forceinline__ int fp8_out_d(int r, int mt) {
+    return 32 * ((r & 7) >> 1) + 4 * mt + 2 * (r >> 3) + (r & 1);
+}
+
+// Column of output element d in a merge row.  The FP8 fragments put d values
+// 32 apart in one store; flipping bits 1-2 of d by its 32-block keeps them on
+// different banks (a permutation inside each block of 32).
+template <class T>
+__device__ __forceinline__ int merge_col(int d) {
+    return T::KV == kFP8 ? d ^ (((d >> 5) & 3) << 1) : d;
 }
 
 template <class T>
@@ -719,7 +788,6 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
     const int v_tok = (lane & 7) + ((mi >> 1) << 3), v_hs = mi & 1;
     const int t0 = lane >> 2, t1 = t0 + 8;
 
-    uint8_t* my_ctile = sm.ctile + warp * T::CTILE;
     bool alive = true;
     int seg_k = 0;
 
@@ -822,15 +890,16 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 __syncwarp();
             }
             float ks0 = 1.0f, ks1 = 1.0f, vs0 = 1.0f, vs1 = 1.0f;
-            uint32_t tbase;
+            const uint32_t tbase = smem_u32(st);
+            Fp8Codes fc;
             if constexpr (T::KV == kFP8) {
+                // this lane's codes and scales are all the page-head it needs:
+                // the stage goes back to the producer before any math
                 ks0 = sc[t0] * 256.0f; ks1 = sc[t1] * 256.0f;
                 vs0 = sc[16 + t0]; vs1 = sc[16 + t1];
-                dequant_half<T>(st, my_ctile, 0, lane);      // K rows
+                load_fp8_codes(st, lane, fc);
                 __syncwarp();
-                tbase = smem_u32(my_ctile);
-            } else {
-                tbase = smem_u32(st);
+                if (lane == 0) mbar_arrive(&sm.empty[s]);
             }
 
             // ---- S^T = K Q^T  (16 tokens x 8*NT heads), two independent chains
@@ -842,9 +911,15 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
 #pragma unroll
             for (int kt = 0; kt < T::KT; ++kt) {
                 uint32_t a0, a1, a2, a3;
-                const uint32_t addr = tbase + (kt >> 2) * T::TCOL + k_tok * 128 +
-                                      ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4);
-                ldsm_x4(addr, a0, a1, a2, a3);
+                if constexpr (T::KV == kFP8) {
+                    const uint32_t w0 = run_word(fc.k[0], kt), w1 = run_word(fc.k[1], kt);
+                    a0 = fp8x2_to_f16x2_scaled(w0, 0); a1 = fp8x2_to_f16x2_scaled(w1, 0);
+                    a2 = fp8x2_to_f16x2_scaled(w0, 1); a3 = fp8x2_to_f16x2_scaled(w1, 1);
+                } else {
+                    const uint32_t addr = tbase + (kt >> 2) * kStageColumn + k_tok * 128 +
+                                          ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4);
+                    ldsm_x4(addr, a0, a1, a2, a3);
+                }
 #pragma unroll
                 for (int nt = 0; nt < T::NT; ++nt) {
                     if (kt & 1) mma_16816<T::MMA_BF16>(sb[nt], a0, a1, a2, a3, qf[nt][kt][0], qf[nt][kt][1]);
@@ -852,13 +927,6 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 }
             }
 
-            if constexpr (T::KV == kFP8) {
-                // the K half is in registers now: expand the V half into the tile
-                __syncwarp();
-                dequant_half<T>(st, my_ctile, 16, lane);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.empty[s]);   // stage no longer needed
-            }
 
             // ---- online softmax (log2 domain) with a lazily raised maximum
             const bool v0 = t0 < valid, v1 = t1 < valid;
@@ -909,13 +977,21 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 pb[nt][1] = movmatrix_t(pack2<T::MMA_BF16>(q10, q11));
             }
 
-            // ---- O^T += V^T P^T  (D x 8*NT); V rows start at row VROW of the tile
+            // ---- O^T += V^T P^T  (D x 8*NT); V is stage rows 16-31
 #pragma unroll
             for (int mt = 0; mt < T::MT; ++mt) {
                 uint32_t a0, a1, a2, a3;
-                const uint32_t addr = tbase + (mt >> 2) * T::TCOL + (T::VROW + v_tok) * 128 +
-                                      ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4);
-                ldsm_x4_t(addr, a0, a1, a2, a3);
+                if constexpr (T::KV == kFP8) {
+                    const uint32_t w0 = run_word(fc.v[0], mt), w1 = run_word(fc.v[1], mt);
+                    a0 = movmatrix_t(fp8x2_to_f16x2_scaled(w0, 0));
+                    a1 = movmatrix_t(fp8x2_to_f16x2_scaled(w0, 1));
+                    a2 = movmatrix_t(fp8x2_to_f16x2_scaled(w1, 0));
+                    a3 = movmatrix_t(fp8x2_to_f16x2_scaled(w1, 1));
+                } else {
+                    const uint32_t addr = tbase + (mt >> 2) * kStageColumn + (16 + v_tok) * 128 +
+                                          ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4);
+                    ldsm_x4_t(addr, a0, a1, a2, a3);
+                }
 #pragma unroll
                 for (int nt = 0; nt < T::NT; ++nt)
                     mma_16816<T::MMA_BF16>(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
@@ -929,7 +1005,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         // ---- merge the W warps' states for this segment
         if (ctid == 0 && x + cnt >= end) VW_TRACE(5, globaltimer());
         if (!alive && lane == 0) sm.flag[1] = 1;  // abort marker, read by all warps below
-        float* mo = sm.mo + warp * T::G * T::D;
+        float* mo = sm.mo + warp * T::G * T::MROW;
 #pragma unroll
         for (int nt = 0; nt < T::NT; ++nt) {
 #pragma unroll
@@ -940,11 +1016,13 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             const int j0 = nt * 8 + 2 * (lane & 3);
 #pragma unroll
             for (int mt = 0; mt < T::MT; ++mt) {
-                const int d = mt * 16 + (lane >> 2);
-                mo[j0 * T::D + d] = o[nt][mt][0];
-                mo[(j0 + 1) * T::D + d] = o[nt][mt][1];
-                mo[j0 * T::D + d + 8] = o[nt][mt][2];
-                mo[(j0 + 1) * T::D + d + 8] = o[nt][mt][3];
+                // O^T rows lane/4 and lane/4 + 8 of d-tile mt
+                const int dA = T::KV == kFP8 ? fp8_out_d(lane >> 2, mt) : mt * 16 + (lane >> 2);
+                const int dB = T::KV == kFP8 ? fp8_out_d((lane >> 2) + 8, mt) : dA + 8;
+                mo[j0 * T::MROW + merge_col<T>(dA)] = o[nt][mt][0];
+                mo[(j0 + 1) * T::MROW + merge_col<T>(dA)] = o[nt][mt][1];
+                mo[j0 * T::MROW + merge_col<T>(dB)] = o[nt][mt][2];
+                mo[(j0 + 1) * T::MROW + merge_col<T>(dB)] = o[nt][mt][3];
             }
             if (lane < 4) {
                 sm.mm[warp * T::G + j0] = mrun[nt][0];
@@ -987,7 +1065,8 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             const int j = idx / T::D, d = idx - j * T::D;
             float Os = 0.0f;
 #pragma unroll
-            for (int w = 0; w < W; ++w) Os += sm.mo[(w * T::G + j) * T::D + d] * sm.mf[w * T::G + j];
+            for (int w = 0; w < W; ++w)
+                Os += sm.mo[(w * T::G + j) * T::MROW + merge_col<T>(d)] * sm.mf[w * T::G + j];
             if (complete) {
                 out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
                     f32_to_io<T::IO>(Os / sm.mf[(W + 1) * T::G + j] * T::VFOLD);
@@ -1004,7 +1083,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
 }
 
 template <class T>
-__global__ void __launch_bounds__(kThreads, T::MIN_CTAS)
+__global__ void __launch_bounds__(T::THREADS, T::MIN_CTAS)
 decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -1047,22 +1126,23 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     if (planned) {
         const int* entry = p.plan + kPlanCta + (size_t)blockIdx.x * kPlanCtaInts;
         // (L2 reads: the plan is rewritten by later plan launches)
-        for (int i = threadIdx.x; i <= (int)p.B; i += kThreads) {
+        for (int i = threadIdx.x; i <= (int)p.B; i += T::THREADS) {
             sm.pfx[i] = __ldcg(p.plan + kPlanPfx + i);
             sm.nzp[i] = __ldcg(p.plan + kPlanNzp + i);
         }
-        if (warp == kProducerWarp) {
+        if (warp >= T::W) {
+            // every producer warp takes the first batch into its own buffer
             if (lane == 0) prefetch_tensormap(&tmap);
-            if (lane < 3) sm.flag[2 + lane] = __ldcg(entry + lane);
+            if (warp == T::W && lane < 3) sm.flag[2 + lane] = __ldcg(entry + lane);
             const int4 rec = __ldcg(reinterpret_cast<const int4*>(entry + 4) + lane);
             PageInfo pi;
             pi.kvrow = p.k_new != nullptr ? rec.x : -1;
             pi.row0 = rec.y >= 0 ? rec.y + (int)(p.layer * p.num_blocks * p.Hkv * 32u) : rec.y;
             pi.qseg = rec.z;
             pi.qrow = rec.w;
-            sm.pinfo[lane] = pi;
+            sm.pinfo[(warp - T::W) * 64 + lane] = pi;
         }
-    } else if (warp == kProducerWarp) {
+    } else if (warp == T::W) {
         if (lane == 0) prefetch_tensormap(&tmap);
         warp_prefixes(p.seq_lens, (int)p.B, (int)p.bt_stride, p.err, blockIdx.x == 0, sm.pfx, sm.nzp,
                       lane);
@@ -1082,8 +1162,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     }
     if (begin >= end) return;
 
-    if (warp == kProducerWarp) {
-        if (lane == 0) VW_TRACE(15, globaltimer());
+    if (warp >= T::W) {
+        if (warp == T::W && lane == 0) VW_TRACE(15, globaltimer());
         // ordinal of the first segment of this range among non-empty segments
         int first_ord;
         if (planned) {
@@ -1095,7 +1175,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         }
         DecodeParams pp = p;
         if (!early) pp.flags &= ~(kDecodePdl | kDecodeEarlyPages);   // already waited above
-        producer<T>(&tmap, pp, sm, begin, end - begin, first_ord, deadline);
+        producer<T>(&tmap, pp, sm, begin, end - begin, first_ord, T::PW == 1 ? 0 : warp - T::W,
+                    deadline);
     } else {
         if (early) {
             griddep_wait();            // q, k_new, v_new may come from the predecessor
@@ -1285,7 +1366,7 @@ cudaError_t launch_t(const DecodeLaunch& L) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(L.grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(T::THREADS);
     cfg.dynamicSmemBytes = T::SMEM;
     cfg.stream = L.stream;
     cudaLaunchAttribute attr[1];
