@@ -218,6 +218,44 @@ typedef struct {
 } vw_step_host_args;
 VW_API int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* args, void* stream);
 
+/* ---- Chunked prefill over the pool ------------------------------------------
+ * Replaces: launch_flash_attn_prefill (kernels/attention/flash_attention.bm:167-177,
+ * kernel flash_attention_fwd :31-106), which attends over contiguous K/V and
+ * ignores its block table.  Here the chunk of sequence b is the query tokens
+ * cu_seqlens[b] .. cu_seqlens[b+1]-1 at positions ctx_start[b] + i (the tokens
+ * before ctx_start[b] are already cached, e.g. a radix-matched prefix or an
+ * earlier chunk; scheduler/scheduler.bm:251-266 cuts prompts into chunks of
+ * up to 2048 tokens).  With k_new / v_new the chunk's own K/V rows are first
+ * appended to slots block_tables[b][p/16]*16 + p%16 (FP8 pools quantise them);
+ * then token i attends to keys 0 .. ctx_start[b]+i with VW_PREFILL_CAUSAL, or
+ * to all ctx_start[b] + n_b keys without it (the reference kernel has no mask).
+ * Pools of f16 / bf16 pages; FP8 pools take the append but the attention
+ * returns VW_ERR_UNSUPPORTED.  Device pointers, 16-byte aligned (the int
+ * arrays 4-byte). */
+typedef struct {
+    uint32_t layer;
+    uint32_t num_seqs;             /* B, at most the pool's max_batch */
+    uint32_t num_tokens;           /* T = cu_seqlens[B]: rows of q, k_new, v_new, out */
+    uint32_t num_q_heads;          /* multiple of num_kv_heads */
+    uint32_t block_table_stride;
+    uint32_t flags;                /* VW_PREFILL_* */
+    const void* q;                 /* [T][num_q_heads][head_dim] io dtype */
+    const void* k_new;             /* [T][num_kv_heads][head_dim] chunk rows, or NULL when the */
+    const void* v_new;             /*   pages already hold them */
+    const int32_t* cu_seqlens;     /* [B+1] chunk offsets, cu_seqlens[0] = 0, non-decreasing */
+    const int32_t* ctx_start;      /* [B] tokens cached before each chunk */
+    const uint32_t* block_tables;  /* [B][block_table_stride] */
+    void* out;                     /* [T][num_q_heads][head_dim] io dtype */
+    float scale;                   /* softmax scale; 0 means 1/sqrt(head_dim) (flash_attention.bm:174) */
+    float rope_theta;              /* with VW_PREFILL_ROPE: q and the chunk's K rows are rotated */
+} vw_prefill_args;
+
+#define VW_PREFILL_CAUSAL 0x1u     /* token i attends to keys 0 .. its own position */
+#define VW_PREFILL_ROPE 0x2u       /* RoPE (kernels/rope/rope.bm:22-52) at each token's position */
+#define VW_PREFILL_PDL 0x4u        /* launch as a programmatic dependent of the previous kernel */
+
+VW_API int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* args, void* stream);
+
 /* ---- Host block manager (engine/kv_cache.bm:29-164, C++ implementation) ---- */
 typedef struct vw_block_manager vw_block_manager;
 /* kv_cache.bm:41-58: free list 0..max_blocks, the next alloc pops the last. */
@@ -309,8 +347,8 @@ typedef struct {
  * attention (embedding, QKV/O projections, MLP, LM head) are outside this
  * library, so the caller binds the pool and the per-layer q / new K / new V
  * rows and the attention output buffer that voidweb_forward_pass reads and
- * writes (host, shapes as in vw_step_host_args, sequence order = descriptor
- * order).  The binding is process-wide. */
+ * writes (host, [L][rows][heads][head_dim] in the io dtype, one row per token
+ * of each descriptor, in descriptor order).  The binding is process-wide. */
 VW_API int32_t vw_forward_bind(vw_pool* pool, const void* q, const void* k_new, const void* v_new,
                         void* attn_out);
 /* Number of tokens already cached for seq_id (e.g. after a prefill done
@@ -319,13 +357,17 @@ VW_API int32_t vw_forward_bind(vw_pool* pool, const void* q, const void* k_new, 
 VW_API int32_t vw_forward_set_seq_len(uint64_t seq_id, uint32_t len);
 VW_API int32_t vw_forward_release(uint64_t seq_id);
 
-/* engine/ffi.bm:68,113: returns 0 on success.  For each decode descriptor
- * (num_tokens == 1, is_prefill == 0) the new token goes to position
- * len(seq_id) of the sequence, its host block list (block_ptr, num_blocks) is
- * the block table, attention covers len(seq_id)+1 tokens on every layer, and
- * len(seq_id) then grows by one.  Prefill descriptors return
- * VW_ERR_UNSUPPORTED (nothing runs); logits_out is not written (no LM head in
- * this library). */
+/* engine/ffi.bm:68,113: returns 0 on success.  Descriptor i owns num_tokens
+ * consecutive rows of the bound buffers (rows in descriptor order:
+ * [L][sum of num_tokens][heads][head_dim]).  A decode descriptor
+ * (is_prefill == 0, num_tokens == 1) puts its token at position len(seq_id)
+ * and attends over len(seq_id)+1 tokens; a prefill descriptor (is_prefill ==
+ * 1, the scheduler's chunk, scheduler/scheduler.bm:251-266) puts its
+ * num_tokens tokens at positions len(seq_id) .. len(seq_id)+num_tokens-1 and
+ * each attends causally over the cached tokens and the chunk up to itself.
+ * The host block list (block_ptr, num_blocks) is the block table; len(seq_id)
+ * then grows by num_tokens.  Prefill needs an f16 / bf16 pool.  logits_out is
+ * not written (no LM head in this library). */
 VW_API int32_t voidweb_forward_pass(const ForwardArgs* args);
 
 #ifdef __cplusplus

@@ -58,6 +58,10 @@ def lib() -> ctypes.CDLL:
                                            ctypes.c_int]),
             "vwo_paged_decode_f64": (i32, [vp, vp, vp, u32, vp, u32, vp, u32, vp, u32, f64, vp,
                                            ctypes.c_int]),
+            "vwo_paged_prefill_f32": (i32, [vp, vp, vp, u32, vp, u32, vp, vp, vp, u32, u32,
+                                            ctypes.c_int, f32, vp, ctypes.c_int]),
+            "vwo_paged_prefill_f64": (i32, [vp, vp, vp, u32, vp, u32, vp, vp, vp, u32, u32,
+                                            ctypes.c_int, f64, vp, ctypes.c_int]),
             "vwo_rope_apply": (None, [vp, u32, u32, u32, vp, f32, u32]),
             "vwo_rolling_hash": (u64, [u64, vp, u32]),
             "vwo_bm_new": (vp, [u32, u32]), "vwo_bm_delete": (None, [vp]),
@@ -212,6 +216,50 @@ def paged_decode_f64(g: Geom, data, scales, layer, q, Hq, block_tables, seq_lens
     if rc != 0:
         raise ValueError("oracle: seq_len 0")
     return out
+
+
+def prefill_slots(block_tables, cu_q, ctx_start) -> np.ndarray:
+    """Slot of every chunk token: token i of sequence b at position
+    p = ctx_start[b] + i - cu_q[b] lives at block_tables[b][p // 16] * 16 + p % 16
+    (the paging rule of flash_attention.bm:132-140)."""
+    bt = np.asarray(block_tables, dtype=np.int64)
+    cu = np.asarray(cu_q, dtype=np.int64)
+    cs = np.asarray(ctx_start, dtype=np.int64)
+    out = np.empty(int(cu[-1]), dtype=np.int64)
+    for b in range(cu.size - 1):
+        p = cs[b] + np.arange(cu[b + 1] - cu[b])
+        out[cu[b]:cu[b + 1]] = bt[b, p // 16] * 16 + p % 16
+    return out
+
+
+def _prefill(fn, g: Geom, data, scales, layer, q, Hq, block_tables, cu_q, ctx_start, causal,
+             scale, out, nthreads):
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    bt = np.ascontiguousarray(block_tables, dtype=np.uint32)
+    cu = np.ascontiguousarray(cu_q, dtype=np.int32)
+    cs = np.ascontiguousarray(ctx_start, dtype=np.int32)
+    rc = fn(ctypes.byref(g), _p(data), _p(scales), layer, _p(q), Hq, _p(cu), _p(cs), _p(bt),
+            bt.shape[1], cs.size, 1 if causal else 0, scale, _p(out), nthreads)
+    if rc != 0:
+        raise ValueError("oracle: chunk outside its block table")
+    return out
+
+
+def paged_prefill_f32(g: Geom, data, scales, layer, q, Hq, block_tables, cu_q, ctx_start, causal,
+                      scale, nthreads=0) -> np.ndarray:
+    """flash_attention.bm:31-106 over the pool (f32, the reference's tile order);
+    q [T][Hq][D] io bits -> out [T][Hq][D] io bits."""
+    out = np.zeros((int(np.asarray(cu_q)[-1]), Hq, g.head_dim), dtype=np.uint16)
+    return _prefill(lib().vwo_paged_prefill_f32, g, data, scales, layer, q, Hq, block_tables, cu_q,
+                    ctx_start, causal, scale, out, nthreads)
+
+
+def paged_prefill_f64(g: Geom, data, scales, layer, q, Hq, block_tables, cu_q, ctx_start, causal,
+                      scale, nthreads=0) -> np.ndarray:
+    """The same attention in fp64 with a two-pass softmax -> out [T][Hq][D] f64."""
+    out = np.zeros((int(np.asarray(cu_q)[-1]), Hq, g.head_dim), dtype=np.float64)
+    return _prefill(lib().vwo_paged_prefill_f64, g, data, scales, layer, q, Hq, block_tables, cu_q,
+                    ctx_start, causal, scale, out, nthreads)
 
 
 def rolling_hash(prev: int, tokens) -> int:

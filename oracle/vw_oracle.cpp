@@ -388,6 +388,133 @@ int vwo_paged_decode_f64(const vwo_geom* g, const void* data, const float* scale
 }
 
 // ---------------------------------------------------------------------------
+// Paged prefill attention
+// ---------------------------------------------------------------------------
+
+// kernels/attention/flash_attention.bm:31-106 (flash_attention_fwd) over the
+// pool: query token i of sequence b (rows cu_q[b] .. cu_q[b+1]-1 of q) sits
+// at position p = ctx_start[b] + i - cu_q[b] and attends, with `causal`, to
+// keys 0 .. p, else to all ctx_start[b] + n_b keys (the reference's seq_kv,
+// no mask).  f32 in the reference's order: keys in tiles of BLOCK_KV = 64
+// (:56-58), dot = sum_d q*k in order (:66-68), s = dot*scale (:69), per tile
+// the online update of :80-96.  One change: the running maximum is
+// max(m_i, tile max), where :80-81 take the tile max alone; the two agree
+// after the final division unless a later tile's maximum is far below an
+// earlier one (then the reference's alpha = exp(m_i - m_new) > 1 overflows),
+// and with a causal mask a tile can hold no key of a row at all, which the
+// reference's rule turns into 0/0.  q / out: [T][Hq][D] io dtype.  Returns
+// nonzero for a chunk past its block table row.
+int vwo_paged_prefill_f32(const vwo_geom* g, const void* data, const float* scales,
+                          uint32_t layer, const void* q, uint32_t Hq, const int32_t* cu_q,
+                          const int32_t* ctx_start, const uint32_t* bt, uint32_t bt_stride,
+                          uint32_t B, int causal, float scale, void* out, int nthreads) {
+    const uint32_t H = g->num_kv_heads, D = g->head_dim, G = Hq / H;
+    for (uint32_t b = 0; b < B; ++b)
+        if (ctx_start[b] < 0 || cu_q[b + 1] < cu_q[b] ||
+            (int64_t)ctx_start[b] + cu_q[b + 1] - cu_q[b] > (int64_t)bt_stride * 16)
+            return 1;
+    const int64_t T = cu_q[B];
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1)
+#endif
+    for (int64_t job = 0; job < T * (int64_t)Hq; ++job) {
+        const int64_t i = job / Hq;
+        const uint32_t hq = (uint32_t)(job % Hq), h = hq / G;
+        uint32_t b = 0;
+        while (b + 1 < B && cu_q[b + 1] <= i) ++b;
+        const int64_t p = ctx_start[b] + (i - cu_q[b]);
+        const int64_t total = ctx_start[b] + (cu_q[b + 1] - cu_q[b]);
+        const int64_t kend = causal ? p + 1 : total;
+        std::vector<float> qf(D), acc(D, 0.0f), st(64);
+        for (uint32_t d = 0; d < D; ++d) qf[d] = io_to_f32(q, ((size_t)i * Hq + hq) * D + d, g->io_dtype);
+        float m = -std::numeric_limits<float>::infinity(), l = 0.0f;
+        for (int64_t k0 = 0; k0 < kend; k0 += 64) {
+            float tmax = -std::numeric_limits<float>::infinity();
+            for (int64_t kv = 0; kv < 64; ++kv) {
+                const int64_t key = k0 + kv;
+                if (key >= kend) { st[kv] = -std::numeric_limits<float>::infinity(); continue; }
+                const uint32_t phys = bt[(size_t)b * bt_stride + key / 16];
+                const size_t rk = row_index(g, layer, phys, 0, h, (uint32_t)(key % 16));
+                float dot = 0.0f;
+                for (uint32_t d = 0; d < D; ++d) dot += qf[d] * kv_value(g, data, scales, rk, d);
+                st[kv] = dot * scale;
+                tmax = std::max(tmax, st[kv]);
+            }
+            const float m_new = std::max(m, tmax);
+            float exp_sum = 0.0f;
+            for (int64_t kv = 0; kv < 64; ++kv) exp_sum += std::exp(st[kv] - m_new);
+            const float alpha = std::exp(m - m_new);
+            for (uint32_t d = 0; d < D; ++d) {
+                float a = 0.0f;
+                for (int64_t kv = 0; kv < 64; ++kv) {
+                    const int64_t key = k0 + kv;
+                    if (key >= kend) continue;
+                    const uint32_t phys = bt[(size_t)b * bt_stride + key / 16];
+                    const size_t rv = row_index(g, layer, phys, 1, h, (uint32_t)(key % 16));
+                    a += std::exp(st[kv] - m_new) * kv_value(g, data, scales, rv, d);
+                }
+                acc[d] = acc[d] * alpha + a;
+            }
+            l = alpha * l + exp_sum;
+            m = m_new;
+        }
+        uint16_t* o = (uint16_t*)out + ((size_t)i * Hq + hq) * D;
+        for (uint32_t d = 0; d < D; ++d) o[d] = f32_to_io(acc[d] / l, g->io_dtype);
+    }
+    return 0;
+}
+
+// Same attention in fp64 with a two-pass softmax (the tolerance reference).
+// out: [T][Hq][D] f64.
+int vwo_paged_prefill_f64(const vwo_geom* g, const void* data, const float* scales,
+                          uint32_t layer, const void* q, uint32_t Hq, const int32_t* cu_q,
+                          const int32_t* ctx_start, const uint32_t* bt, uint32_t bt_stride,
+                          uint32_t B, int causal, double scale, double* out, int nthreads) {
+    const uint32_t H = g->num_kv_heads, D = g->head_dim, G = Hq / H;
+    for (uint32_t b = 0; b < B; ++b)
+        if (ctx_start[b] < 0 || cu_q[b + 1] < cu_q[b] ||
+            (int64_t)ctx_start[b] + cu_q[b + 1] - cu_q[b] > (int64_t)bt_stride * 16)
+            return 1;
+    const int64_t T = cu_q[B];
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1)
+#endif
+    for (int64_t job = 0; job < T * (int64_t)Hq; ++job) {
+        const int64_t i = job / Hq;
+        const uint32_t hq = (uint32_t)(job % Hq), h = hq / G;
+        uint32_t b = 0;
+        while (b + 1 < B && cu_q[b + 1] <= i) ++b;
+        const int64_t p = ctx_start[b] + (i - cu_q[b]);
+        const int64_t total = ctx_start[b] + (cu_q[b + 1] - cu_q[b]);
+        const int64_t kend = causal ? p + 1 : total;
+        std::vector<double> qf(D), sc((size_t)kend), acc(D, 0.0);
+        for (uint32_t d = 0; d < D; ++d) qf[d] = io_to_f32(q, ((size_t)i * Hq + hq) * D + d, g->io_dtype);
+        double mx = -std::numeric_limits<double>::infinity();
+        for (int64_t key = 0; key < kend; ++key) {
+            const uint32_t phys = bt[(size_t)b * bt_stride + key / 16];
+            const size_t rk = row_index(g, layer, phys, 0, h, (uint32_t)(key % 16));
+            double dot = 0.0;
+            for (uint32_t d = 0; d < D; ++d) dot += qf[d] * (double)kv_value(g, data, scales, rk, d);
+            sc[key] = dot * scale;
+            mx = std::max(mx, sc[key]);
+        }
+        double den = 0.0;
+        for (int64_t key = 0; key < kend; ++key) {
+            const uint32_t phys = bt[(size_t)b * bt_stride + key / 16];
+            const size_t rv = row_index(g, layer, phys, 1, h, (uint32_t)(key % 16));
+            const double w = std::exp(sc[key] - mx);
+            den += w;
+            for (uint32_t d = 0; d < D; ++d) acc[d] += w * (double)kv_value(g, data, scales, rv, d);
+        }
+        double* o = out + ((size_t)i * Hq + hq) * D;
+        for (uint32_t d = 0; d < D; ++d) o[d] = acc[d] / den;
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
 // BlockManager  (engine/kv_cache.bm:29-164)
 // ---------------------------------------------------------------------------
 

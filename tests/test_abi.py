@@ -46,6 +46,8 @@ _Static_assert(sizeof(ForwardArgs) == 52, "ForwardArgs");
 _Static_assert(offsetof(ForwardArgs, logits_out) == 44, "logits_out");
 _Static_assert(sizeof(vw_decode_args) == 80, "vw_decode_args");
 _Static_assert(sizeof(vw_pool_config) == 56, "vw_pool_config");
+_Static_assert(sizeof(vw_prefill_args) == 88, "vw_prefill_args");
+_Static_assert(offsetof(vw_prefill_args, q) == 24, "vw_prefill_args.q");
 int main(void) { return 0; }
 '''
     with tempfile.TemporaryDirectory() as d:
@@ -55,6 +57,8 @@ int main(void) { return 0; }
                         os.path.join(d, "t")], check=True)
     assert ctypes.sizeof(C.DecodeArgs) == 80
     assert ctypes.sizeof(C.PoolConfig) == 56
+    assert ctypes.sizeof(C.PrefillArgs) == 88
+    assert C.PrefillArgs.q.offset == 24
 
 
 def test_errors_cross_the_boundary_as_codes():
@@ -68,6 +72,7 @@ def test_errors_cross_the_boundary_as_codes():
     cfg = C.PoolConfig(1, 2, 128, 8, C.VW_BF16, C.VW_F16, 0, 8, 0, 0, None, None)
     assert L.vw_pool_create(ctypes.byref(cfg), ctypes.byref(h)) == C.VW_ERR_INVALID_ARG
     assert L.vw_paged_decode(None, None, None) == C.VW_ERR_INVALID_ARG
+    assert L.vw_paged_prefill(None, None, None) == C.VW_ERR_INVALID_ARG
     # the forward-pass symbol refuses to run without a bound pool
     args = C.ForwardArgs()
     assert L.voidweb_forward_pass(ctypes.byref(args)) != 0

@@ -22,10 +22,13 @@ VW_ERR_UNSUPPORTED = 2
 VW_ERR_CUDA = 3
 VW_ERR_OOM = 4
 VW_ERR_DEVICE_CHECK = 5
+# device error word bits (vw_pool_check)
+VW_DEV_ERR_BLOCK_ID, VW_DEV_ERR_SEQ_LEN, VW_DEV_ERR_TIMEOUT, VW_DEV_ERR_SLOT = 0x1, 0x2, 0x4, 0x8
 
 VW_F16, VW_BF16, VW_FP8_E4M3 = 0, 1, 2
 VW_FP8_REFERENCE, VW_FP8_OCP = 0, 1
 VW_DECODE_PDL, VW_DECODE_EARLY_PAGES, VW_DECODE_PLANNED, VW_DECODE_ROPE = 0x1, 0x2, 0x4, 0x8
+VW_PREFILL_CAUSAL, VW_PREFILL_ROPE, VW_PREFILL_PDL = 0x1, 0x2, 0x4
 
 DEV_ERR_BLOCK_ID, DEV_ERR_SEQ_LEN, DEV_ERR_TIMEOUT, DEV_ERR_SLOT = 1, 2, 4, 8
 
@@ -55,6 +58,13 @@ class StepHostArgs(ctypes.Structure):
                 ("rope_theta", f32)]
 
 
+class PrefillArgs(ctypes.Structure):
+    _fields_ = [("layer", u32), ("num_seqs", u32), ("num_tokens", u32), ("num_q_heads", u32),
+                ("block_table_stride", u32), ("flags", u32), ("q", vp), ("k_new", vp),
+                ("v_new", vp), ("cu_seqlens", vp), ("ctx_start", vp), ("block_tables", vp),
+                ("out", vp), ("scale", f32), ("rope_theta", f32)]
+
+
 class SeqDescriptor(ctypes.Structure):
     """engine/ffi.bm:15-24 (#[repr(C)] #[packed], 33 bytes)."""
     _pack_ = 1
@@ -80,6 +90,7 @@ SIGNATURES = {
     "vw_pool_check": (i32, [vp, ctypes.POINTER(u32)]),
     "vw_kv_append": (i32, [vp, u32, vp, vp, vp, u32, vp]),
     "vw_paged_decode": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
+    "vw_paged_prefill": (i32, [vp, ctypes.POINTER(PrefillArgs), vp]),
     "vw_decode_plan": (i32, [vp, vp, vp, u32, u32, u32, vp]),
     "vw_paged_decode_static": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
     "vw_block_copy": (i32, [vp, vp, u32, vp]),

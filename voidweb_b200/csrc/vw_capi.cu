@@ -101,9 +101,11 @@ struct vw_pool {
     const void* plan_tables = nullptr;
     const void* plan_lens = nullptr;
     uint32_t plan_seqs = 0, plan_stride = 0, plan_q_heads = 0;
-    // staging for vw_decode_step_host (grow-only)
+    // staging for vw_decode_step_host and for the forward pass's prefill (grow-only)
     uint8_t* stage = nullptr;
     size_t stage_bytes = 0;
+    uint8_t* pstage = nullptr;
+    size_t pstage_bytes = 0;
     cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
     std::vector<cudaEvent_t> ev_in, ev_done;
     cudaEvent_t ev_entry = nullptr, ev_exit = nullptr;
@@ -119,6 +121,7 @@ void pool_free_all(vw_pool* p) {
     if (p->plan) cudaFree(p->plan);
     if (p->err) cudaFree(p->err);
     if (p->stage) cudaFree(p->stage);
+    if (p->pstage) cudaFree(p->pstage);
     if (p->s_h2d) cudaStreamDestroy(p->s_h2d);
     if (p->s_d2h) cudaStreamDestroy(p->s_d2h);
     for (auto e : p->ev_in) cudaEventDestroy(e);
@@ -390,6 +393,93 @@ int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream)
     return decode_launch(pool, args, static_cast<cudaStream_t>(stream));
 }
 
+// ---------------------------------------------------------------------------
+// Chunked prefill: launch_flash_attn_prefill (kernels/attention/flash_attention.bm:167-177)
+// over the pool's pages.
+// ---------------------------------------------------------------------------
+
+static int32_t prefill_validate(const vw_pool* pool, const vw_prefill_args* a) {
+    if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: null argument");
+    const PoolGeom& g = pool->geom;
+    if (a->flags & ~(uint32_t)(VW_PREFILL_CAUSAL | VW_PREFILL_ROPE | VW_PREFILL_PDL))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: unknown flags 0x%x", a->flags);
+    if ((a->flags & VW_PREFILL_ROPE) && !(a->rope_theta > 1.0f && std::isfinite(a->rope_theta)))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: VW_PREFILL_ROPE needs a finite rope_theta > 1");
+    if (a->layer >= g.num_layers)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: layer %u >= %u", a->layer, g.num_layers);
+    if (a->num_seqs > pool->cfg.max_batch || a->num_seqs > (uint32_t)kMaxBatchPerLaunch)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: num_seqs %u > max_batch %u", a->num_seqs,
+                    pool->cfg.max_batch);
+    if (a->num_q_heads == 0 || a->num_q_heads % g.num_kv_heads != 0 || a->num_q_heads > 65535)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: num_q_heads %u not a multiple of %u",
+                    a->num_q_heads, g.num_kv_heads);
+    if (a->block_table_stride == 0)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: block_table_stride must be > 0");
+    if (a->num_tokens > (1u << 24))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: num_tokens %u too large", a->num_tokens);
+    if (!a->q || !a->cu_seqlens || !a->ctx_start || !a->block_tables || !a->out)
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: null device pointer");
+    if ((a->k_new == nullptr) != (a->v_new == nullptr))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: k_new and v_new go together");
+    if (!aligned(a->q, 16) || !aligned(a->out, 16) || !aligned(a->cu_seqlens, 4) ||
+        !aligned(a->ctx_start, 4) || !aligned(a->block_tables, 4) ||
+        (a->k_new && (!aligned(a->k_new, 16) || !aligned(a->v_new, 16))))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: misaligned pointer");
+    if (!(a->scale >= 0.0f) || std::isinf(a->scale))
+        return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: bad scale");
+    if (g.kv_kind == kFP8)
+        return fail(VW_ERR_UNSUPPORTED, "vw_paged_prefill: FP8 pools are not supported by the prefill attention");
+    return VW_OK;
+}
+
+int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) {
+    int32_t rc = prefill_validate(pool, a);
+    if (rc != VW_OK) return rc;
+    if (a->num_seqs == 0 || a->num_tokens == 0) return VW_OK;
+    DeviceScope ds(pool->cfg.device);
+    const PoolGeom& g = pool->geom;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    const float theta = (a->flags & VW_PREFILL_ROPE) ? a->rope_theta : 0.0f;
+    if (a->k_new) {
+        e = launch_prefill_append(g, pool->data, pool->scales, a->layer, a->k_new, a->v_new,
+                                  a->cu_seqlens, a->ctx_start, a->block_tables, a->block_table_stride,
+                                  a->num_seqs, a->num_tokens, theta, pool->err, s);
+        if (e != cudaSuccess) return cuda_fail(e, "vw_paged_prefill: append launch");
+    }
+    PrefillLaunch L{};
+    PrefillParams& p = L.p;
+    p.q = a->q;
+    p.out = a->out;
+    p.cu_q = a->cu_seqlens;
+    p.ctx_start = a->ctx_start;
+    p.block_tables = a->block_tables;
+    p.err = pool->err;
+    p.B = a->num_seqs;
+    p.T = a->num_tokens;
+    p.Hq = a->num_q_heads;
+    p.Hkv = g.num_kv_heads;
+    p.group = a->num_q_heads / g.num_kv_heads;
+    p.num_blocks = g.num_blocks;
+    p.layer = a->layer;
+    p.bt_stride = a->block_table_stride;
+    p.causal = (a->flags & VW_PREFILL_CAUSAL) ? 1u : 0u;
+    // the attention of a chunk waits for its append (same stream); the PDL flag
+    // lets the first launch of the two overlap its predecessor
+    p.flags = (a->flags & VW_PREFILL_PDL) && !a->k_new ? kDecodePdl : 0u;
+    const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.rope_theta = theta;
+    L.tmap = &pool->tmap;
+    L.head_dim = g.head_dim;
+    L.kv_kind = g.kv_kind;
+    L.io_kind = g.io_kind;
+    L.stream = s;
+    e = launch_paged_prefill(L);
+    if (e != cudaSuccess) return cuda_fail(e, "vw_paged_prefill: launch");
+    return VW_OK;
+}
+
 int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32_t* seq_lens,
                        uint32_t num_seqs, uint32_t block_table_stride, uint32_t num_q_heads,
                        void* stream) {
@@ -606,6 +696,71 @@ int32_t vw_forward_release(uint64_t seq_id) {
     return VW_OK;
 }
 
+// The prefill descriptors of a forward pass (rows gathered from the bound
+// buffers into [L][Tp][...] host arrays): per layer, chunk append + causal
+// prefill attention, with the outputs copied back to `out` [L][Tp][Hq][D].
+static int32_t forward_prefill(vw_pool* pool, uint32_t L, uint32_t Hq, uint32_t Bp, uint32_t Tp,
+                               const std::vector<uint8_t>& q, const std::vector<uint8_t>& k,
+                               const std::vector<uint8_t>& v, const std::vector<int32_t>& cu,
+                               const std::vector<int32_t>& ctx, const std::vector<uint32_t>& bt,
+                               uint32_t stride, float rope_theta, std::vector<uint8_t>& out) {
+    const PoolGeom& g = pool->geom;
+    const size_t qb = (size_t)Tp * Hq * g.head_dim * 2, kb = (size_t)Tp * g.num_kv_heads * g.head_dim * 2;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    const size_t need = up(qb) * 2 * L + up(kb) * 2 * L + up(cu.size() * 4) + up(ctx.size() * 4) +
+                        up(bt.size() * 4);
+    DeviceScope ds(pool->cfg.device);
+    cudaError_t e;
+    if (pool->pstage_bytes < need) {
+        if (pool->pstage) cudaFree(pool->pstage);
+        pool->pstage = nullptr;
+        pool->pstage_bytes = 0;
+        if ((e = cudaMalloc(&pool->pstage, need)) != cudaSuccess)
+            return fail(VW_ERR_OOM, "voidweb_forward_pass: prefill staging: %s", cudaGetErrorString(e));
+        pool->pstage_bytes = need;
+    }
+    uint8_t* d_q = pool->pstage;
+    uint8_t* d_out = d_q + up(qb) * L;
+    uint8_t* d_k = d_out + up(qb) * L;
+    uint8_t* d_v = d_k + up(kb) * L;
+    int32_t* d_cu = reinterpret_cast<int32_t*>(d_v + up(kb) * L);
+    int32_t* d_ctx = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(d_cu) + up(cu.size() * 4));
+    uint32_t* d_bt = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(d_ctx) + up(ctx.size() * 4));
+    bool ok = cudaMemcpy(d_cu, cu.data(), cu.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(d_ctx, ctx.data(), ctx.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(d_bt, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    for (uint32_t l = 0; l < L && ok; ++l)
+        ok = cudaMemcpy(d_q + l * up(qb), q.data() + l * qb, qb, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(d_k + l * up(kb), k.data() + l * kb, kb, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(d_v + l * up(kb), v.data() + l * kb, kb, cudaMemcpyHostToDevice) == cudaSuccess;
+    if (!ok) return fail(VW_ERR_CUDA, "voidweb_forward_pass: prefill upload");
+    for (uint32_t l = 0; l < L; ++l) {
+        vw_prefill_args pa{};
+        pa.layer = l;
+        pa.num_seqs = Bp;
+        pa.num_tokens = Tp;
+        pa.num_q_heads = Hq;
+        pa.block_table_stride = stride;
+        pa.flags = VW_PREFILL_CAUSAL | (rope_theta > 0.0f ? VW_PREFILL_ROPE : 0u);
+        pa.q = d_q + l * up(qb);
+        pa.k_new = d_k + l * up(kb);
+        pa.v_new = d_v + l * up(kb);
+        pa.cu_seqlens = d_cu;
+        pa.ctx_start = d_ctx;
+        pa.block_tables = d_bt;
+        pa.out = d_out + l * up(qb);
+        pa.scale = 0.0f;
+        pa.rope_theta = rope_theta;
+        int32_t rc = vw_paged_prefill(pool, &pa, nullptr);
+        if (rc != VW_OK) return rc;
+    }
+    out.resize(qb * L);
+    for (uint32_t l = 0; l < L; ++l)
+        if ((e = cudaMemcpy(out.data() + l * qb, d_out + l * up(qb), qb, cudaMemcpyDeviceToHost)) != cudaSuccess)
+            return cuda_fail(e, "voidweb_forward_pass: prefill download");
+    return VW_OK;
+}
+
 int32_t voidweb_forward_pass(const ForwardArgs* args) {
     if (!args) return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null args");
     ForwardState& s = fwd();
@@ -619,43 +774,126 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
         return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: model shape does not match the pool");
     if (a.num_seqs == 0) return VW_OK;
     if (!a.seqs) return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null seqs");
+    if (a.num_heads == 0 || a.num_heads % g.num_kv_heads != 0)
+        return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: num_heads %u does not fit %u KV heads",
+                    a.num_heads, g.num_kv_heads);
     std::vector<SeqDescriptor> d(a.num_seqs);
     std::memcpy(d.data(), a.seqs, sizeof(SeqDescriptor) * a.num_seqs);
+    const uint32_t L = g.num_layers, Hq = a.num_heads, D = g.head_dim, Hkv = g.num_kv_heads;
+    // rows of descriptor i: [row0[i], row0[i] + num_tokens)
+    std::vector<uint32_t> row0(a.num_seqs), pos(a.num_seqs), pf, dc;
+    uint64_t T = 0;
     uint32_t stride = 1;
-    for (const auto& sd : d) {
-        if (sd.is_prefill || sd.num_tokens != 1)
-            return fail(VW_ERR_UNSUPPORTED, "voidweb_forward_pass: prefill descriptors are not supported");
-        if (sd.num_blocks > stride) stride = sd.num_blocks;
-    }
-    std::vector<uint32_t> table((size_t)a.num_seqs * stride, 0), lens(a.num_seqs);
+    std::unordered_map<uint64_t, uint32_t> seen;
     for (uint32_t i = 0; i < a.num_seqs; ++i) {
-        const uint32_t pos = s.seq_len.count(d[i].seq_id) ? s.seq_len[d[i].seq_id] : 0;
-        if ((uint64_t)pos + 1 > (uint64_t)d[i].num_blocks * 16)
-            return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: seq %llu needs %u blocks, has %u",
-                        (unsigned long long)d[i].seq_id, pos / 16 + 1, d[i].num_blocks);
-        if (d[i].num_blocks && !d[i].block_ptr)
+        const SeqDescriptor& sd = d[i];
+        if (sd.num_tokens == 0 || (!sd.is_prefill && sd.num_tokens != 1))
+            return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: seq %llu has %u tokens",
+                        (unsigned long long)sd.seq_id, sd.num_tokens);
+        if (seen.count(sd.seq_id))
+            return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: seq %llu appears twice",
+                        (unsigned long long)sd.seq_id);
+        seen[sd.seq_id] = i;
+        row0[i] = (uint32_t)T;
+        T += sd.num_tokens;
+        pos[i] = s.seq_len.count(sd.seq_id) ? s.seq_len[sd.seq_id] : 0;
+        if ((uint64_t)pos[i] + sd.num_tokens > (uint64_t)sd.num_blocks * 16)
+            return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: seq %llu needs %llu blocks, has %u",
+                        (unsigned long long)sd.seq_id,
+                        (unsigned long long)(((uint64_t)pos[i] + sd.num_tokens + 15) / 16), sd.num_blocks);
+        if (sd.num_blocks && !sd.block_ptr)
             return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null block_ptr");
-        std::memcpy(&table[(size_t)i * stride], reinterpret_cast<const void*>(d[i].block_ptr),
-                    (size_t)d[i].num_blocks * 4);
-        lens[i] = pos + 1;
+        if (sd.num_blocks > stride) stride = sd.num_blocks;
+        (sd.is_prefill ? pf : dc).push_back(i);
     }
-    vw_step_host_args st{};
-    st.num_seqs = a.num_seqs;
-    st.num_q_heads = a.num_heads;
-    st.block_table_stride = stride;
-    st.q = s.q;
-    st.k_new = s.k;
-    st.v_new = s.v;
-    st.block_tables = table.data();
-    st.seq_lens = lens.data();
-    st.out = s.out;
-    st.scale = 0.0f;
-    // ModelConfig.rope_theta (engine/ffi.bm:37): q and the new K rows are rotated
-    // in the decode, as the engine's own kernels would before attention
-    st.rope_theta = a.rope_theta > 1.0f ? a.rope_theta : 0.0f;
-    int32_t rc = vw_decode_step_host(s.pool, &st, nullptr);
-    if (rc != VW_OK) return rc;
-    for (uint32_t i = 0; i < a.num_seqs; ++i) s.seq_len[d[i].seq_id] = lens[i];
+    if (T > (1u << 24)) return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: too many tokens");
+    const float theta = a.rope_theta > 1.0f ? a.rope_theta : 0.0f;
+    const size_t qrow = (size_t)Hq * D * 2, krow = (size_t)Hkv * D * 2;
+    const uint8_t* hq = static_cast<const uint8_t*>(s.q);
+    const uint8_t* hk = static_cast<const uint8_t*>(s.k);
+    const uint8_t* hv = static_cast<const uint8_t*>(s.v);
+    uint8_t* ho = static_cast<uint8_t*>(s.out);
+    auto table_of = [&](uint32_t i, uint32_t* dst) {
+        std::memcpy(dst, reinterpret_cast<const void*>(d[i].block_ptr), (size_t)d[i].num_blocks * 4);
+    };
+
+    if (!pf.empty()) {
+        if (g.kv_kind == kFP8)
+            return fail(VW_ERR_UNSUPPORTED, "voidweb_forward_pass: prefill needs an f16 / bf16 pool");
+        const uint32_t Bp = (uint32_t)pf.size();
+        uint32_t Tp = 0;
+        std::vector<int32_t> cu(Bp + 1, 0), ctx(Bp);
+        std::vector<uint32_t> bt((size_t)Bp * stride, 0);
+        for (uint32_t k = 0; k < Bp; ++k) {
+            cu[k] = (int32_t)Tp;
+            Tp += d[pf[k]].num_tokens;
+            ctx[k] = (int32_t)pos[pf[k]];
+            table_of(pf[k], &bt[(size_t)k * stride]);
+        }
+        cu[Bp] = (int32_t)Tp;
+        std::vector<uint8_t> q((size_t)L * Tp * qrow), kk((size_t)L * Tp * krow), vv((size_t)L * Tp * krow), o;
+        for (uint32_t l = 0; l < L; ++l)
+            for (uint32_t k = 0; k < Bp; ++k) {
+                const size_t n = d[pf[k]].num_tokens, src = (size_t)l * T + row0[pf[k]], dst = (size_t)l * Tp + cu[k];
+                std::memcpy(&q[dst * qrow], hq + src * qrow, n * qrow);
+                std::memcpy(&kk[dst * krow], hk + src * krow, n * krow);
+                std::memcpy(&vv[dst * krow], hv + src * krow, n * krow);
+            }
+        int32_t rc = forward_prefill(s.pool, L, Hq, Bp, Tp, q, kk, vv, cu, ctx, bt, stride, theta, o);
+        if (rc != VW_OK) return rc;
+        for (uint32_t l = 0; l < L; ++l)
+            for (uint32_t k = 0; k < Bp; ++k) {
+                const size_t n = d[pf[k]].num_tokens, dst = (size_t)l * T + row0[pf[k]], src = (size_t)l * Tp + cu[k];
+                std::memcpy(ho + dst * qrow, &o[src * qrow], n * qrow);
+            }
+    }
+
+    if (!dc.empty()) {
+        const uint32_t Bd = (uint32_t)dc.size();
+        std::vector<uint32_t> table((size_t)Bd * stride, 0), lens(Bd);
+        for (uint32_t k = 0; k < Bd; ++k) {
+            table_of(dc[k], &table[(size_t)k * stride]);
+            lens[k] = pos[dc[k]] + 1;
+        }
+        // an all-decode batch uses the bound buffers in place; otherwise the
+        // decode rows are gathered into [L][Bd][...] arrays first
+        const bool direct = pf.empty();
+        std::vector<uint8_t> q, kk, vv, o;
+        if (!direct) {
+            q.resize((size_t)L * Bd * qrow);
+            kk.resize((size_t)L * Bd * krow);
+            vv.resize((size_t)L * Bd * krow);
+            o.resize((size_t)L * Bd * qrow);
+            for (uint32_t l = 0; l < L; ++l)
+                for (uint32_t k = 0; k < Bd; ++k) {
+                    const size_t src = (size_t)l * T + row0[dc[k]], dst = (size_t)l * Bd + k;
+                    std::memcpy(&q[dst * qrow], hq + src * qrow, qrow);
+                    std::memcpy(&kk[dst * krow], hk + src * krow, krow);
+                    std::memcpy(&vv[dst * krow], hv + src * krow, krow);
+                }
+        }
+        vw_step_host_args st{};
+        st.num_seqs = Bd;
+        st.num_q_heads = Hq;
+        st.block_table_stride = stride;
+        st.q = direct ? s.q : q.data();
+        st.k_new = direct ? s.k : kk.data();
+        st.v_new = direct ? s.v : vv.data();
+        st.block_tables = table.data();
+        st.seq_lens = lens.data();
+        st.out = direct ? s.out : o.data();
+        st.scale = 0.0f;
+        // ModelConfig.rope_theta (engine/ffi.bm:37): q and the new K rows are rotated
+        // in the decode, as the engine's own kernels would before attention
+        st.rope_theta = theta;
+        int32_t rc = vw_decode_step_host(s.pool, &st, nullptr);
+        if (rc != VW_OK) return rc;
+        if (!direct)
+            for (uint32_t l = 0; l < L; ++l)
+                for (uint32_t k = 0; k < Bd; ++k)
+                    std::memcpy(ho + ((size_t)l * T + row0[dc[k]]) * qrow, &o[((size_t)l * Bd + k) * qrow], qrow);
+    }
+    for (uint32_t i = 0; i < a.num_seqs; ++i) s.seq_len[d[i].seq_id] = pos[i] + d[i].num_tokens;
     return VW_OK;
 }
 

@@ -56,6 +56,7 @@
 #include "vw_fp8.cuh"
 #include "vw_internal.h"
 #include "vw_ptx.cuh"
+#include "vw_rope.cuh"
 
 #ifndef VW_DECODE_WARPS
 #define VW_DECODE_WARPS 4
@@ -576,20 +577,6 @@ __device__ __forceinline__ void merge_unit(const DecodeParams& p, int b, int h, 
 }
 
 // ------------------------------------------------------------------ consumer
-
-// Rotary position embedding of one pair (x[d], x[d + D/2]) at position pos,
-// kernels/rope/rope.bm:22-52: theta_d = 1 / theta^(2d/D), angle = theta_d * pos,
-// (x_r, x_i) -> (x_r cos - x_i sin, x_r sin + x_i cos), all in f32 with no
-// fused multiply-adds, the result rounded to the io type by the caller.
-__device__ __forceinline__ void rope_pair(float& xr, float& xi, int d, int D, float theta, float pos) {
-    const float freq = __fdiv_rn(1.0f, powf(theta, __fdiv_rn(2.0f * (float)d, (float)D)));
-    float s, c;
-    sincosf(__fmul_rn(freq, pos), &s, &c);
-    const float r = __fsub_rn(__fmul_rn(xr, c), __fmul_rn(xi, s));
-    const float i = __fadd_rn(__fmul_rn(xr, s), __fmul_rn(xi, c));
-    xr = r;
-    xi = i;
-}
 
 // Query fragments (B operand of S^T = K Q^T) from the staged query tile.
 // 2-byte pages: a lane's fragments hold elements d and d + D/2 (k-steps kt and

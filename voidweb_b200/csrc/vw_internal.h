@@ -65,6 +65,31 @@ int decode_ctas_per_sm();
 size_t decode_scratch_floats_o(int grid, int head_dim);
 size_t decode_scratch_floats_ml(int grid);
 
+// Paged prefill (chunked prefill over the pool): sequence b's chunk of
+// n_b = cu_q[b+1] - cu_q[b] tokens sits at positions ctx_start[b] + i.
+struct PrefillParams {
+    const void* q;              // [T][Hq][D] io dtype (packed chunk tokens of all sequences)
+    void* out;                  // [T][Hq][D] io dtype
+    const int32_t* cu_q;        // [B+1] token offsets of the chunks
+    const int32_t* ctx_start;   // [B] tokens cached before each chunk
+    const uint32_t* block_tables;   // [B][bt_stride]
+    uint32_t* err;              // device error word
+    uint32_t B, T, Hq, Hkv, group, num_blocks, layer, bt_stride, causal, flags;
+    float scale_log2;           // softmax scale * log2(e)
+    float rope_theta;           // > 0: rotate q at its position (RoPE)
+};
+
+struct PrefillLaunch {
+    PrefillParams p;
+    const CUtensorMap* tmap;    // the pool's page-head map (as for the decode)
+    uint32_t head_dim, kv_kind, io_kind;
+    cudaStream_t stream;
+};
+
+// Returns cudaSuccess or the launch error; shapes were validated by the caller.
+cudaError_t launch_paged_prefill(const PrefillLaunch& L);
+int prefill_query_tile();
+
 struct PoolGeom {
     uint32_t num_layers, num_kv_heads, head_dim, num_blocks, kv_kind, io_kind, fp8_ocp;
 };
@@ -74,6 +99,14 @@ cudaError_t launch_kv_append(const PoolGeom& g, uint8_t* data, float* scales, ui
                              uint32_t n, uint32_t* err, cudaStream_t s);
 cudaError_t launch_block_copy(const PoolGeom& g, uint8_t* data, float* scales,
                               const uint32_t* pairs, uint32_t n, uint32_t* err, cudaStream_t s);
+// Chunk append of a prefill: token i of sequence b (cu_q[b] <= i < cu_q[b+1]) at
+// position ctx_start[b] + i - cu_q[b] goes to slot
+// block_tables[b][p/16] * 16 + p % 16; K rows rotated first when rope_theta > 0.
+cudaError_t launch_prefill_append(const PoolGeom& g, uint8_t* data, float* scales, uint32_t layer,
+                                  const void* k_new, const void* v_new, const int32_t* cu_q,
+                                  const int32_t* ctx_start, const uint32_t* block_tables,
+                                  uint32_t bt_stride, uint32_t B, uint32_t T, float rope_theta,
+                                  uint32_t* err, cudaStream_t s);
 cudaError_t launch_kv_gather(const PoolGeom& g, const uint8_t* data, const float* scales,
                              uint32_t layer, const uint32_t* block_table, uint32_t seq_len,
                              void* out_k, void* out_v, float* out_ks, float* out_vs,

@@ -4,8 +4,8 @@
 // All three are HBM-bound copies: one warp moves one token row of one KV head
 // (D elements) with 16-B (or 8-B) vector accesses, so a warp touches whole 32-B
 // sectors and consecutive warps walk consecutive rows.  Pool layout:
-//   data  [L][NB][2][Hkv][16][D]   (2 = K, V; element f16/bf16 or an E4M3 code)
-//   scale [L][NB][2][Hkv][16]      (FP8 pools only)
+//   data  [L][NB][Hkv][2][16][D]   (2 = K, V; element f16/bf16 or an E4M3 code)
+//   scale [L][NB][Hkv][2][16]      (FP8 pools only)
 // Bounds: every block id and slot is checked against the pool before it is
 // used; a bad one sets a bit in the pool's device error word and the row is
 // skipped, so no kernel here can write outside the pool.

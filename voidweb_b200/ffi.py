@@ -41,19 +41,27 @@ class KernelLib:
         self._handle = None
         self._forward = None
 
-    def forward_pass(self, cfg: dict, decode_seqs, vocab_size: int = 1) -> np.ndarray:
+    def forward_pass(self, cfg: dict, decode_seqs, vocab_size: int = 1,
+                     prefill_seqs=()) -> np.ndarray:
         """decode_seqs: list of (seq_id, last_token, block_table) like DecodeSeq
-        (scheduler/scheduler.bm:113-117).  cfg: num_heads, num_kv_heads,
-        num_layers, head_dim, hidden_size, rope_theta, quant_type.  Returns the
-        logits buffer [num_seqs * vocab_size] (ffi.bm:94); this library fills
-        the bound attention outputs, not logits."""
-        n = len(decode_seqs)
-        tok_storage = [np.array([t], dtype=np.uint32) for (_, t, _) in decode_seqs]
-        blk_storage = [np.ascontiguousarray(bt, dtype=np.uint32) for (_, _, bt) in decode_seqs]
+        (scheduler/scheduler.bm:112-116); prefill_seqs: list of (seq_id,
+        chunk_tokens, block_table) like PrefillSeq (:106-110).  Descriptors are
+        built as build_seq_descriptors does (:134-170): prefill chunks first
+        (is_prefill 1, num_tokens = chunk length), then decodes (num_tokens 1).
+        cfg: num_heads, num_kv_heads, num_layers, head_dim, hidden_size,
+        rope_theta, quant_type.  Returns the logits buffer [num_seqs *
+        vocab_size] (ffi.bm:94); this library fills the bound attention outputs,
+        not logits."""
+        entries = [(sid, np.ascontiguousarray(toks, dtype=np.uint32), bt, 1)
+                   for (sid, toks, bt) in prefill_seqs]
+        entries += [(sid, np.array([t], dtype=np.uint32), bt, 0) for (sid, t, bt) in decode_seqs]
+        n = len(entries)
+        tok_storage = [e[1] for e in entries]
+        blk_storage = [np.ascontiguousarray(e[2], dtype=np.uint32) for e in entries]
         descs = (C.SeqDescriptor * max(n, 1))()
-        for i, (sid, _, _) in enumerate(decode_seqs):
-            descs[i] = C.SeqDescriptor(sid, tok_storage[i].ctypes.data, 1,
-                                       blk_storage[i].ctypes.data, blk_storage[i].size, 0)
+        for i, (sid, toks, _, is_pf) in enumerate(entries):
+            descs[i] = C.SeqDescriptor(sid, tok_storage[i].ctypes.data, toks.size,
+                                       blk_storage[i].ctypes.data, blk_storage[i].size, is_pf)
         logits = np.zeros(n * vocab_size, dtype=np.float32)
         args = C.ForwardArgs(ctypes.cast(descs, ctypes.c_void_p), n, cfg.get("hidden_size", 0),
                              cfg["num_heads"], cfg["num_kv_heads"], cfg["num_layers"], vocab_size,

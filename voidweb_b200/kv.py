@@ -146,6 +146,31 @@ class KvPool:
         C.check(C.lib().vw_paged_decode(self._h, ctypes.byref(a), _stream(stream)))
         return out
 
+    def paged_prefill(self, layer: int, q: torch.Tensor, cu_seqlens: torch.Tensor,
+                      ctx_start: torch.Tensor, block_tables: torch.Tensor, out: torch.Tensor,
+                      k_new=None, v_new=None, causal: bool = True, scale: float = 0.0,
+                      rope_theta: float = 0.0, stream=None, flags: int = 0) -> torch.Tensor:
+        """Chunked prefill of one layer (launch_flash_attn_prefill,
+        flash_attention.bm:167-177, over the pool's pages).
+
+        Sequence b's chunk is rows cu_seqlens[b] .. cu_seqlens[b+1]-1 of q
+        [T][Hq][D] at positions ctx_start[b] + i; with k_new / v_new [T][Hkv][D]
+        its rows are appended first.  causal: token i attends to keys 0 .. its
+        position, else to the whole ctx_start[b] + n_b context.  rope_theta > 0
+        rotates q and the appended K rows at their positions (VW_PREFILL_ROPE).
+        cu_seqlens, ctx_start: int32; block_tables: [B][stride] int32.
+        """
+        T, Hq, _ = q.shape
+        if causal:
+            flags |= C.VW_PREFILL_CAUSAL
+        if rope_theta > 0.0:
+            flags |= C.VW_PREFILL_ROPE
+        a = C.PrefillArgs(layer, ctx_start.shape[0], T, Hq, block_tables.shape[1], flags, _ptr(q),
+                          _ptr(k_new), _ptr(v_new), _ptr(cu_seqlens), _ptr(ctx_start),
+                          _ptr(block_tables), _ptr(out), scale, rope_theta)
+        C.check(C.lib().vw_paged_prefill(self._h, ctypes.byref(a), _stream(stream)))
+        return out
+
     def plan(self, block_tables: torch.Tensor, seq_lens: torch.Tensor, num_q_heads: int,
              stream=None) -> None:
         """Page assignment of a decode batch for every layer's paged_decode with
