@@ -43,6 +43,10 @@ WORKLOADS = {
                               kv="fp8", io="bf16", seed=3),
     "llama3-70b-1kvhead-b256": dict(L=80, Hq=8, Hkv=1, D=128, B=256, ctx=("uniform", 2048, 8192),
                                     kv="bf16", io="bf16", seed=4),
+    # chunked prefill (vw_paged_prefill): B sequences, each a `chunk`-token chunk
+    # (the scheduler's largest, scheduler/scheduler.bm:255) after a cached prefix
+    "qwen2.5-7b-prefill-4x2048": dict(kind="prefill", L=28, Hq=28, Hkv=4, D=128, B=4, chunk=2048,
+                                      ctx=("uniform", 0, 2048), kv="bf16", io="bf16", seed=11),
 }
 DEFAULT = "qwen2.5-7b-decode-b16"
 L2_BYTES = 126 * 1024 * 1024
@@ -73,6 +77,122 @@ def algorithmic_bytes_per_launch(w, seq_lens):
 # default workload, from one ncu --set full capture of that launch; ncu cannot
 # run inside the timed bench, so the figure is carried here.
 NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 70_964_480}
+
+
+def tensor_peak():
+    """Measured bf16 dense TFLOP/s: (burst, sustained, kind)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, "fallback"
+
+
+def prefill_flops(w, prefix):
+    """Attention FLOPs of one layer of the prefill workload: each query token at
+    position p attends to p + 1 keys (causal), 2*D FLOPs per key for Q K^T and
+    2*D for P V, for every query head."""
+    keys = 0
+    for cs in prefix:
+        keys += int(w["chunk"]) * int(cs) + w["chunk"] * (w["chunk"] + 1) // 2
+    return 4 * w["D"] * w["Hq"] * keys
+
+
+def run_prefill_bench(args, w):
+    """Chunked prefill of every layer (append of the chunk rows + causal prefill
+    attention over the pool), timed with CUDA events over K steps."""
+    import torch
+    from voidweb_b200.kv import KvPool, PoolSpec
+    import oracle
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        print(json.dumps({"metric": "prefill attention TFLOP/s", "error": "single GPU only"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    L, Hq, Hkv, D, B, n = w["L"], w["Hq"], w["Hkv"], w["D"], w["B"], w["chunk"]
+    prefix = ctx_lengths(w, 0)
+    pages = (prefix + n + 15) // 16
+    NB = int(pages.sum()) + 64
+    rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919))
+    perm = rng.permutation(NB)
+    stride = int(pages.max())
+    bt = np.zeros((B, stride), dtype=np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[off:off + pages[b]]
+        off += pages[b]
+    T = B * n
+    pool = KvPool(PoolSpec(L, Hkv, D, NB, w["kv"], w["io"], max_batch=B), device=0)
+    pool.pages_u8().view(torch.bfloat16).normal_()
+    q = torch.randn((L, T, Hq, D), device=dev).bfloat16()
+    kn = torch.randn((L, T, Hkv, D), device=dev).bfloat16()
+    vn = torch.randn((L, T, Hkv, D), device=dev).bfloat16()
+    out = torch.empty_like(q)
+    cu = torch.arange(0, T + 1, n, dtype=torch.int32, device=dev)
+    cs = torch.from_numpy(prefix.astype(np.int32)).to(dev)
+    btd = torch.from_numpy(bt).to(dev)
+
+    def step():
+        for layer in range(L):
+            pool.paged_prefill(layer, q[layer], cu, cs, btd, out[layer], k_new=kn[layer],
+                               v_new=vn[layer], causal=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    assert pool.check() == 0
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = prefill_flops(w, prefix) * L
+    tflops = flops / (ms * 1e-3) / 1e12
+    burst, sustained, kind = tensor_peak()
+    # CPU: the oracle's f32 restatement on a bounded sample (one layer, the
+    # first 16 query tokens of each chunk), with all host threads
+    cpu = None
+    if not args.no_cpu_baseline:
+        thr = cpu_threads()
+        g = oracle.geom(1, Hkv, D, NB, oracle.BF16, oracle.BF16)
+        data = pool.pages_u8().view(torch.int16)[: NB * Hkv * 2 * 16 * D].cpu().numpy().view(np.uint16)
+        data = data.reshape(oracle.pool_shape(g))
+        m = 16
+        qs = q[0].view(torch.int16).cpu().numpy().view(np.uint16).reshape(B, n, Hq, D)[:, :m].reshape(B * m, Hq, D)
+        cus = np.arange(0, B * m + 1, m, dtype=np.int32)
+        t0 = time.perf_counter()
+        oracle.paged_prefill_f32(g, data, None, 0, qs, Hq, bt, cus, prefix.astype(np.int32), True,
+                                 1.0 / math.sqrt(D), nthreads=thr)
+        dt = time.perf_counter() - t0
+        sample_flops = sum(4 * D * Hq * (m * int(c0) + m * (m + 1) // 2) for c0 in prefix)
+        cpu = {"value": round(sample_flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": thr,
+               "kind": "port",
+               "sample": f"1 layer, the first {m} query tokens of each of the {B} chunks"}
+    print(json.dumps({
+        "metric": "prefill attention TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv,
+                   "head_dim": D, "seqs": B, "chunk_tokens": n,
+                   "cached_prefix": [int(x) for x in prefix], "block_size": 16, "kv_dtype": w["kv"],
+                   "causal": True, "parallelism": "single",
+                   "l2": f"inputs larger than L2 ({NB * Hkv * 2 * 16 * D * 2 * L / 1e9:.2f} GB of pages)"},
+        "tok_per_s": round(T / (ms * 1e-3), 1),
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": sustained,
+                     "unit": "TFLOP/s", "frac": round(tflops / sustained, 4), "traffic": None,
+                     "peak_kind": f"{kind} sustained (burst {burst})",
+                     "flops_per_step": flops},
+        "cpu_baseline": cpu, "e2e": None, "clocks": clk, "gpu_launches": args.steps * L * 2,
+    }))
 
 
 def hbm_peak():
@@ -271,6 +391,14 @@ def main():
     w = dict(WORKLOADS[args.workload])
     if args.layers > 0:
         w["L"] = min(args.layers, w["L"])
+    if w.get("kind") == "prefill":
+        if args.warmup < 3:
+            args.warmup = 3
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the decode "
+                              "workloads; the prefill line's cpu_baseline is the oracle sample"}))
+            return
+        return run_prefill_bench(args, w)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

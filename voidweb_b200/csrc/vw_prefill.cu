@@ -13,16 +13,19 @@
 // decoder needs) or to all ctx_start[b] + n_b keys (the reference kernel's
 // seq_kv, without a mask).
 //
-//  * Work split.  CTA (tile, q head): 64 query tokens of one sequence for one
-//    query head; four consumer warps own 16 tokens each; the page-heads of the
-//    head's KV head stream through a ring of shared-memory stages (one TMA box
-//    per page-head, the decode's tensor map) and every warp reads every page.
-//  * Math.  Per page (16 keys) and warp: S = Q K^T as 2 x D/16 mma.sync
-//    m16n8k16 (query tokens as M, keys as N, K fragments by ldmatrix from the
-//    swizzled stage), the causal / length mask, an online softmax in the log2
-//    domain, then O += P V with P reused from the S fragments as the A operand
-//    (for bf16 pages as a bf16 pair hi + lo) and V fragments by transposing
-//    ldmatrix.  f32 accumulation.
+//  * Work split.  CTA (tile, q head): 128 query tokens of one sequence for one
+//    query head; the page-heads of the head's KV head stream through a ring of
+//    shared-memory stages (one TMA box per page-head, the decode's tensor map).
+//  * Math on the fifth-generation tensor cores (tcgen05): per page-head,
+//    S = Q K^T with M = 128 query rows and N = 16 keys (A = the query tile, B =
+//    the staged K rows, both 128-B-swizzled K-major shared-memory operands),
+//    accumulated in tensor memory; four softmax warps (one query row per
+//    thread, no shuffles) read S, apply the causal / length mask and an online
+//    softmax with a lazily raised maximum, and write P back to tensor memory;
+//    then O += P V with P from tensor memory and the staged V rows as an
+//    MN-major operand (M = 128, N = head_dim, K = 16 keys).  O stays in tensor
+//    memory until the epilogue.  bf16 probabilities are written as a bf16 pair
+//    hi + lo (two PV MMAs) so that P keeps ~2^-18 relative precision.
 //  * Every wait is bounded; on timeout the kernel records kDevErrTimeout,
 //    drains its TMA loads and returns.
 #include <cuda.h>
@@ -34,33 +37,13 @@
 #include "vw_internal.h"
 #include "vw_ptx.cuh"
 #include "vw_rope.cuh"
+#include "vw_tc.cuh"
 
 namespace vw {
 
 namespace {
 
-constexpr int kPfWarps = 4;                       // consumer warps, 16 query tokens each
-constexpr int kPfTile = 16 * kPfWarps;            // query tokens per CTA
-constexpr int kPfStages = 8;                      // page-head stages in the ring
-
 constexpr int pf_align(int x, int a) { return (x + a - 1) / a * a; }
-
-template <int D_, int IO_>
-struct PfTraits {
-    static constexpr int D = D_, IO = IO_;
-    static constexpr int W = kPfWarps;
-    static constexpr int THREADS = (W + 1) * 32;
-    static constexpr int KT = D / 16;             // k-steps of S = Q K^T
-    static constexpr int NO = D / 8;              // n-tiles (8 d each) of O
-    static constexpr int CHUNKS = D * 2 / 128;    // 128-B columns of a row
-    static constexpr int STAGE = 32 * D * 2;      // one page-head: K rows 0-15, V rows 16-31
-    static constexpr int S = kPfStages;
-    static constexpr int TPFX = pf_align((kMaxBatchPerLaunch + 1) * 4, 128);
-    static constexpr int SMEM = 1024 + S * STAGE + TPFX + 2 * S * 8;
-    static constexpr bool MMA_BF16 = IO == kBF16;
-    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-    static_assert(STAGE % 1024 == 0, "1024-B stage alignment (128-B swizzle)");
-};
 
 template <int IO>
 __device__ __forceinline__ float pf_io_to_f32(uint32_t h) {
@@ -173,60 +156,78 @@ __global__ void __launch_bounds__(256) prefill_append_kernel(
 
 // ------------------------------------------------------------------ attention
 
-// Query fragments (A operand of S = Q K^T) of this warp's 16 tokens, rows
-// lane/4 and lane/4 + 8: k-step kt holds elements kt*16 + 2c, +1 (regs 0, 1)
-// and kt*16 + 8 + 2c, +1 (regs 2, 3), c = lane % 4.  With rope_theta > 0 each
-// row is rotated at its own position (the partner d + D/2 of an element of
-// k-step kt < KT/2 is the same register of k-step kt + KT/2).
-template <class T>
-__device__ __forceinline__ void pf_load_q(const PrefillParams& p, const uint8_t* q0, int row_stride,
-                                          bool live0, bool live1, float pos0, float pos1, int lane,
-                                          uint32_t (&qa)[T::KT][4]) {
-    const int g = lane >> 2, c = lane & 3;
-    const uint8_t* r0 = q0 + (size_t)g * row_stride;
-    const uint8_t* r1 = q0 + (size_t)(g + 8) * row_stride;
-#pragma unroll
-    for (int kt = 0; kt < T::KT; ++kt) {
-        const int d0 = kt * 16 + 2 * c, d1 = d0 + 8;
-        qa[kt][0] = live0 ? __ldg(reinterpret_cast<const uint32_t*>(r0 + d0 * 2)) : 0u;
-        qa[kt][1] = live1 ? __ldg(reinterpret_cast<const uint32_t*>(r1 + d0 * 2)) : 0u;
-        qa[kt][2] = live0 ? __ldg(reinterpret_cast<const uint32_t*>(r0 + d1 * 2)) : 0u;
-        qa[kt][3] = live1 ? __ldg(reinterpret_cast<const uint32_t*>(r1 + d1 * 2)) : 0u;
-    }
-    if (p.rope_theta > 0.0f) {
-#pragma unroll
-        for (int kt = 0; kt < T::KT / 2; ++kt)
-#pragma unroll
-            for (int x = 0; x < 4; ++x) {
-                const int d = kt * 16 + (x >> 1) * 8 + 2 * c;
-                const float pos = (x & 1) ? pos1 : pos0;
-                uint32_t& a = qa[kt][x];
-                uint32_t& bb = qa[kt + T::KT / 2][x];
-                float ar = pf_io_to_f32<T::IO>(a & 0xFFFFu), ai = pf_io_to_f32<T::IO>(bb & 0xFFFFu);
-                float br = pf_io_to_f32<T::IO>(a >> 16), bi = pf_io_to_f32<T::IO>(bb >> 16);
-                rope_pair(ar, ai, d, T::D, p.rope_theta, pos);
-                rope_pair(br, bi, d + 1, T::D, p.rope_theta, pos);
-                a = (uint32_t)pf_f32_to_io<T::IO>(ar) | ((uint32_t)pf_f32_to_io<T::IO>(br) << 16);
-                bb = (uint32_t)pf_f32_to_io<T::IO>(ai) | ((uint32_t)pf_f32_to_io<T::IO>(bi) << 16);
-            }
-    }
-}
+constexpr int kTcRows = 128;                      // query tokens per CTA: the MMA's M
+constexpr int kTcStages = 8;                      // page-head stages in the ring
+constexpr float kTcRescale = 8.0f;                // log2 units: p <= 2^8 against a stale max
 
+template <int D_, int IO_>
+struct TcTraits {
+    static constexpr int D = D_, IO = IO_;
+    static constexpr bool BF = IO == kBF16;
+    static constexpr int CH = D * 2 / 128;            // 128-B columns of a row
+    static constexpr int STAGE = 32 * D * 2;          // one page-head: K rows 0-15, V rows 16-31
+    static constexpr int S = kTcStages;
+    static constexpr int QBYTES = kTcRows * D * 2;    // query tile [CH][128 rows][128 B]
+    static constexpr int KSTEPS = D / 16;             // MMAs of S = Q K^T per page
+    // tensor memory: O in columns [0, D), S buffers at D and D + 16 (16 f32
+    // columns each), P buffers at D + 32 and D + 48 (8 columns of bf16/f16 pairs,
+    // then 8 more for the low part of bf16 probabilities)
+    static constexpr int COL_S = D, COL_P = D + 32;
+    static constexpr uint32_t TMEM_COLS = D == 128 ? 256u : 128u;
+    static constexpr int TPFX = pf_align((kMaxBatchPerLaunch + 1) * 4, 128);
+    static constexpr int NBAR = 2 * S + 9;            // full, empty; s_full/s_free/p_full/p_free x2; done
+    static constexpr int SMEM = 1024 + QBYTES + S * STAGE + TPFX + NBAR * 8 + 16;
+    static constexpr int THREADS = 6 * 32;            // 4 softmax warps, 1 MMA warp, 1 producer warp
+    static constexpr uint32_t IDESC_S = idesc_f16(BF, false, kTcRows, 16);
+    static constexpr uint32_t IDESC_PV = idesc_f16(BF, true, kTcRows, D);
+    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    static_assert(COL_P + 32 <= (int)TMEM_COLS, "tensor-memory columns");
+    static_assert(STAGE % 1024 == 0 && QBYTES % 1024 == 0, "1024-B alignment (128-B swizzle)");
+};
+
+// CTA (tile, q head): 128 query tokens of one sequence for one query head.
+//  * warps 0-3 (thread r = query row r = tensor-memory lane r): load and
+//    (RoPE-)rotate the query rows into a 128-B-swizzled K-major tile, then per
+//    page read S from tensor memory, mask, run the online softmax with a lazily
+//    raised maximum (O in tensor memory is rescaled only when a row's maximum
+//    grows by more than 2^8) and write P back to tensor memory; finally read O,
+//    divide by the row sum and store the rows.
+//  * warp 4: allocates tensor memory and one lane issues, per page-head j,
+//    S_j = Q K_j^T (D/16 MMAs, M = 128, N = 16 keys, K = 16) into S buffer j%2,
+//    then O += P_{j-1} V_{j-1} (M = 128, N = D, K = 16 keys; A = P from tensor
+//    memory, B = the staged V rows as an MN-major operand), so the MMAs of one
+//    page overlap the softmax of the previous one.  Commits release the stage,
+//    the P buffer and, at the end, the epilogue.
+//  * warp 5: the TMA producer of page-heads (as the decode).
 template <class T>
 __global__ void __launch_bounds__(T::THREADS, 2)
 prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = base;
-    int* tpfx = reinterpret_cast<int*>(base + T::S * T::STAGE);
+    uint8_t* qs = base;
+    uint8_t* stages = base + T::QBYTES;
+    int* tpfx = reinterpret_cast<int*>(stages + T::S * T::STAGE);
     uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tpfx) + T::TPFX);
     uint64_t* empty = full + T::S;
+    uint64_t* s_full = empty + T::S;
+    uint64_t* s_free = s_full + 2;
+    uint64_t* p_full = s_free + 2;
+    uint64_t* p_free = p_full + 2;
+    uint64_t* done = p_free + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t deadline = cycles() + kWaitDeadlineCycles;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < T::S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], T::W); }
+        for (int s = 0; s < T::S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_free[b], 4);
+            mbar_init(&p_full[b], 4);
+            mbar_init(&p_free[b], 1);
+        }
+        mbar_init(done, 1);
         fence_mbar_init();
     }
     if (p.flags & kDecodePdl) griddep_wait();     // q, chunk rows and pages from the predecessor
@@ -239,7 +240,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
             int nt = 0;
             if (b < (int)p.B) {
                 const int n = __ldg(p.cu_q + b + 1) - __ldg(p.cu_q + b);
-                nt = n > 0 ? (n + kPfTile - 1) / kPfTile : 0;
+                nt = n > 0 ? (n + kTcRows - 1) / kTcRows : 0;
             }
             int incl = nt;
 #pragma unroll
@@ -265,13 +266,60 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         if (threadIdx.x == 0) atomicOr(p.err, kDevErrSeqLen);
         return;
     }
-    const int t0 = (x - tpfx[b]) * kPfTile;
-    const int qmax = cs + min(t0 + kPfTile - 1, n - 1);          // last query position of the tile
+    const int t0 = (x - tpfx[b]) * kTcRows;
+    const int qmax = cs + min(t0 + kTcRows - 1, n - 1);          // last query position of the tile
     const int kend = p.causal ? qmax + 1 : total;                // keys [0, kend)
     const int npages = (kend + kBlockSize - 1) / kBlockSize;
     const int j = blockIdx.y, h = j / (int)p.group;
 
-    if (warp == T::W) {
+    if (warp == 4) {
+        tmem_alloc(tmem_slot, T::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (warp < 4) {
+        // query row r into the swizzled K-major tile: 16-B unit u of the row goes
+        // to column u / 8, unit (u % 8) ^ (r % 8)
+        const int r = threadIdx.x, tq = t0 + r;
+        const bool live = tq < n;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(p.q) + ((size_t)(q_off + tq) * p.Hq + j) * T::D * 2;
+        constexpr int U = T::D / 8, HALF = U / 2;
+#pragma unroll
+        for (int u = 0; u < HALF; ++u) {
+            uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+            if (live) {
+                lo = __ldg(reinterpret_cast<const uint4*>(src + u * 16));
+                hi = __ldg(reinterpret_cast<const uint4*>(src + (u + HALF) * 16));
+            }
+            if (p.rope_theta > 0.0f && live) {
+                // pairs (d, d + D/2): element e of unit u with element e of unit u + D/16
+                uint32_t a[4] = {lo.x, lo.y, lo.z, lo.w}, c[4] = {hi.x, hi.y, hi.z, hi.w};
+                const float pos = (float)(cs + tq);
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    float ar = pf_io_to_f32<T::IO>(a[w] & 0xFFFFu), ai = pf_io_to_f32<T::IO>(c[w] & 0xFFFFu);
+                    float br = pf_io_to_f32<T::IO>(a[w] >> 16), bi = pf_io_to_f32<T::IO>(c[w] >> 16);
+                    const int d = u * 8 + 2 * w;
+                    rope_pair(ar, ai, d, T::D, p.rope_theta, pos);
+                    rope_pair(br, bi, d + 1, T::D, p.rope_theta, pos);
+                    a[w] = (uint32_t)pf_f32_to_io<T::IO>(ar) | ((uint32_t)pf_f32_to_io<T::IO>(br) << 16);
+                    c[w] = (uint32_t)pf_f32_to_io<T::IO>(ai) | ((uint32_t)pf_f32_to_io<T::IO>(bi) << 16);
+                }
+                lo = make_uint4(a[0], a[1], a[2], a[3]);
+                hi = make_uint4(c[0], c[1], c[2], c[3]);
+            }
+            const int u2 = u + HALF;
+            *reinterpret_cast<uint4*>(qs + (u >> 3) * (kTcRows * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(qs + (u2 >> 3) * (kTcRows * 128) + r * 128 + (((u2 & 7) ^ (r & 7)) << 4)) = hi;
+        }
+        // generic-proxy writes, read next by the tensor cores (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+
+    if (warp == 5) {
         // ---- producer: block ids 32 at a time, lane 0 issues one box per page-head
         bool ok = true;
         for (int i0 = 0; i0 < npages && ok; i0 += 32) {
@@ -292,7 +340,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                             atomicOr(p.err, kDevErrBlockId);
                         mbar_arrive_expect_tx(&full[s], T::STAGE);
                         uint8_t* st = stages + s * T::STAGE;
-                        if constexpr (T::CHUNKS == 1)
+                        if constexpr (T::CH == 1)
                             tma_load_2d(st, &tmap, &full[s], 0, row0);
                         else
                             tma_load_3d(st, &tmap, &full[s], 0, row0, 0);
@@ -311,159 +359,164 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                     break;
                 }
         }
-        return;
-    }
-
-    // ---- consumer warp: query tokens t0 + 16*warp + (lane/4, lane/4 + 8)
-    const int g = lane >> 2, c = lane & 3;
-    const int tq0 = t0 + 16 * warp + g, tq1 = tq0 + 8;
-    const bool live0 = tq0 < n, live1 = tq1 < n;
-    const int qp0 = cs + tq0, qp1 = cs + tq1;                    // query positions
-    const int kend0 = p.causal ? qp0 + 1 : total, kend1 = p.causal ? qp1 + 1 : total;
-    const size_t row_stride = (size_t)p.Hq * T::D * 2;
-    const uint8_t* qbase = reinterpret_cast<const uint8_t*>(p.q) +
-                           ((size_t)(q_off + t0 + 16 * warp) * p.Hq + j) * T::D * 2;
-    uint32_t qa[T::KT][4];
-    pf_load_q<T>(p, qbase, (int)row_stride, live0, live1, (float)qp0, (float)qp1, lane, qa);
-
-    float o[T::NO][4];
+    } else if (warp == 4) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t qaddr = smem_u32(qs);
+            auto issue_pv = [&](int jj) -> bool {
+                const int bb = jj & 1;
+                if (!mbar_wait(&p_full[bb], (jj >> 1) & 1, deadline)) return false;
+                tc_fence_after();
+                const uint32_t st = smem_u32(stages + (jj % T::S) * T::STAGE);
+                // V rows 16-31: MN-major, 64-element columns 4096 B apart, 8-key groups 1024 B apart
+                const uint64_t vdesc = smem_desc_sw128(st + 16 * 128, 4096, 1024);
+                const uint32_t pcol = tbase + T::COL_P + 16 * bb;
+                tc_mma_ts(tbase, pcol, vdesc, T::IDESC_PV, jj > 0 ? 1u : 0u);
+                if constexpr (T::BF) tc_mma_ts(tbase, pcol + 8, vdesc, T::IDESC_PV, 1u);
+                tc_commit(&empty[jj % T::S]);
+                tc_commit(&p_free[bb]);
+                return true;
+            };
+            for (int jj = 0; jj < npages && ok; ++jj) {
+                const int s = jj % T::S, bb = jj & 1;
+                if (!mbar_wait(&full[s], (jj / T::S) & 1, deadline)) { ok = false; break; }
+                uint8_t* st = stages + s * T::STAGE;
+                const int key0 = jj * kBlockSize;
+                if (key0 + kBlockSize > total) {
+                    // keys past the sequence hold whatever the pool has there: zero
+                    // their V rows so that masked probabilities cannot meet NaN or Inf
+                    const int valid = total - key0;
+                    for (int c = 0; c < T::CH; ++c)
+                        for (int row = 16 + valid; row < 32; ++row)
+                            for (int u = 0; u < 8; ++u)
+                                *reinterpret_cast<uint4*>(st + c * 4096 + row * 128 + u * 16) = make_uint4(0, 0, 0, 0);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                }
+                if (jj >= 2 && !mbar_wait(&s_free[bb], ((jj - 2) >> 1) & 1, deadline)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(st);
 #pragma unroll
-    for (int nt = 0; nt < T::NO; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-
-    // ldmatrix lane geometry (as the decode): K rows feed the B operand of
-    // S = Q K^T (keys as N), V rows the B operand of O = P V through the
-    // transposing load
-    const int mi = lane >> 3;
-    const int k_tok = (lane & 7) + ((mi & 1) << 3), k_hs = mi >> 1;
-    const int v_tok = (lane & 7) + ((mi >> 1) << 3), v_hs = mi & 1;
-    bool alive = true;
-    for (int ii = 0; ii < npages && alive; ++ii) {
-        const int s = ii % T::S;
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (ii / T::S) & 1, deadline))) {
-            if (lane == 0) atomicOr(p.err, kDevErrTimeout);
-            alive = false;
-            break;
-        }
-        uint8_t* st = stages + s * T::STAGE;
-        const int key0 = ii * kBlockSize;
-        if (key0 + kBlockSize > total) {
-            // keys past the sequence hold whatever the pool has there: zero
-            // their V rows (every warp writes the same zeros before reading) so
-            // that masked probabilities cannot meet NaN or Inf
-            const int valid = total - key0;
-            const int per_row = T::CHUNKS * 8;
-            for (int k = lane; k < (16 - valid) * per_row; k += 32) {
-                const int piece = k % per_row, row = 16 + valid + k / per_row;
-                *reinterpret_cast<uint4*>(st + (piece >> 3) * 4096 + row * 128 + ((piece & 7) << 4)) =
-                    make_uint4(0, 0, 0, 0);
+                for (int kk = 0; kk < T::KSTEPS; ++kk) {
+                    const uint64_t adesc = smem_desc_sw128(qaddr + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bdesc = smem_desc_sw128(sa + (kk >> 2) * 4096 + (kk & 3) * 32, 16, 1024);
+                    tc_mma_ss(tbase + T::COL_S + 16 * bb, adesc, bdesc, T::IDESC_S, kk > 0 ? 1u : 0u);
+                }
+                tc_commit(&s_full[bb]);
+                if (jj >= 1 && !issue_pv(jj - 1)) { ok = false; break; }
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (ok && npages > 0) ok = issue_pv(npages - 1);
+            if (!ok) atomicOr(p.err, kDevErrTimeout);
+            // every MMA issued here completes before the epilogue reads O and
+            // before the tensor memory is freed
+            tc_commit(done);
+            if (!mbar_wait(done, 0, deadline)) atomicOr(p.err, kDevErrTimeout);
+        }
+    } else {
+        // ---- softmax warps: thread r owns query row r
+        const int r = threadIdx.x, tq = t0 + r;
+        const bool live = tq < n;
+        const int kend_r = live ? (p.causal ? cs + tq + 1 : total) : 0;
+        const uint32_t lanes = (uint32_t)(warp * 32) << 16;
+        float m_ref = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int jj = 0; jj < npages; ++jj) {
+            const int bb = jj & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[bb], (jj >> 1) & 1, deadline))) { ok = false; break; }
+            tc_fence_after();
+            uint32_t sr[16];
+            tmem_ld16(tbase + lanes + T::COL_S + 16 * bb, sr);
+            tmem_wait_ld();
+            tc_fence_before();
             __syncwarp();
-        }
-        const uint32_t tbase = smem_u32(st);
-        float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            if (lane == 0) mbar_arrive(&s_free[bb]);
+            const int key0 = jj * kBlockSize;
+            float xs[16], tmax = -INFINITY;
 #pragma unroll
-        for (int kt = 0; kt < T::KT; ++kt) {
-            uint32_t r0, r1, r2, r3;
-            ldsm_x4(tbase + (kt >> 2) * 4096 + k_tok * 128 + ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4),
-                    r0, r1, r2, r3);
-            // r0 / r2: keys 0-7 (d 0-7 / 8-15 of the k-step), r1 / r3: keys 8-15
-            mma_16816<T::MMA_BF16>(sa[0], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], r0, r2);
-            mma_16816<T::MMA_BF16>(sa[1], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], r1, r3);
-        }
-        // scores of rows g (sa[.][0..1]) and g+8 (sa[.][2..3]); keys key0 + 8*nh + 2c + e
-        float sv[2][4];
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int nh = 0; nh < 2; ++nh)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int key = key0 + nh * 8 + 2 * c + e;
-                sv[nh][e] = key < kend0 ? sa[nh][e] * p.scale_log2 : -INFINITY;
-                sv[nh][2 + e] = key < kend1 ? sa[nh][2 + e] * p.scale_log2 : -INFINITY;
-                mx0 = fmaxf(mx0, sv[nh][e]);
-                mx1 = fmaxf(mx1, sv[nh][2 + e]);
+            for (int k = 0; k < 16; ++k) {
+                xs[k] = key0 + k < kend_r ? __uint_as_float(sr[k]) * p.scale_log2 : -INFINITY;
+                tmax = fmaxf(tmax, xs[k]);
             }
-#pragma unroll
-        for (int off = 1; off < 4; off <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-        }
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        // a row with no key yet keeps the reference point 0 (its scores are -inf)
-        const float ref0 = mn0 == -INFINITY ? 0.0f : mn0, ref1 = mn1 == -INFINITY ? 0.0f : mn1;
-        const float al0 = ex2(m0 - ref0), al1 = ex2(m1 - ref1);
-        m0 = mn0;
-        m1 = mn1;
-        l0 *= al0;
-        l1 *= al1;
-#pragma unroll
-        for (int nt = 0; nt < T::NO; ++nt) {
-            o[nt][0] *= al0; o[nt][1] *= al0;
-            o[nt][2] *= al1; o[nt][3] *= al1;
-        }
-        float pr[2][4];
-#pragma unroll
-        for (int nh = 0; nh < 2; ++nh) {
-            pr[nh][0] = ex2(sv[nh][0] - ref0);
-            pr[nh][1] = ex2(sv[nh][1] - ref0);
-            pr[nh][2] = ex2(sv[nh][2] - ref1);
-            pr[nh][3] = ex2(sv[nh][3] - ref1);
-            l0 += pr[nh][0] + pr[nh][1];
-            l1 += pr[nh][2] + pr[nh][3];
-        }
-        // P as the A operand (16 tokens x 16 keys): the S fragments in place.
-        // A bf16 probability keeps 8 significant bits, too few where a row's
-        // output is a near-cancelling sum of a few large V terms; bf16 pages
-        // therefore add the rounding residual as a second operand (P = hi + lo,
-        // ~2^-18 relative), f16 pages keep P in f16 (11 bits).
-        uint32_t ph[4], pl[4] = {0u, 0u, 0u, 0u};
-        {
-            const float x[4][2] = {{pr[0][0], pr[0][1]}, {pr[0][2], pr[0][3]},
-                                   {pr[1][0], pr[1][1]}, {pr[1][2], pr[1][3]}};
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                ph[r] = pack2<T::MMA_BF16>(x[r][0], x[r][1]);
-                if constexpr (T::MMA_BF16)
-                    pl[r] = pack2<true>(x[r][0] - bf16_bits_to_f32(ph[r] & 0xFFFFu),
-                                        x[r][1] - bf16_bits_to_f32(ph[r] >> 16));
+            // P buffer bb is free once PV(jj-2) has completed; that also orders
+            // the wait for PV(jj-1) below (a parity wait needs the phase before)
+            if (jj >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_free[bb], ((jj - 2) >> 1) & 1, deadline))) {
+                ok = false;
+                break;
             }
-        }
-#pragma unroll
-        for (int mt = 0; mt < T::D / 16; ++mt) {
-            uint32_t r0, r1, r2, r3;
-            ldsm_x4_t(tbase + (mt >> 2) * 4096 + (16 + v_tok) * 128 +
-                          ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4),
-                      r0, r1, r2, r3);
-            // r0 / r2: d 16mt .. +7 for keys 0-7 / 8-15; r1 / r3: d 16mt + 8 .. +15
-            mma_16816<T::MMA_BF16>(o[2 * mt], ph[0], ph[1], ph[2], ph[3], r0, r2);
-            mma_16816<T::MMA_BF16>(o[2 * mt + 1], ph[0], ph[1], ph[2], ph[3], r1, r3);
-            if constexpr (T::MMA_BF16) {
-                mma_16816<true>(o[2 * mt], pl[0], pl[1], pl[2], pl[3], r0, r2);
-                mma_16816<true>(o[2 * mt + 1], pl[0], pl[1], pl[2], pl[3], r1, r3);
+            const bool need = tmax > m_ref + kTcRescale;
+            float alpha = 1.0f;
+            if (need) {
+                alpha = ex2(m_ref - tmax);      // 0 while the row had no key
+                m_ref = tmax;
             }
+            if (__any_sync(0xffffffffu, need && jj > 0)) {
+                // rescale O: after PV(jj-1), before PV(jj)
+                if (!__all_sync(0xffffffffu, mbar_wait(&p_free[bb ^ 1], ((jj - 1) >> 1) & 1, deadline))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c0 = 0; c0 < T::D; c0 += 16) {
+                    uint32_t o16[16];
+                    tmem_ld16(tbase + lanes + c0, o16);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) o16[k] = __float_as_uint(__uint_as_float(o16[k]) * alpha);
+                    tmem_st16(tbase + lanes + c0, o16);
+                }
+            }
+            l *= alpha;
+            const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
+            uint32_t ph[8], pl[8];
+            float ls = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float p0 = ex2(xs[2 * k] - mu), p1 = ex2(xs[2 * k + 1] - mu);
+                ls += p0 + p1;
+                ph[k] = pack2<T::BF>(p0, p1);
+                pl[k] = T::BF ? pack2<true>(p0 - bf16_bits_to_f32(ph[k] & 0xFFFFu),
+                                            p1 - bf16_bits_to_f32(ph[k] >> 16))
+                              : 0u;
+            }
+            l += ls;
+            tmem_st8(tbase + lanes + T::COL_P + 16 * bb, ph);
+            if constexpr (T::BF) tmem_st8(tbase + lanes + T::COL_P + 16 * bb + 8, pl);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[bb]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        // epilogue: O / l, after the last PV
+        if (ok && __all_sync(0xffffffffu, mbar_wait(done, 0, deadline))) {
+            tc_fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + ((size_t)(q_off + tq) * p.Hq + j) * T::D * 2;
+#pragma unroll 1
+            for (int c0 = 0; c0 < T::D; c0 += 16) {
+                uint32_t o16[16];
+                tmem_ld16(tbase + lanes + c0, o16);
+                tmem_wait_ld();
+                uint32_t w[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    w[k] = (uint32_t)pf_f32_to_io<T::IO>(__uint_as_float(o16[2 * k]) * inv) |
+                           ((uint32_t)pf_f32_to_io<T::IO>(__uint_as_float(o16[2 * k + 1]) * inv) << 16);
+                if (live) {
+                    *reinterpret_cast<uint4*>(dst + c0 * 2) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(dst + c0 * 2 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+            }
+        } else if (lane == 0) {
+            atomicOr(p.err, kDevErrTimeout);
+        }
     }
-    if (!alive) return;
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
-    uint8_t* obase = reinterpret_cast<uint8_t*>(p.out) + ((size_t)(q_off + t0 + 16 * warp) * p.Hq + j) * T::D * 2;
-#pragma unroll
-    for (int nt = 0; nt < T::NO; ++nt) {
-        const int d = nt * 8 + 2 * c;
-        if (live0)
-            *reinterpret_cast<uint32_t*>(obase + (size_t)g * row_stride + d * 2) =
-                (uint32_t)pf_f32_to_io<T::IO>(o[nt][0] * inv0) | ((uint32_t)pf_f32_to_io<T::IO>(o[nt][1] * inv0) << 16);
-        if (live1)
-            *reinterpret_cast<uint32_t*>(obase + (size_t)(g + 8) * row_stride + d * 2) =
-                (uint32_t)pf_f32_to_io<T::IO>(o[nt][2] * inv1) | ((uint32_t)pf_f32_to_io<T::IO>(o[nt][3] * inv1) << 16);
+    // tensor memory is freed by the warp that allocated it, after every use
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc(tbase, T::TMEM_COLS);
     }
 }
 
@@ -477,8 +530,8 @@ cudaError_t launch_t(const PrefillLaunch& L) {
         configured.store(true);
     }
     const PrefillParams& p = L.p;
-    // an upper bound on the query tiles: sum over b of ceil(n_b / 64) <= T / 64 + B
-    const uint32_t tiles = (p.T + kPfTile - 1) / kPfTile + p.B;
+    // an upper bound on the query tiles: sum over b of ceil(n_b / 128) <= T / 128 + B
+    const uint32_t tiles = (p.T + kTcRows - 1) / kTcRows + p.B;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles, p.Hq);
     cfg.blockDim = dim3(T::THREADS);
@@ -496,14 +549,14 @@ cudaError_t launch_t(const PrefillLaunch& L) {
 
 }  // namespace
 
-int prefill_query_tile() { return kPfTile; }
+int prefill_query_tile() { return kTcRows; }
 
 cudaError_t launch_paged_prefill(const PrefillLaunch& L) {
     if (L.kv_kind == kFP8) return cudaErrorNotSupported;
     if (L.head_dim == 128)
-        return L.io_kind == kBF16 ? launch_t<PfTraits<128, kBF16>>(L) : launch_t<PfTraits<128, kF16>>(L);
+        return L.io_kind == kBF16 ? launch_t<TcTraits<128, kBF16>>(L) : launch_t<TcTraits<128, kF16>>(L);
     if (L.head_dim == 64)
-        return L.io_kind == kBF16 ? launch_t<PfTraits<64, kBF16>>(L) : launch_t<PfTraits<64, kF16>>(L);
+        return L.io_kind == kBF16 ? launch_t<TcTraits<64, kBF16>>(L) : launch_t<TcTraits<64, kF16>>(L);
     return cudaErrorNotSupported;
 }
 
