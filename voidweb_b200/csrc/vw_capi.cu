@@ -86,7 +86,8 @@ struct vw_pool {
     float* scales = nullptr;
     bool own_data = false, own_scales = false;
     uint64_t data_bytes = 0, scale_bytes = 0;
-    alignas(64) CUtensorMap tmap;
+    alignas(64) CUtensorMap tmap;       // page-head boxes (decode)
+    alignas(64) CUtensorMap tmap_half;  // 16-row boxes of one 128-B column (prefill)
     float* part_o = nullptr;
     float* part_ml = nullptr;
     uint32_t* err = nullptr;
@@ -152,6 +153,16 @@ int32_t encode_pool_map(vw_pool* p) {
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(VW_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    // Second view for the prefill: token rows of head_dim elements; one box =
+    // 16 rows (the K or the V half of a page-head) of one 128-B column, so that
+    // the K rows of consecutive page-heads land 16 rows apart in one tile.
+    cuuint64_t dims2[2] = {(cuuint64_t)g.head_dim, rows};
+    cuuint64_t strides2[1] = {row};
+    cuuint32_t box2[2] = {(cuuint32_t)(128 / eb), 16};
+    r = fn(&p->tmap_half, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+           p->data, dims2, strides2, box2, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VW_ERR_CUDA, "cuTensorMapEncodeTiled (half) failed (%d)", (int)r);
     return VW_OK;
 }
 
@@ -470,7 +481,7 @@ int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) 
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.rope_theta = theta;
-    L.tmap = &pool->tmap;
+    L.tmap = &pool->tmap_half;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;
     L.io_kind = g.io_kind;

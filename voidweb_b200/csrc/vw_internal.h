@@ -81,7 +81,7 @@ struct PrefillParams {
 
 struct PrefillLaunch {
     PrefillParams p;
-    const CUtensorMap* tmap;    // the pool's page-head map (as for the decode)
+    const CUtensorMap* tmap;    // the pool's 16-row half-page-head map
     uint32_t head_dim, kv_kind, io_kind;
     cudaStream_t stream;
 };

@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(256) prefill_append_kernel(
 // ------------------------------------------------------------------ attention
 
 constexpr int kTcRows = 128;                      // query tokens per CTA: the MMA's M
-constexpr int kTcStages = 8;                      // page-head stages in the ring
+constexpr int kTcPages = 4;                       // page-heads per round (16 keys each)
 constexpr float kTcRescale = 8.0f;                // log2 units: p <= 2^8 against a stale max
 
 template <int D_, int IO_>
@@ -165,40 +165,51 @@ struct TcTraits {
     static constexpr int D = D_, IO = IO_;
     static constexpr bool BF = IO == kBF16;
     static constexpr int CH = D * 2 / 128;            // 128-B columns of a row
-    static constexpr int STAGE = 32 * D * 2;          // one page-head: K rows 0-15, V rows 16-31
-    static constexpr int S = kTcStages;
+    static constexpr int R = kTcPages;                // page-heads per round
+    static constexpr int KEYS = 16 * R;               // keys per round: the N of S = Q K^T
+    // round stages: the K rows and the V rows of a round's page-heads, each a tile
+    // [CH][KEYS rows][128 B] (128-B swizzled); head_dim 64 keeps more stages so
+    // that shared memory holds two CTAs per SM, which is what tensor memory allows
+    static constexpr int NST = D == 128 ? 2 : 4;
+    static constexpr int TILE = CH * KEYS * 128;      // bytes of one K (or V) tile
+    static constexpr int STAGE = 2 * TILE;            // K tile, then V tile
+    static constexpr int HALF_BOX = 16 * 128;         // one TMA box: 16 rows of one column
     static constexpr int QBYTES = kTcRows * D * 2;    // query tile [CH][128 rows][128 B]
-    static constexpr int KSTEPS = D / 16;             // MMAs of S = Q K^T per page
-    // tensor memory: O in columns [0, D), S buffers at D and D + 16 (16 f32
-    // columns each), P buffers at D + 32 and D + 48 (8 columns of bf16/f16 pairs,
-    // then 8 more for the low part of bf16 probabilities)
-    static constexpr int COL_S = D, COL_P = D + 32;
-    static constexpr uint32_t TMEM_COLS = D == 128 ? 256u : 128u;
+    static constexpr int KSTEPS = D / 16;             // MMAs of S = Q K^T per round
+    // tensor memory: O in columns [0, D); two S buffers of KEYS f32 columns.  P
+    // (bf16/f16 pairs: KEYS/2 columns, then KEYS/2 for the low part of bf16
+    // probabilities) is written over the S buffer it was computed from.
+    static constexpr int COL_S = D;
+    static constexpr uint32_t TMEM_COLS = 256u;       // two CTAs per SM share the 512 columns
     static constexpr int TPFX = pf_align((kMaxBatchPerLaunch + 1) * 4, 128);
-    static constexpr int NBAR = 2 * S + 9;            // full, empty; s_full/s_free/p_full/p_free x2; done
-    static constexpr int SMEM = 1024 + QBYTES + S * STAGE + TPFX + NBAR * 8 + 16;
+    static constexpr int NBAR = 2 * NST + 7;          // full, empty; s_full/p_full/p_free x2; done
+    static constexpr int SMEM = 1024 + QBYTES + NST * STAGE + TPFX + NBAR * 8 + 16;
     static constexpr int THREADS = 6 * 32;            // 4 softmax warps, 1 MMA warp, 1 producer warp
-    static constexpr uint32_t IDESC_S = idesc_f16(BF, false, kTcRows, 16);
+    static constexpr uint32_t IDESC_S = idesc_f16(BF, false, kTcRows, KEYS);
     static constexpr uint32_t IDESC_PV = idesc_f16(BF, true, kTcRows, D);
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-    static_assert(COL_P + 32 <= (int)TMEM_COLS, "tensor-memory columns");
-    static_assert(STAGE % 1024 == 0 && QBYTES % 1024 == 0, "1024-B alignment (128-B swizzle)");
+    static_assert(COL_S + 2 * KEYS <= (int)TMEM_COLS, "tensor-memory columns");
+    static_assert(STAGE % 1024 == 0 && QBYTES % 1024 == 0 && TILE % 1024 == 0, "1024-B alignment");
+    static_assert(3 * (SMEM + 1024) > 233472, "at most two CTAs per SM (tensor memory)");
 };
 
 // CTA (tile, q head): 128 query tokens of one sequence for one query head.
+//  * warp 5 (producer): per round of R page-heads, two TMA boxes per 128-B
+//    column of each page-head, its 16 K rows into the round's K tile and its 16
+//    V rows into the V tile, so that the keys of the round are R*16 rows with a
+//    uniform stride in both tiles.
+//  * warp 4: allocates tensor memory; one lane issues per round t
+//    S_t = Q K_t^T (D/16 MMAs, M = 128, N = R*16 keys, K = 16; both operands
+//    128-B-swizzled K-major shared-memory tiles) into S buffer t%2, then
+//    O += P_{t-1} V_{t-1} (per page-head: M = 128, N = D, K = 16 keys; A = P
+//    from tensor memory, B = the V tile rows as an MN-major operand).  S_t is
+//    issued only after P_{t-2}'s MMAs completed, since P_{t-2} occupies the
+//    buffer.  Commits release the round stage, the buffer and the epilogue.
 //  * warps 0-3 (thread r = query row r = tensor-memory lane r): load and
-//    (RoPE-)rotate the query rows into a 128-B-swizzled K-major tile, then per
-//    page read S from tensor memory, mask, run the online softmax with a lazily
-//    raised maximum (O in tensor memory is rescaled only when a row's maximum
-//    grows by more than 2^8) and write P back to tensor memory; finally read O,
-//    divide by the row sum and store the rows.
-//  * warp 4: allocates tensor memory and one lane issues, per page-head j,
-//    S_j = Q K_j^T (D/16 MMAs, M = 128, N = 16 keys, K = 16) into S buffer j%2,
-//    then O += P_{j-1} V_{j-1} (M = 128, N = D, K = 16 keys; A = P from tensor
-//    memory, B = the staged V rows as an MN-major operand), so the MMAs of one
-//    page overlap the softmax of the previous one.  Commits release the stage,
-//    the P buffer and, at the end, the epilogue.
-//  * warp 5: the TMA producer of page-heads (as the decode).
+//    (RoPE-)rotate the query rows into the swizzled K-major tile; per round read
+//    S, mask, run the online softmax with a lazily raised maximum (O in tensor
+//    memory is rescaled only when a row's maximum grows by more than 2^8) and
+//    write P over S; finally read O, divide by the row sum and store the rows.
 template <class T>
 __global__ void __launch_bounds__(T::THREADS, 2)
 prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) {
@@ -207,12 +218,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* qs = base;
     uint8_t* stages = base + T::QBYTES;
-    int* tpfx = reinterpret_cast<int*>(stages + T::S * T::STAGE);
+    int* tpfx = reinterpret_cast<int*>(stages + T::NST * T::STAGE);
     uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tpfx) + T::TPFX);
-    uint64_t* empty = full + T::S;
-    uint64_t* s_full = empty + T::S;
-    uint64_t* s_free = s_full + 2;
-    uint64_t* p_full = s_free + 2;
+    uint64_t* empty = full + T::NST;
+    uint64_t* s_full = empty + T::NST;
+    uint64_t* p_full = s_full + 2;
     uint64_t* p_free = p_full + 2;
     uint64_t* done = p_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -220,10 +230,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     const uint64_t deadline = cycles() + kWaitDeadlineCycles;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < T::S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < T::NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&s_free[b], 4);
             mbar_init(&p_full[b], 4);
             mbar_init(&p_free[b], 1);
         }
@@ -270,6 +279,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     const int qmax = cs + min(t0 + kTcRows - 1, n - 1);          // last query position of the tile
     const int kend = p.causal ? qmax + 1 : total;                // keys [0, kend)
     const int npages = (kend + kBlockSize - 1) / kBlockSize;
+    const int nrounds = (npages + T::R - 1) / T::R;
     const int j = blockIdx.y, h = j / (int)p.group;
 
     if (warp == 4) {
@@ -320,41 +330,42 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     const uint32_t tbase = *tmem_slot;
 
     if (warp == 5) {
-        // ---- producer: block ids 32 at a time, lane 0 issues one box per page-head
+        // ---- producer: round t into stage t % NST, R page-heads
         bool ok = true;
-        for (int i0 = 0; i0 < npages && ok; i0 += 32) {
-            const int m = min(32, npages - i0);
+        for (int t = 0; t < nrounds && ok; ++t) {
+            const int st_i = t % T::NST;
+            const int pg0 = t * T::R, m = min(T::R, npages - pg0);
             uint32_t blk = 0xFFFFFFFFu;
-            if (lane < m) blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + i0 + lane);
-            for (int jj = 0; jj < m; ++jj) {
-                const uint32_t bj = __shfl_sync(0xffffffffu, blk, jj);
-                if (lane == 0 && ok) {
-                    const int ii = i0 + jj, s = ii % T::S;
-                    if (ii >= T::S && !mbar_wait(&empty[s], ((ii / T::S) - 1) & 1, deadline)) {
-                        ok = false;
-                    } else {
-                        int row0 = -32;                  // negative row: TMA zero-fills
-                        if (bj < p.num_blocks)
-                            row0 = (int)(((p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 32u);
-                        else
-                            atomicOr(p.err, kDevErrBlockId);
-                        mbar_arrive_expect_tx(&full[s], T::STAGE);
-                        uint8_t* st = stages + s * T::STAGE;
-                        if constexpr (T::CH == 1)
-                            tma_load_2d(st, &tmap, &full[s], 0, row0);
-                        else
-                            tma_load_3d(st, &tmap, &full[s], 0, row0, 0);
+            if (lane < m) blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg0 + lane);
+            if (lane == 0) {
+                if (t >= T::NST && !mbar_wait(&empty[st_i], ((t / T::NST) - 1) & 1, deadline)) ok = false;
+                if (ok) mbar_arrive_expect_tx(&full[st_i], (uint32_t)(m * 2 * T::CH * T::HALF_BOX));
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            uint8_t* kt = stages + st_i * T::STAGE;
+            for (int pg = 0; pg < m && ok; ++pg) {
+                const uint32_t bj = __shfl_sync(0xffffffffu, blk, pg);
+                if (lane == 0) {
+                    int row0 = -32;                      // negative rows: TMA zero-fills
+                    if (bj < p.num_blocks)
+                        row0 = (int)(((p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 32u);
+                    else
+                        atomicOr(p.err, kDevErrBlockId);
+#pragma unroll
+                    for (int c = 0; c < T::CH; ++c) {
+                        uint8_t* kd = kt + c * (T::KEYS * 128) + pg * T::HALF_BOX;
+                        tma_load_2d(kd, &tmap, &full[st_i], c * 64, row0);
+                        tma_load_2d(kd + T::TILE, &tmap, &full[st_i], c * 64, row0 + 16);
                     }
                 }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
             }
         }
         if (lane == 0) {
             if (!ok) atomicOr(p.err, kDevErrTimeout);
             // drain: no TMA write may land after the CTA has exited
-            const int issued = ok ? npages : 0;
-            for (int ii = issued > T::S ? issued - T::S : 0; ii < issued; ++ii)
-                if (!mbar_wait(&full[ii % T::S], (ii / T::S) & 1, deadline)) {
+            const int issued = ok ? nrounds : 0;
+            for (int t = issued > T::NST ? issued - T::NST : 0; t < issued; ++t)
+                if (!mbar_wait(&full[t % T::NST], (t / T::NST) & 1, deadline)) {
                     atomicOr(p.err, kDevErrTimeout);
                     break;
                 }
@@ -363,49 +374,61 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         // ---- MMA issuer
         if (lane == 0) {
             bool ok = true;
-            const uint32_t qaddr = smem_u32(qs);
-            auto issue_pv = [&](int jj) -> bool {
-                const int bb = jj & 1;
-                if (!mbar_wait(&p_full[bb], (jj >> 1) & 1, deadline)) return false;
+            // descriptors: the query tile's per k-step (fixed), and per stage a base
+            // to which a k-step adds (kk / 4) * column + (kk % 4) * 32 bytes (>> 4 in
+            // the address field, which never carries: shared memory ends below 256 KB)
+            uint64_t qdesc[T::KSTEPS];
+#pragma unroll
+            for (int kk = 0; kk < T::KSTEPS; ++kk)
+                qdesc[kk] = smem_desc_sw128(smem_u32(qs) + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, 16, 1024);
+            // K tile: K-major, 8-key groups 1024 B apart; V tile: MN-major, 64-element
+            // columns KEYS*128 B apart, 8-key groups 1024 B apart
+            const uint64_t kdesc0 = smem_desc_sw128(smem_u32(stages), 16, 1024);
+            const uint64_t vdesc0 = smem_desc_sw128(smem_u32(stages) + T::TILE, T::KEYS * 128, 1024);
+            auto issue_pv = [&](int t) -> bool {
+                const int bb = t & 1, st_i = t % T::NST;
+                if (!mbar_wait(&p_full[bb], (t >> 1) & 1, deadline)) return false;
                 tc_fence_after();
-                const uint32_t st = smem_u32(stages + (jj % T::S) * T::STAGE);
-                // V rows 16-31: MN-major, 64-element columns 4096 B apart, 8-key groups 1024 B apart
-                const uint64_t vdesc = smem_desc_sw128(st + 16 * 128, 4096, 1024);
-                const uint32_t pcol = tbase + T::COL_P + 16 * bb;
-                tc_mma_ts(tbase, pcol, vdesc, T::IDESC_PV, jj > 0 ? 1u : 0u);
-                if constexpr (T::BF) tc_mma_ts(tbase, pcol + 8, vdesc, T::IDESC_PV, 1u);
-                tc_commit(&empty[jj % T::S]);
+                const uint32_t pcol = tbase + T::COL_S + T::KEYS * bb;
+                const uint64_t vst = vdesc0 + (uint64_t)((st_i * T::STAGE) >> 4);
+                for (int pg = 0; pg < T::R && t * T::R + pg < npages; ++pg) {
+                    const uint64_t vdesc = vst + (uint64_t)((pg * T::HALF_BOX) >> 4);
+                    tc_mma_ts(tbase, pcol + 8 * pg, vdesc, T::IDESC_PV, (t > 0 || pg > 0) ? 1u : 0u);
+                    if constexpr (T::BF) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
+                }
+                tc_commit(&empty[st_i]);
                 tc_commit(&p_free[bb]);
                 return true;
             };
-            for (int jj = 0; jj < npages && ok; ++jj) {
-                const int s = jj % T::S, bb = jj & 1;
-                if (!mbar_wait(&full[s], (jj / T::S) & 1, deadline)) { ok = false; break; }
-                uint8_t* st = stages + s * T::STAGE;
-                const int key0 = jj * kBlockSize;
-                if (key0 + kBlockSize > total) {
-                    // keys past the sequence hold whatever the pool has there: zero
-                    // their V rows so that masked probabilities cannot meet NaN or Inf
-                    const int valid = total - key0;
+            for (int t = 0; t < nrounds && ok; ++t) {
+                const int bb = t & 1, st_i = t % T::NST;
+                if (!mbar_wait(&full[st_i], (t / T::NST) & 1, deadline)) { ok = false; break; }
+                const int keyl = total - t * T::KEYS;   // keys of the round inside the sequence
+                if (keyl < T::KEYS && keyl > 0 && (keyl & 15)) {
+                    // the page-head holding the sequence's last key: its V rows past
+                    // the end hold whatever the pool has there; zero them so that
+                    // masked probabilities cannot meet NaN or Inf
+                    uint8_t* vt = stages + st_i * T::STAGE + T::TILE;
                     for (int c = 0; c < T::CH; ++c)
-                        for (int row = 16 + valid; row < 32; ++row)
+                        for (int row = keyl; row < ((keyl + 15) & ~15); ++row)
                             for (int u = 0; u < 8; ++u)
-                                *reinterpret_cast<uint4*>(st + c * 4096 + row * 128 + u * 16) = make_uint4(0, 0, 0, 0);
+                                *reinterpret_cast<uint4*>(vt + c * (T::KEYS * 128) + row * 128 + u * 16) =
+                                    make_uint4(0, 0, 0, 0);
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
-                if (jj >= 2 && !mbar_wait(&s_free[bb], ((jj - 2) >> 1) & 1, deadline)) { ok = false; break; }
+                // buffer bb holds P_{t-2} until its MMAs complete
+                if (t >= 2 && !mbar_wait(&p_free[bb], ((t - 2) >> 1) & 1, deadline)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sa = smem_u32(st);
+                const uint64_t kst = kdesc0 + (uint64_t)((st_i * T::STAGE) >> 4);
+                const uint32_t dcol = tbase + T::COL_S + T::KEYS * bb;
 #pragma unroll
-                for (int kk = 0; kk < T::KSTEPS; ++kk) {
-                    const uint64_t adesc = smem_desc_sw128(qaddr + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bdesc = smem_desc_sw128(sa + (kk >> 2) * 4096 + (kk & 3) * 32, 16, 1024);
-                    tc_mma_ss(tbase + T::COL_S + 16 * bb, adesc, bdesc, T::IDESC_S, kk > 0 ? 1u : 0u);
-                }
+                for (int kk = 0; kk < T::KSTEPS; ++kk)
+                    tc_mma_ss(dcol, qdesc[kk], kst + (uint64_t)(((kk >> 2) * (T::KEYS * 128) + (kk & 3) * 32) >> 4),
+                              T::IDESC_S, kk > 0 ? 1u : 0u);
                 tc_commit(&s_full[bb]);
-                if (jj >= 1 && !issue_pv(jj - 1)) { ok = false; break; }
+                if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
             }
-            if (ok && npages > 0) ok = issue_pv(npages - 1);
+            if (ok && nrounds > 0) ok = issue_pv(nrounds - 1);
             if (!ok) atomicOr(p.err, kDevErrTimeout);
             // every MMA issued here completes before the epilogue reads O and
             // before the tensor memory is freed
@@ -420,38 +443,47 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         const uint32_t lanes = (uint32_t)(warp * 32) << 16;
         float m_ref = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (int jj = 0; jj < npages; ++jj) {
-            const int bb = jj & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[bb], (jj >> 1) & 1, deadline))) { ok = false; break; }
+        for (int t = 0; t < nrounds; ++t) {
+            const int bb = t & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[bb], (t >> 1) & 1, deadline))) { ok = false; break; }
             tc_fence_after();
-            uint32_t sr[16];
-            tmem_ld16(tbase + lanes + T::COL_S + 16 * bb, sr);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[bb]);
-            const int key0 = jj * kBlockSize;
-            float xs[16], tmax = -INFINITY;
+            float xs[T::KEYS];
+            {
+                uint32_t sr[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                xs[k] = key0 + k < kend_r ? __uint_as_float(sr[k]) * p.scale_log2 : -INFINITY;
-                tmax = fmaxf(tmax, xs[k]);
+                for (int c16 = 0; c16 < T::KEYS / 16; ++c16) {
+                    tmem_ld16(tbase + lanes + T::COL_S + T::KEYS * bb + 16 * c16, sr);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) xs[16 * c16 + k] = __uint_as_float(sr[k]);
+                }
             }
-            // P buffer bb is free once PV(jj-2) has completed; that also orders
-            // the wait for PV(jj-1) below (a parity wait needs the phase before)
-            if (jj >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_free[bb], ((jj - 2) >> 1) & 1, deadline))) {
-                ok = false;
-                break;
+            // keys of page-heads past npages are stale rows; they lie past kend_r.
+            // Scores stay unscaled here (scale > 0 keeps the order); the scale is
+            // folded into the exponent below.
+            const int key0 = t * T::KEYS;
+            float tmax = -INFINITY;
+            if (__all_sync(0xffffffffu, key0 + T::KEYS <= kend_r)) {
+#pragma unroll
+                for (int k = 0; k < T::KEYS; ++k) tmax = fmaxf(tmax, xs[k]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < T::KEYS; ++k) {
+                    xs[k] = key0 + k < kend_r ? xs[k] : -INFINITY;
+                    tmax = fmaxf(tmax, xs[k]);
+                }
             }
+            tmax *= p.scale_log2;
             const bool need = tmax > m_ref + kTcRescale;
             float alpha = 1.0f;
             if (need) {
                 alpha = ex2(m_ref - tmax);      // 0 while the row had no key
                 m_ref = tmax;
             }
-            if (__any_sync(0xffffffffu, need && jj > 0)) {
-                // rescale O: after PV(jj-1), before PV(jj)
-                if (!__all_sync(0xffffffffu, mbar_wait(&p_free[bb ^ 1], ((jj - 1) >> 1) & 1, deadline))) {
+            if (__any_sync(0xffffffffu, need && t > 0)) {
+                // rescale O: after PV(t-1) (whose phase is the next of its buffer:
+                // S_t was issued after PV(t-2) completed), before PV(t)
+                if (!__all_sync(0xffffffffu, mbar_wait(&p_free[bb ^ 1], ((t - 1) >> 1) & 1, deadline))) {
                     ok = false;
                     break;
                 }
@@ -468,20 +500,24 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
             }
             l *= alpha;
             const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
-            uint32_t ph[8], pl[8];
             float ls = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float p0 = ex2(xs[2 * k] - mu), p1 = ex2(xs[2 * k + 1] - mu);
-                ls += p0 + p1;
-                ph[k] = pack2<T::BF>(p0, p1);
-                pl[k] = T::BF ? pack2<true>(p0 - bf16_bits_to_f32(ph[k] & 0xFFFFu),
-                                            p1 - bf16_bits_to_f32(ph[k] >> 16))
-                              : 0u;
+            for (int c8 = 0; c8 < T::KEYS / 16; ++c8) {
+                uint32_t ph[8], pl[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float p0 = ex2(fmaf(xs[16 * c8 + 2 * k], p.scale_log2, -mu));
+                    const float p1 = ex2(fmaf(xs[16 * c8 + 2 * k + 1], p.scale_log2, -mu));
+                    ls += p0 + p1;
+                    ph[k] = pack2<T::BF>(p0, p1);
+                    pl[k] = T::BF ? pack2<true>(p0 - bf16_bits_to_f32(ph[k] & 0xFFFFu),
+                                                p1 - bf16_bits_to_f32(ph[k] >> 16))
+                                  : 0u;
+                }
+                tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + 8 * c8, ph);
+                if constexpr (T::BF) tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + T::KEYS / 2 + 8 * c8, pl);
             }
             l += ls;
-            tmem_st8(tbase + lanes + T::COL_P + 16 * bb, ph);
-            if constexpr (T::BF) tmem_st8(tbase + lanes + T::COL_P + 16 * bb + 8, pl);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
