@@ -314,6 +314,70 @@ VW_API void vw_radix_unlock(vw_radix* r, const uint32_t* tokens, uint32_t n);
 /* Rename block ids after a compaction: every id equal to pairs[i].src becomes pairs[i].dst. */
 VW_API void vw_radix_remap(vw_radix* r, const uint32_t* pairs, uint32_t num_pairs);
 
+/* ---- Continuous-batching scheduler wired to the block manager ---------------
+ * scheduler/scheduler.bm:186-293 (FCFS waiting queue, running set, a prefill
+ * token budget per step, chunks of at most max_chunk prompt tokens, one decode
+ * token per running sequence; engine/engine.bm:127-146 runs schedule -> forward
+ * -> sample -> commit) with the KV bookkeeping the reference leaves out: block
+ * tables allocated from the block manager, prefix reuse of full 16-token pages
+ * through the chained prefix hash (kv_cache.bm:127-164; the index holds one
+ * reference per kept page and releases the least recently used ones when the
+ * pool runs out), copy-on-write pairs for shared pages a step writes,
+ * preemption (recompute) of the youngest request when a decode cannot get a
+ * page, and continuation of prompts longer than one chunk.  The block
+ * manager is the caller's (one per pool); the scheduler only calls it. */
+typedef struct vw_sched vw_sched;
+typedef struct {
+    uint32_t max_batch_tokens;     /* prefill tokens per step (engine.bm:115 uses 8192) */
+    uint32_t max_running_seqs;     /* engine.bm:116 uses 256 */
+    uint32_t max_chunk;            /* scheduler.bm:255 uses 2048 */
+    uint32_t max_seq_len;          /* prompt + new tokens of one request */
+    uint32_t prefix_cache;         /* 1: reuse and keep full pages by prefix hash */
+    uint32_t reserved;             /* must be 0 */
+} vw_sched_config;
+typedef struct {                   /* one sequence of a step, in descriptor order */
+    uint64_t seq_id;
+    uint32_t is_prefill;           /* 1: a prompt chunk, 0: a decode (1 token) */
+    uint32_t num_tokens;           /* tokens appended this step */
+    uint32_t ctx_start;            /* tokens already cached = the first token's position */
+    uint32_t samples;              /* 1: commit the token sampled from this step's last row */
+    uint32_t token_offset;         /* index of the first token in the batch's tokens[] */
+    uint32_t reserved;
+} vw_sched_seq;
+typedef struct {                   /* arrays owned by the scheduler, valid until its next call */
+    uint32_t num_seqs;
+    uint32_t table_stride;
+    const vw_sched_seq* seqs;      /* prefill chunks first, then decodes */
+    const uint32_t* tokens;        /* the step's input tokens */
+    const uint32_t* block_tables;  /* [num_seqs][table_stride], covering ctx_start + num_tokens */
+    uint32_t num_copies;
+    uint32_t reserved;
+    const uint32_t* copies;        /* [num_copies][2] (src, dst): vw_block_copy before the step */
+} vw_sched_batch;
+typedef struct {
+    uint32_t waiting, running, finished;
+    uint32_t cached_pages;         /* pages the prefix index keeps (one reference each) */
+    uint32_t table_refs;           /* block-table entries of the running requests */
+    uint32_t free_blocks;
+    uint32_t preemptions;
+    uint32_t reserved;
+} vw_sched_stat;
+VW_API int32_t vw_sched_create(const vw_sched_config* cfg, vw_block_manager* bm, vw_sched** out);
+VW_API int32_t vw_sched_destroy(vw_sched* s);     /* releases every page it holds */
+/* scheduler.bm:230-235; stop_token < 0: none (Request::is_done, scheduler.bm:85-95) */
+VW_API int32_t vw_sched_add_request(vw_sched* s, const uint32_t* prompt, uint32_t n,
+                                    uint32_t max_new_tokens, int64_t stop_token, uint64_t* id_out);
+/* scheduler.bm:241-293 plus the bookkeeping above */
+VW_API int32_t vw_sched_schedule(vw_sched* s, vw_sched_batch* out);
+/* scheduler.bm:296-319: every scheduled sequence's tokens are cached; (ids[i],
+ * tokens[i]) are the tokens sampled for the sequences with samples = 1. */
+VW_API int32_t vw_sched_commit(vw_sched* s, const uint64_t* ids, const uint32_t* tokens, uint32_t n);
+/* scheduler.bm:322-326, one request at a time: its id and output tokens (up to
+ * cap); VW_ERR_INVALID_ARG when none is finished. */
+VW_API int32_t vw_sched_take_finished(vw_sched* s, uint64_t* id, uint32_t* out_tokens, uint32_t cap,
+                                      uint32_t* num_out);
+VW_API int32_t vw_sched_stats(const vw_sched* s, vw_sched_stat* st);
+
 /* Message for the last failure on this thread ("" if none). */
 VW_API const char* vw_last_error(void);
 

@@ -65,6 +65,27 @@ class PrefillArgs(ctypes.Structure):
                 ("out", vp), ("scale", f32), ("rope_theta", f32)]
 
 
+class SchedConfig(ctypes.Structure):
+    _fields_ = [("max_batch_tokens", u32), ("max_running_seqs", u32), ("max_chunk", u32),
+                ("max_seq_len", u32), ("prefix_cache", u32), ("reserved", u32)]
+
+
+class SchedSeq(ctypes.Structure):
+    _fields_ = [("seq_id", u64), ("is_prefill", u32), ("num_tokens", u32), ("ctx_start", u32),
+                ("samples", u32), ("token_offset", u32), ("reserved", u32)]
+
+
+class SchedBatch(ctypes.Structure):
+    _fields_ = [("num_seqs", u32), ("table_stride", u32), ("seqs", ctypes.POINTER(SchedSeq)),
+                ("tokens", ctypes.POINTER(u32)), ("block_tables", ctypes.POINTER(u32)),
+                ("num_copies", u32), ("reserved", u32), ("copies", ctypes.POINTER(u32))]
+
+
+class SchedStat(ctypes.Structure):
+    _fields_ = [("waiting", u32), ("running", u32), ("finished", u32), ("cached_pages", u32),
+                ("table_refs", u32), ("free_blocks", u32), ("preemptions", u32), ("reserved", u32)]
+
+
 class SeqDescriptor(ctypes.Structure):
     """engine/ffi.bm:15-24 (#[repr(C)] #[packed], 33 bytes)."""
     _pack_ = 1
@@ -91,6 +112,13 @@ SIGNATURES = {
     "vw_kv_append": (i32, [vp, u32, vp, vp, vp, u32, vp]),
     "vw_paged_decode": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
     "vw_paged_prefill": (i32, [vp, ctypes.POINTER(PrefillArgs), vp]),
+    "vw_sched_create": (i32, [ctypes.POINTER(SchedConfig), vp, ctypes.POINTER(vp)]),
+    "vw_sched_destroy": (i32, [vp]),
+    "vw_sched_add_request": (i32, [vp, vp, u32, u32, ctypes.c_int64, ctypes.POINTER(u64)]),
+    "vw_sched_schedule": (i32, [vp, ctypes.POINTER(SchedBatch)]),
+    "vw_sched_commit": (i32, [vp, vp, vp, u32]),
+    "vw_sched_take_finished": (i32, [vp, ctypes.POINTER(u64), vp, u32, ctypes.POINTER(u32)]),
+    "vw_sched_stats": (i32, [vp, ctypes.POINTER(SchedStat)]),
     "vw_decode_plan": (i32, [vp, vp, vp, u32, u32, u32, vp]),
     "vw_paged_decode_static": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
     "vw_block_copy": (i32, [vp, vp, u32, vp]),
