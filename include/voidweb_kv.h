@@ -256,6 +256,23 @@ typedef struct {
 
 VW_API int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* args, void* stream);
 
+/* ---- FP8 weight path sharing the KV codec ---------------------------------------
+ * rms_norm_fp8_out (kernels/norm/rms_norm.bm:62-94): x, weight f16
+ * [rows][hidden] / [hidden] -> out E4M3 codes [rows][hidden] of
+ * ((x * inv_rms) * w) * scale through the reference encoder, in the reference's
+ * operation order (codes bit-exact). */
+VW_API int32_t vw_rms_norm_fp8_out(const void* x, const void* weight, uint8_t* out, uint32_t rows,
+                                   uint32_t hidden, float scale, float eps, void* stream);
+/* gemm_fp8 (kernels/gemm/gemm_fp8.bm:31-107): C [M][N] bf16 = (a_scale *
+ * b_scale) * (A . B) + bias, A [M][K] and B [K][N] E4M3 codes row-major decoded
+ * as the reference decoder does (gemm_fp8.bm:110-116), bias bf16 [N] or NULL.
+ * N and K multiples of 16; a, b, c 16-byte aligned.  tcgen05 tensor cores. */
+VW_API int32_t vw_gemm_fp8(const uint8_t* a, const uint8_t* b, void* c, const void* bias, uint32_t M,
+                           uint32_t N, uint32_t K, float a_scale, float b_scale, void* stream);
+/* Synchronises, returns and clears the device error word of the two calls above
+ * (VW_DEV_ERR_TIMEOUT); VW_ERR_DEVICE_CHECK when it was nonzero. */
+VW_API int32_t vw_fp8_weight_check(uint32_t* device_error);
+
 /* ---- Host block manager (engine/kv_cache.bm:29-164, C++ implementation) ---- */
 typedef struct vw_block_manager vw_block_manager;
 /* kv_cache.bm:41-58: free list 0..max_blocks, the next alloc pops the last. */

@@ -63,6 +63,8 @@ def lib() -> ctypes.CDLL:
             "vwo_paged_prefill_f64": (i32, [vp, vp, vp, u32, vp, u32, vp, vp, vp, u32, u32,
                                             ctypes.c_int, f64, vp, ctypes.c_int]),
             "vwo_rope_apply": (None, [vp, u32, u32, u32, vp, f32, u32]),
+            "vwo_rms_norm_fp8_out": (None, [vp, vp, u32, u32, f32, f32, vp]),
+            "vwo_gemm_fp8_f64": (None, [vp, vp, vp, u32, u32, u32, f32, f32, vp, ctypes.c_int]),
             "vwo_rolling_hash": (u64, [u64, vp, u32]),
             "vwo_bm_new": (vp, [u32, u32]), "vwo_bm_delete": (None, [vp]),
             "vwo_bm_capacity": (u32, [vp]), "vwo_bm_free_count": (u32, [vp]),
@@ -260,6 +262,29 @@ def paged_prefill_f64(g: Geom, data, scales, layer, q, Hq, block_tables, cu_q, c
     out = np.zeros((int(np.asarray(cu_q)[-1]), Hq, g.head_dim), dtype=np.float64)
     return _prefill(lib().vwo_paged_prefill_f64, g, data, scales, layer, q, Hq, block_tables, cu_q,
                     ctx_start, causal, scale, out, nthreads)
+
+
+def rms_norm_fp8_out(x_f16: np.ndarray, weight_f16: np.ndarray, scale: float, eps: float) -> np.ndarray:
+    """rms_norm.bm:62-94: rows of f16 bits -> E4M3 codes (reference encoder)."""
+    x = np.ascontiguousarray(x_f16, dtype=np.uint16)
+    w = np.ascontiguousarray(weight_f16, dtype=np.uint16)
+    rows, hidden = x.shape
+    out = np.zeros((rows, hidden), dtype=np.uint8)
+    lib().vwo_rms_norm_fp8_out(_p(x), _p(w), rows, hidden, scale, eps, _p(out))
+    return out
+
+
+def gemm_fp8_f64(a: np.ndarray, b: np.ndarray, bias_bf16, a_scale: float, b_scale: float,
+                 nthreads: int = 0) -> np.ndarray:
+    """gemm_fp8.bm:31-107 in f64: A [M][K], B [K][N] E4M3 codes -> C [M][N]."""
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    M, K = a.shape
+    N = b.shape[1]
+    bias = None if bias_bf16 is None else np.ascontiguousarray(bias_bf16, dtype=np.uint16)
+    c = np.zeros((M, N), dtype=np.float64)
+    lib().vwo_gemm_fp8_f64(_p(a), _p(b), _p(bias), M, N, K, a_scale, b_scale, _p(c), nthreads)
+    return c
 
 
 def rolling_hash(prev: int, tokens) -> int:

@@ -515,6 +515,71 @@ int vwo_paged_prefill_f64(const vwo_geom* g, const void* data, const float* scal
 }
 
 // ---------------------------------------------------------------------------
+// FP8 weight path (kernels/norm/rms_norm.bm:62-94, kernels/gemm/gemm_fp8.bm:31-107)
+// ---------------------------------------------------------------------------
+
+// rms_norm_fp8_out (rms_norm.bm:62-94) for `rows` rows of `hidden` f16 values:
+// one warp per row in the reference, so the sum of squares is restated in
+// its order -- lane l sums x[l], x[l+32], ... in f32 (:73-77), then the
+// butterfly shuffles add the partner lane's sum at distances 16, 8, 4, 2, 1
+// (:79-83; every lane ends with the same value) -- then
+// inv_rms = 1 / sqrt(sum / hidden + eps) (:85) and each element
+// ((x * inv_rms) * w) * scale (:90, left to right) goes through the reference
+// encoder (:98-113).  x, weight: f16 bits; out: E4M3 codes.
+void vwo_rms_norm_fp8_out(const uint16_t* x, const uint16_t* weight, uint32_t rows,
+                          uint32_t hidden, float scale, float eps, uint8_t* out) {
+    for (uint32_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + (size_t)r * hidden;
+        float part[32];
+        for (uint32_t l = 0; l < 32; ++l) {
+            float acc = 0.0f;
+            for (uint32_t d = l; d < hidden; d += 32) {
+                const float v = vwo_f16_to_f32(xr[d]);
+                acc += v * v;
+            }
+            part[l] = acc;
+        }
+        for (uint32_t off = 16; off >= 1; off >>= 1) {
+            float nxt[32];
+            for (uint32_t l = 0; l < 32; ++l) nxt[l] = part[l] + part[l ^ off];
+            std::memcpy(part, nxt, sizeof part);
+        }
+        const float inv_rms = 1.0f / std::sqrt(part[0] / (float)hidden + eps);
+        for (uint32_t d = 0; d < hidden; ++d) {
+            const float v = vwo_f16_to_f32(xr[d]), w = vwo_f16_to_f32(weight[d]);
+            const float normed = v * inv_rms * w * scale;
+            out[(size_t)r * hidden + d] = vwo_fp8_encode_ref(normed);
+        }
+    }
+}
+
+// gemm_fp8 (gemm_fp8.bm:31-107) in f64: C[m][n] = (a_scale * b_scale) *
+// sum_k dec(A[m][k]) dec(B[k][n]) + bias[n], dec = the reference decoder
+// (:110-116), A [M][K] and B [K][N] E4M3 codes row-major, bias and the result
+// C f64 [M][N] (the tolerance reference; the reference rounds C to bf16).
+void vwo_gemm_fp8_f64(const uint8_t* a, const uint8_t* b, const uint16_t* bias_bf16, uint32_t M,
+                      uint32_t N, uint32_t K, float a_scale, float b_scale, double* c, int nthreads) {
+    float dec[256];
+    for (int i = 0; i < 256; ++i) dec[i] = vwo_fp8_decode_ref((uint8_t)i);
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(static)
+#endif
+    for (int64_t m = 0; m < (int64_t)M; ++m) {
+        std::vector<double> acc(N, 0.0);
+        for (uint32_t k = 0; k < K; ++k) {
+            const double av = dec[a[(size_t)m * K + k]];
+            if (av == 0.0) continue;
+            const uint8_t* brow = b + (size_t)k * N;
+            for (uint32_t n = 0; n < N; ++n) acc[n] += av * dec[brow[n]];
+        }
+        const double sc = (double)(a_scale * b_scale);
+        for (uint32_t n = 0; n < N; ++n)
+            c[(size_t)m * N + n] = acc[n] * sc + (bias_bf16 ? (double)vwo_bf16_to_f32(bias_bf16[n]) : 0.0);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // BlockManager  (engine/kv_cache.bm:29-164)
 // ---------------------------------------------------------------------------
 

@@ -112,6 +112,9 @@ SIGNATURES = {
     "vw_kv_append": (i32, [vp, u32, vp, vp, vp, u32, vp]),
     "vw_paged_decode": (i32, [vp, ctypes.POINTER(DecodeArgs), vp]),
     "vw_paged_prefill": (i32, [vp, ctypes.POINTER(PrefillArgs), vp]),
+    "vw_rms_norm_fp8_out": (i32, [vp, vp, vp, u32, u32, f32, f32, vp]),
+    "vw_gemm_fp8": (i32, [vp, vp, vp, vp, u32, u32, u32, f32, f32, vp]),
+    "vw_fp8_weight_check": (i32, [ctypes.POINTER(u32)]),
     "vw_sched_create": (i32, [ctypes.POINTER(SchedConfig), vp, ctypes.POINTER(vp)]),
     "vw_sched_destroy": (i32, [vp]),
     "vw_sched_add_request": (i32, [vp, vp, u32, u32, ctypes.c_int64, ctypes.POINTER(u64)]),

@@ -491,6 +491,46 @@ int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) 
     return VW_OK;
 }
 
+// ---------------------------------------------------------------------------
+// FP8 weight path: rms_norm_fp8_out (kernels/norm/rms_norm.bm:62-94) and
+// gemm_fp8 (kernels/gemm/gemm_fp8.bm:31-107).
+// ---------------------------------------------------------------------------
+
+int32_t vw_rms_norm_fp8_out(const void* x, const void* weight, uint8_t* out, uint32_t rows, uint32_t hidden,
+                            float scale, float eps, void* stream) {
+    if (!x || !weight || !out) return fail(VW_ERR_INVALID_ARG, "vw_rms_norm_fp8_out: null pointer");
+    if (hidden == 0) return fail(VW_ERR_INVALID_ARG, "vw_rms_norm_fp8_out: hidden must be > 0");
+    if (!aligned(x, 2) || !aligned(weight, 2))
+        return fail(VW_ERR_INVALID_ARG, "vw_rms_norm_fp8_out: misaligned pointer");
+    if (!std::isfinite(scale) || !(eps >= 0.0f) || !std::isfinite(eps))
+        return fail(VW_ERR_INVALID_ARG, "vw_rms_norm_fp8_out: bad scale / eps");
+    cudaError_t e = launch_rms_norm_fp8(x, weight, out, rows, hidden, scale, eps, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_rms_norm_fp8_out");
+}
+
+int32_t vw_gemm_fp8(const uint8_t* a, const uint8_t* b, void* c, const void* bias, uint32_t M, uint32_t N,
+                    uint32_t K, float a_scale, float b_scale, void* stream) {
+    if (!a || !b || !c) return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: null pointer");
+    if (M == 0 || N == 0 || K == 0) return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: empty shape");
+    if (N % 16 || K % 16) return fail(VW_ERR_UNSUPPORTED, "vw_gemm_fp8: N and K must be multiples of 16");
+    if ((uint64_t)M * K >= (1ull << 40) || (uint64_t)K * N >= (1ull << 40))
+        return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: too large");
+    if (!aligned(a, 16) || !aligned(b, 16) || !aligned(c, 16) || (bias && !aligned(bias, 2)))
+        return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: misaligned pointer");
+    if (!std::isfinite(a_scale) || !std::isfinite(b_scale))
+        return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: bad scale");
+    cudaError_t e = launch_gemm_fp8(a, b, c, bias, M, N, K, a_scale, b_scale, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_gemm_fp8");
+}
+
+int32_t vw_fp8_weight_check(uint32_t* device_error) {
+    uint32_t w = 0;
+    cudaError_t e = fp8w_error(&w, true);
+    if (device_error) *device_error = w;
+    if (e != cudaSuccess) return cuda_fail(e, "vw_fp8_weight_check");
+    return w ? VW_ERR_DEVICE_CHECK : VW_OK;
+}
+
 int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32_t* seq_lens,
                        uint32_t num_seqs, uint32_t block_table_stride, uint32_t num_q_heads,
                        void* stream) {

@@ -107,6 +107,12 @@ cudaError_t launch_prefill_append(const PoolGeom& g, uint8_t* data, float* scale
                                   const int32_t* ctx_start, const uint32_t* block_tables,
                                   uint32_t bt_stride, uint32_t B, uint32_t T, float rope_theta,
                                   uint32_t* err, cudaStream_t s);
+// FP8 weight path (vw_fp8w.cu): RMSNorm with E4M3 output and the E4M3 GEMM.
+cudaError_t launch_rms_norm_fp8(const void* x, const void* w, uint8_t* out, uint32_t rows, uint32_t hidden,
+                                float scale, float eps, cudaStream_t s);
+cudaError_t launch_gemm_fp8(const uint8_t* a, const uint8_t* b, void* c, const void* bias, uint32_t M,
+                            uint32_t N, uint32_t K, float a_scale, float b_scale, cudaStream_t s);
+cudaError_t fp8w_error(uint32_t* word, bool clear);
 cudaError_t launch_kv_gather(const PoolGeom& g, const uint8_t* data, const float* scales,
                              uint32_t layer, const uint32_t* block_table, uint32_t seq_len,
                              void* out_k, void* out_v, float* out_ks, float* out_vs,

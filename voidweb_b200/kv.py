@@ -227,3 +227,35 @@ def launch_paged_attn_decode(pool: KvPool, layer: int, q, block_table, seq_lens,
 
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+# ---- FP8 weight path (kernels/norm/rms_norm.bm:62-94, kernels/gemm/gemm_fp8.bm:31-107) ----
+
+def rms_norm_fp8_out(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, scale: float,
+                     eps: float = 1e-5, stream=None) -> torch.Tensor:
+    """E4M3 codes of RMSNorm(x) * weight * scale: x f16 [rows][hidden], weight f16
+    [hidden], out uint8 [rows][hidden] (the reference encoder; bit-exact)."""
+    rows, hidden = x.shape
+    C.check(C.lib().vw_rms_norm_fp8_out(_ptr(x), _ptr(weight), _ptr(out), rows, hidden, scale, eps,
+                                        _stream(stream)))
+    return out
+
+
+def gemm_fp8(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, bias=None, a_scale: float = 1.0,
+             b_scale: float = 1.0, stream=None) -> torch.Tensor:
+    """C = (a_scale * b_scale) * (A . B) + bias: A uint8 [M][K], B uint8 [K][N] E4M3
+    codes (the reference decoder), bias bf16 [N] or None, out bf16 [M][N]."""
+    M, K = a.shape
+    N = b.shape[1]
+    C.check(C.lib().vw_gemm_fp8(_ptr(a), _ptr(b), _ptr(out), _ptr(bias), M, N, K, a_scale, b_scale,
+                                _stream(stream)))
+    return out
+
+
+def fp8_weight_check() -> int:
+    """Synchronise; return (and clear) the device error word of the two calls above."""
+    w = ctypes.c_uint32(0)
+    rc = C.lib().vw_fp8_weight_check(ctypes.byref(w))
+    if rc not in (C.VW_OK, C.VW_ERR_DEVICE_CHECK):
+        C.check(rc)
+    return int(w.value)
