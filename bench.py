@@ -47,6 +47,8 @@ WORKLOADS = {
     # (the scheduler's largest, scheduler/scheduler.bm:255) after a cached prefix
     "qwen2.5-7b-prefill-4x2048": dict(kind="prefill", L=28, Hq=28, Hkv=4, D=128, B=4, chunk=2048,
                                       ctx=("uniform", 0, 2048), kv="bf16", io="bf16", seed=11),
+    # the FP8 weight path's GEMM (gemm_fp8.bm:31-107): E4M3 A [M][K] x B [K][N] -> bf16
+    "fp8-gemm-8192": dict(kind="gemm", M=8192, N=8192, K=8192, seed=12),
 }
 DEFAULT = "qwen2.5-7b-decode-b16"
 L2_BYTES = 126 * 1024 * 1024
@@ -192,6 +194,66 @@ def run_prefill_bench(args, w):
                      "peak_kind": f"{kind} sustained (burst {burst})",
                      "flops_per_step": flops},
         "cpu_baseline": cpu, "e2e": None, "clocks": clk, "gpu_launches": args.steps * L * 2,
+    }))
+
+
+def run_gemm_bench(args, w):
+    """vw_gemm_fp8 on E4M3 codes, timed with CUDA events over K launches."""
+    import torch
+    from voidweb_b200.kv import fp8_weight_check, gemm_fp8
+    import oracle
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        print(json.dumps({"metric": "fp8 gemm TFLOP/s", "error": "single GPU only"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    M, N, K = w["M"], w["N"], w["K"]
+    g = torch.Generator(device=dev).manual_seed(w["seed"])
+    # codes of N(0,1)-like magnitudes: exponent field 4..9, any sign and mantissa
+    def codes(shape):
+        e = torch.randint(4, 10, shape, device=dev, generator=g, dtype=torch.int32)
+        m = torch.randint(0, 16, shape, device=dev, generator=g, dtype=torch.int32)
+        return ((e << 3) | (m & 7) | ((m >> 3) << 7)).to(torch.uint8)
+    a, b = codes((M, K)), codes((K, N))
+    bias = torch.randn(N, device=dev).bfloat16()
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup):
+        gemm_fp8(a, b, out, bias, 0.01, 0.01)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.steps):
+        gemm_fp8(a, b, out, bias, 0.01, 0.01)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    assert fp8_weight_check() == 0
+    ms = e0.elapsed_time(e1) / args.steps
+    tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    burst, sustained, kind = tensor_peak()
+    cpu = None
+    if not args.no_cpu_baseline:
+        thr = cpu_threads()
+        m = 16
+        an, bn = a[:m].cpu().numpy(), b.cpu().numpy()
+        t0 = time.perf_counter()
+        oracle.gemm_fp8_f64(an, bn, None, 0.01, 0.01, nthreads=thr)
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(2.0 * m * N * K / dt / 1e12, 6), "unit": "TFLOP/s", "cores": thr,
+               "kind": "port", "sample": f"{m} rows of A against all of B (fp64 oracle)"}
+    print(json.dumps({
+        "metric": "fp8 gemm TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in, f16 mma, bf16 out",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "M": M, "N": N, "K": K, "parallelism": "single",
+                   "l2": f"inputs larger than L2 ({(M * K + K * N) / 1e6:.0f} MB of codes)"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": burst, "unit": "TFLOP/s",
+                     "frac": round(tflops / burst, 4), "traffic": None,
+                     "peak_kind": f"{kind} bf16 burst (the MMAs run in f16)"},
+        "cpu_baseline": cpu, "e2e": None, "clocks": clk, "gpu_launches": args.steps,
     }))
 
 
@@ -391,6 +453,14 @@ def main():
     w = dict(WORKLOADS[args.workload])
     if args.layers > 0:
         w["L"] = min(args.layers, w["L"])
+    if w.get("kind") == "gemm":
+        if args.warmup < 3:
+            args.warmup = 3
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the decode "
+                              "workloads; the gemm line's cpu_baseline is the oracle sample"}))
+            return
+        return run_gemm_bench(args, w)
     if w.get("kind") == "prefill":
         if args.warmup < 3:
             args.warmup = 3
