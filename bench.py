@@ -47,6 +47,8 @@ WORKLOADS = {
     # (the scheduler's largest, scheduler/scheduler.bm:255) after a cached prefix
     "qwen2.5-7b-prefill-4x2048": dict(kind="prefill", L=28, Hq=28, Hkv=4, D=128, B=4, chunk=2048,
                                       ctx=("uniform", 0, 2048), kv="bf16", io="bf16", seed=11),
+    "llama3-8b-fp8-prefill-4x2048": dict(kind="prefill", L=32, Hq=32, Hkv=8, D=128, B=4, chunk=2048,
+                                         ctx=("uniform", 0, 2048), kv="fp8", io="bf16", seed=13),
     # the FP8 weight path's GEMM (gemm_fp8.bm:31-107): E4M3 A [M][K] x B [K][N] -> bf16
     "fp8-gemm-8192": dict(kind="gemm", M=8192, N=8192, K=8192, seed=12),
 }
@@ -127,7 +129,12 @@ def run_prefill_bench(args, w):
         off += pages[b]
     T = B * n
     pool = KvPool(PoolSpec(L, Hkv, D, NB, w["kv"], w["io"], max_batch=B), device=0)
-    pool.pages_u8().view(torch.bfloat16).normal_()
+    fp8 = w["kv"] == "fp8"
+    if fp8:     # random codes of the cached prefixes, row scales amax / 448 of N(0, 1) rows
+        pool.pages_u8().random_(0, 256)
+        pool.scales_f32().uniform_(0.005, 0.01)
+    else:
+        pool.pages_u8().view(torch.bfloat16).normal_()
     q = torch.randn((L, T, Hq, D), device=dev).bfloat16()
     kn = torch.randn((L, T, Hkv, D), device=dev).bfloat16()
     vn = torch.randn((L, T, Hkv, D), device=dev).bfloat16()
@@ -164,14 +171,20 @@ def run_prefill_bench(args, w):
     cpu = None
     if not args.no_cpu_baseline:
         thr = cpu_threads()
-        g = oracle.geom(1, Hkv, D, NB, oracle.BF16, oracle.BF16)
-        data = pool.pages_u8().view(torch.int16)[: NB * Hkv * 2 * 16 * D].cpu().numpy().view(np.uint16)
+        g = oracle.geom(1, Hkv, D, NB, oracle.FP8 if fp8 else oracle.BF16, oracle.BF16)
+        rows = NB * Hkv * 2 * 16
+        if fp8:
+            data = pool.pages_u8()[: rows * D].cpu().numpy()
+            scales = pool.scales_f32()[:rows].cpu().numpy().reshape(oracle.pool_shape(g)[:-1])
+        else:
+            data = pool.pages_u8().view(torch.int16)[: rows * D].cpu().numpy().view(np.uint16)
+            scales = None
         data = data.reshape(oracle.pool_shape(g))
         m = 16
         qs = q[0].view(torch.int16).cpu().numpy().view(np.uint16).reshape(B, n, Hq, D)[:, :m].reshape(B * m, Hq, D)
         cus = np.arange(0, B * m + 1, m, dtype=np.int32)
         t0 = time.perf_counter()
-        oracle.paged_prefill_f32(g, data, None, 0, qs, Hq, bt, cus, prefix.astype(np.int32), True,
+        oracle.paged_prefill_f32(g, data, scales, 0, qs, Hq, bt, cus, prefix.astype(np.int32), True,
                                  1.0 / math.sqrt(D), nthreads=thr)
         dt = time.perf_counter() - t0
         sample_flops = sum(4 * D * Hq * (m * int(c0) + m * (m + 1) // 2) for c0 in prefix)
@@ -181,13 +194,13 @@ def run_prefill_bench(args, w):
     print(json.dumps({
         "metric": "prefill attention TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 pages, f16 MMA" if fp8 else "bf16", "data": "synthetic",
         "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv,
                    "head_dim": D, "seqs": B, "chunk_tokens": n,
                    "cached_prefix": [int(x) for x in prefix], "block_size": 16, "kv_dtype": w["kv"],
                    "causal": True, "parallelism": "single",
-                   "l2": f"inputs larger than L2 ({NB * Hkv * 2 * 16 * D * 2 * L / 1e9:.2f} GB of pages)"},
+                   "l2": f"inputs larger than L2 ({NB * Hkv * 2 * 16 * (D * (1 if fp8 else 2) + (4 if fp8 else 0)) * L / 1e9:.2f} GB of pages)"},
         "tok_per_s": round(T / (ms * 1e-3), 1),
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": sustained,
                      "unit": "TFLOP/s", "frac": round(tflops / sustained, 4), "traffic": None,

@@ -229,9 +229,9 @@ VW_API int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* args,
  * appended to slots block_tables[b][p/16]*16 + p%16 (FP8 pools quantise them);
  * then token i attends to keys 0 .. ctx_start[b]+i with VW_PREFILL_CAUSAL, or
  * to all ctx_start[b] + n_b keys without it (the reference kernel has no mask).
- * Pools of f16 / bf16 pages; FP8 pools take the append but the attention
- * returns VW_ERR_UNSUPPORTED.  Device pointers, 16-byte aligned (the int
- * arrays 4-byte). */
+ * Every pool kind: f16 / bf16 pages (head_dim 64 or 128) and FP8 E4M3 pages
+ * (head_dim 128; attention over the dequantised codes).  Device pointers,
+ * 16-byte aligned (the int arrays 4-byte). */
 typedef struct {
     uint32_t layer;
     uint32_t num_seqs;             /* B, at most the pool's max_batch */
@@ -447,8 +447,8 @@ VW_API int32_t vw_forward_release(uint64_t seq_id);
  * num_tokens tokens at positions len(seq_id) .. len(seq_id)+num_tokens-1 and
  * each attends causally over the cached tokens and the chunk up to itself.
  * The host block list (block_ptr, num_blocks) is the block table; len(seq_id)
- * then grows by num_tokens.  Prefill needs an f16 / bf16 pool.  logits_out is
- * not written (no LM head in this library). */
+ * then grows by num_tokens.  logits_out is not written (no LM head in this
+ * library). */
 VW_API int32_t voidweb_forward_pass(const ForwardArgs* args);
 
 #ifdef __cplusplus

@@ -4,8 +4,10 @@ attention is within |gpu - ref| <= 2e-3 + 1e-2 * |ref| of the oracle's fp64
 restatement of flash_attention.bm:31-106 over the pool, causal and not.
 Cases: ragged chunks (1, 16, 63, 64, 65, 129, 300 tokens), cached prefixes
 (ctx_start 0 to 1000), an empty chunk, GQA groups 1 to 7, head_dim 64 and 128,
-f16 and bf16, NaN garbage past every sequence's end, RoPE, the error paths,
-and prefill descriptors through voidweb_forward_pass."""
+f16 and bf16 pages, FP8 E4M3 pages with per-token-per-head scales (codes and
+scales of the append bit-exact, the attention against the fp64 oracle over the
+same dequantised codes), NaN garbage past every sequence's end, RoPE, the error
+paths, and prefill descriptors through voidweb_forward_pass."""
 import numpy as np
 import pytest
 
@@ -25,11 +27,11 @@ def dev():
     return torch.device("cuda", 0)
 
 
-def chunk_case(seed, io, D, Hq, Hkv, chunks, L=2):
+def chunk_case(seed, io, D, Hq, Hkv, chunks, L=2, kv=None):
     """Sequences that hold ctx_start + n tokens once their chunk [(ctx_start, n)]
     is appended; q, k_new, v_new rows of the chunks, packed."""
     ctx = [cs + n for cs, n in chunks]
-    c = kvgen.make_case(seed, L, Hkv, D, Hq, len(chunks), 1, 1, io, io, ctx=ctx)
+    c = kvgen.make_case(seed, L, Hkv, D, Hq, len(chunks), 1, 1, io if kv is None else kv, io, ctx=ctx)
     rng = np.random.Generator(np.random.PCG64(seed + 7))
     cu = np.zeros(len(chunks) + 1, dtype=np.int32)
     cu[1:] = np.cumsum([n for _, n in chunks])
@@ -39,6 +41,15 @@ def chunk_case(seed, io, D, Hq, Hkv, chunks, L=2):
     k = kvgen.io_bits(rng, (T, Hkv, D), io)
     v = kvgen.io_bits(rng, (T, Hkv, D), io)
     return c, q, k, v, cu, cs
+
+
+def fp8_mag(c, data, scales, layer, q, cu, cs, causal):
+    """FP8 pools: the attention over |v| (codes with the sign bit cleared decode
+    to |v|), the scale of an output's f16 probability rounding."""
+    if c.kv != FP8:
+        return None
+    return oracle.paged_prefill_f64(c.geom, data & np.uint8(0x7F), scales, layer, q, c.Hq, c.block_tables,
+                                    cu, cs, causal, 1.0 / np.sqrt(c.D))
 
 
 def run_prefill(pool, c, layer, q, k, v, cu, cs, dev, causal=True, rope_theta=0.0):
@@ -53,29 +64,37 @@ def run_prefill(pool, c, layer, q, k, v, cu, cs, dev, causal=True, rope_theta=0.
 
 
 CASES = [
-    (BF16, 128, 28, 4, [(0, 64), (37, 100), (500, 7), (0, 1), (1000, 300)]),
-    (F16, 64, 14, 2, [(0, 1), (16, 16), (5, 200), (0, 129)]),
-    (BF16, 128, 8, 8, [(123, 65), (0, 63)]),
-    (F16, 128, 32, 8, [(0, 200), (300, 0), (7, 63)]),
+    # (kv, io, head_dim, Hq, Hkv, chunks)
+    (BF16, BF16, 128, 28, 4, [(0, 64), (37, 100), (500, 7), (0, 1), (1000, 300)]),
+    (F16, F16, 64, 14, 2, [(0, 1), (16, 16), (5, 200), (0, 129)]),
+    (BF16, BF16, 128, 8, 8, [(123, 65), (0, 63)]),
+    (F16, F16, 128, 32, 8, [(0, 200), (300, 0), (7, 63)]),
+    (FP8, BF16, 128, 28, 4, [(0, 64), (37, 100), (500, 7), (0, 1), (1000, 300)]),
+    (FP8, F16, 128, 32, 8, [(0, 200), (300, 0), (7, 63), (16, 16)]),
+    (FP8, BF16, 128, 8, 1, [(123, 65), (0, 129)]),
 ]
 
 
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("io,D,Hq,Hkv,chunks", CASES)
-def test_prefill_append_and_attention(dev, io, D, Hq, Hkv, chunks, causal):
-    c, q, k, v, cu, cs = chunk_case(40 + len(chunks) + D, io, D, Hq, Hkv, chunks)
+@pytest.mark.parametrize("kv,io,D,Hq,Hkv,chunks", CASES)
+def test_prefill_append_and_attention(dev, kv, io, D, Hq, Hkv, chunks, causal):
+    c, q, k, v, cu, cs = chunk_case(40 + len(chunks) + D, io, D, Hq, Hkv, chunks, kv=kv)
     pool = make_pool(c, dev)
     layer = 1
     got = run_prefill(pool, c, layer, q, k, v, cu, cs, dev, causal=causal)
     assert pool.check() == 0
-    # the append, bit for bit, at block_tables[b][p/16]*16 + p%16
+    # the append, bit for bit, at block_tables[b][p/16]*16 + p%16 (FP8: the
+    # codes and the scales)
     slots = oracle.prefill_slots(c.block_tables, cu, cs)
     oracle.kv_append(c.geom, c.data, c.scales, layer, k, v, slots)
-    gdata, _ = download_pool(pool, c)
+    gdata, gscales = download_pool(pool, c)
     assert np.array_equal(gdata, c.data)
+    if kv == FP8:
+        assert np.array_equal(gscales, c.scales, equal_nan=True)
     ref = oracle.paged_prefill_f64(c.geom, c.data, c.scales, layer, q, Hq, c.block_tables, cu, cs,
                                    causal, 1.0 / np.sqrt(D))
-    check_close(got, ref, io, f"prefill causal={causal}")
+    check_close(got, ref, io, f"prefill causal={causal}",
+                mag=fp8_mag(c, c.data, c.scales, layer, q, cu, cs, causal))
     pool.close()
 
 
@@ -93,25 +112,37 @@ def test_prefill_over_cached_pages_without_append(dev):
     pool.close()
 
 
-@pytest.mark.parametrize("io,D", [(BF16, 128), (F16, 64)])
-def test_prefill_rope(dev, io, D):
+@pytest.mark.parametrize("kv,io,D", [(BF16, BF16, 128), (F16, F16, 64), (FP8, BF16, 128)])
+def test_prefill_rope(dev, kv, io, D):
     # q and the appended K rows are rotated at their positions (RoPE,
     # kernels/rope/rope.bm:22-52) as separate passes would leave them; the
     # device's sin/cos may round an angle differently from the oracle's, so the
-    # rotated K rows are checked to a few units of the io type (most bit-exact)
+    # rotated K rows are checked to a few units of the io type (most bit-exact;
+    # FP8: most K codes equal, V codes and scales exact)
     theta = 10000.0
-    c, q, k, v, cu, cs = chunk_case(91, io, D, 8, 2, [(40, 50), (0, 33), (700, 5)])
+    c, q, k, v, cu, cs = chunk_case(91, io, D, 8, 2, [(40, 50), (0, 33), (700, 5)], kv=kv)
     pool = make_pool(c, dev)
     got = run_prefill(pool, c, 0, q, k, v, cu, cs, dev, rope_theta=theta)
     assert pool.check() == 0
     pos = np.concatenate([cs[b] + np.arange(cu[b + 1] - cu[b]) for b in range(cs.size)])
     k_rot = oracle.rope_apply(k, pos, theta, io)
     q_rot = oracle.rope_apply(q, pos, theta, io)
-    want = c.data.copy()
     slots = oracle.prefill_slots(c.block_tables, cu, cs)
-    oracle.kv_append(c.geom, want, None, 0, k_rot, v, slots)
-    gdata, _ = download_pool(pool, c)
+    gdata, gscales = download_pool(pool, c)
     blk, t = slots // 16, slots % 16
+    if kv == FP8:
+        want, wsc = c.data.copy(), c.scales.copy()
+        oracle.kv_append(c.geom, want, wsc, 0, k_rot, v, slots)
+        assert np.array_equal(gdata[0, blk, :, 1, t], want[0, blk, :, 1, t]), "V codes"
+        assert np.array_equal(gscales[0, blk, :, 1, t], wsc[0, blk, :, 1, t]), "V scales"
+        assert np.mean(gdata[0, blk, :, 0, t] == want[0, blk, :, 0, t]) >= 0.9, "K codes"
+        ref = oracle.paged_prefill_f64(c.geom, gdata, gscales, 0, q_rot, c.Hq, c.block_tables, cu, cs,
+                                       True, 1.0 / np.sqrt(D))
+        check_close(got, ref, io, "prefill rope fp8", mag=fp8_mag(c, gdata, gscales, 0, q_rot, cu, cs, True))
+        pool.close()
+        return
+    want = c.data.copy()
+    oracle.kv_append(c.geom, want, None, 0, k_rot, v, slots)
     g_k = oracle.io_bits_to_f32(gdata[0, blk, :, 0, t], io)
     w_k = oracle.io_bits_to_f32(want[0, blk, :, 0, t], io)
     rel = 2.0 ** -7 if io == BF16 else 2.0 ** -10
@@ -125,10 +156,11 @@ def test_prefill_rope(dev, io, D):
     pool.close()
 
 
-def test_prefill_scheduler_chunk(dev):
+@pytest.mark.parametrize("kv", [BF16, FP8])
+def test_prefill_scheduler_chunk(dev, kv):
     # one 2048-token chunk (scheduler/scheduler.bm:255, the largest it cuts)
     # after a 512-token cached prefix, Qwen2.5-7B heads
-    c, q, k, v, cu, cs = chunk_case(5, BF16, 128, 28, 4, [(512, 2048)], L=1)
+    c, q, k, v, cu, cs = chunk_case(5, BF16, 128, 28, 4, [(512, 2048)], L=1, kv=kv)
     pool = make_pool(c, dev)
     got = run_prefill(pool, c, 0, q, k, v, cu, cs, dev)
     assert pool.check() == 0
@@ -137,24 +169,22 @@ def test_prefill_scheduler_chunk(dev):
     # the CPU): token r of the chunk, causal, is a one-token chunk at 512 + r
     rows = np.arange(0, 2048, 8)
     ref = np.zeros((rows.size, c.Hq, c.D))
+    mag = np.zeros_like(ref) if kv == FP8 else None
+    one = np.array([0, 1], dtype=np.int32)
     for r_i, r in enumerate(rows):
+        at = np.array([512 + r], dtype=np.int32)
         ref[r_i] = oracle.paged_prefill_f64(c.geom, c.data, c.scales, 0, q[r:r + 1], c.Hq,
-                                            c.block_tables, np.array([0, 1], dtype=np.int32),
-                                            np.array([512 + r], dtype=np.int32), True,
-                                            1.0 / np.sqrt(c.D))[0]
-    check_close(got[rows], ref, BF16, "2048-token chunk")
+                                            c.block_tables, one, at, True, 1.0 / np.sqrt(c.D))[0]
+        if kv == FP8:
+            mag[r_i] = fp8_mag(c, c.data, c.scales, 0, q[r:r + 1], one, at, True)[0]
+    check_close(got[rows], ref, BF16, "2048-token chunk", mag=mag)
     pool.close()
 
 
-def test_prefill_errors(dev):
+@pytest.mark.parametrize("kv", [BF16, FP8])
+def test_prefill_errors(dev, kv):
     from voidweb_b200 import _lib as C
-    # FP8 pools: the append exists, the prefill attention does not (yet)
-    c, q, k, v, cu, cs = chunk_case(3, BF16, 128, 8, 2, [(0, 20)])
-    c8 = kvgen.make_case(3, 1, 2, 128, 8, 1, 40, 40, FP8, BF16)
-    pool8 = make_pool(c8, dev)
-    with pytest.raises(C.VoidwebError, match="FP8"):
-        run_prefill(pool8, c8, 0, q, k, v, cu, cs, dev)
-    pool8.close()
+    c, q, k, v, cu, cs = chunk_case(3, BF16, 128, 8, 2, [(0, 20)], kv=kv)
     # a chunk past its block-table row: flagged on the device, nothing written
     pool = make_pool(c, dev)
     bad_cs = np.array([c.stride * 16], dtype=np.int32)

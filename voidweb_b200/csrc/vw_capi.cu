@@ -438,8 +438,6 @@ static int32_t prefill_validate(const vw_pool* pool, const vw_prefill_args* a) {
         return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: misaligned pointer");
     if (!(a->scale >= 0.0f) || std::isinf(a->scale))
         return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: bad scale");
-    if (g.kv_kind == kFP8)
-        return fail(VW_ERR_UNSUPPORTED, "vw_paged_prefill: FP8 pools are not supported by the prefill attention");
     return VW_OK;
 }
 
@@ -465,6 +463,8 @@ int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) 
     p.cu_q = a->cu_seqlens;
     p.ctx_start = a->ctx_start;
     p.block_tables = a->block_tables;
+    p.kv_data = pool->data;
+    p.kv_scales = pool->scales;
     p.err = pool->err;
     p.B = a->num_seqs;
     p.T = a->num_tokens;
@@ -869,8 +869,6 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
     };
 
     if (!pf.empty()) {
-        if (g.kv_kind == kFP8)
-            return fail(VW_ERR_UNSUPPORTED, "voidweb_forward_pass: prefill needs an f16 / bf16 pool");
         const uint32_t Bp = (uint32_t)pf.size();
         uint32_t Tp = 0;
         std::vector<int32_t> cu(Bp + 1, 0), ctx(Bp);

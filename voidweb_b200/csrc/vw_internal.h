@@ -73,6 +73,8 @@ struct PrefillParams {
     const int32_t* cu_q;        // [B+1] token offsets of the chunks
     const int32_t* ctx_start;   // [B] tokens cached before each chunk
     const uint32_t* block_tables;   // [B][bt_stride]
+    const uint8_t* kv_data;     // pool pages (FP8 pools: the codes the decoder warps read)
+    const float* kv_scales;     // FP8 scales [L][NB][Hkv][2][16]
     uint32_t* err;              // device error word
     uint32_t B, T, Hq, Hkv, group, num_blocks, layer, bt_stride, causal, flags;
     float scale_log2;           // softmax scale * log2(e)

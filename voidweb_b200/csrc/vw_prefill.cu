@@ -160,10 +160,17 @@ constexpr int kTcRows = 128;                      // query tokens per CTA: the M
 constexpr int kTcPages = 4;                       // page-heads per round (16 keys each)
 constexpr float kTcRescale = 8.0f;                // log2 units: p <= 2^8 against a stale max
 
-template <int D_, int IO_>
+template <int D_, int IO_, int KV_>
 struct TcTraits {
     static constexpr int D = D_, IO = IO_;
     static constexpr bool BF = IO == kBF16;
+    // FP8 pools: decoder warps expand the codes into f16 tiles (code b -> the
+    // binary16 value decode(b)/256, exact), so the MMAs run in f16 whatever the
+    // io type; the factor 256 returns through the K scales and the output
+    static constexpr bool FP8 = KV_ == kFP8;
+    static constexpr bool MBF = BF && !FP8;           // the MMAs' operand type is bf16
+    static constexpr float VFOLD = FP8 ? 256.0f : 1.0f;
+    static constexpr int NDEC = FP8 ? 2 : 0;          // decoder warps (FP8 pools)
     static constexpr int CH = D * 2 / 128;            // 128-B columns of a row
     static constexpr int R = kTcPages;                // page-heads per round
     static constexpr int KEYS = 16 * R;               // keys per round: the N of S = Q K^T
@@ -182,18 +189,84 @@ struct TcTraits {
     static constexpr int COL_S = D;
     static constexpr uint32_t TMEM_COLS = 256u;       // two CTAs per SM share the 512 columns
     static constexpr int TPFX = pf_align((kMaxBatchPerLaunch + 1) * 4, 128);
+    // FP8 pools: per stage the round's K scales (x256), then its V scales
+    static constexpr int SCL = FP8 ? NST * 2 * KEYS * 4 : 0;
     static constexpr int NBAR = 2 * NST + 7;          // full, empty; s_full/p_full/p_free x2; done
-    static constexpr int SMEM = 1024 + QBYTES + NST * STAGE + TPFX + NBAR * 8 + 16;
-    static constexpr int THREADS = 6 * 32;            // 4 softmax warps, 1 MMA warp, 1 producer warp
-    static constexpr uint32_t IDESC_S = idesc_f16(BF, false, kTcRows, KEYS);
-    static constexpr uint32_t IDESC_PV = idesc_f16(BF, true, kTcRows, D);
+    static constexpr int SMEM = 1024 + QBYTES + NST * STAGE + SCL + TPFX + NBAR * 8 + 16;
+    // 4 softmax warps, 1 MMA warp, then 1 TMA producer warp or NDEC decoder warps
+    static constexpr int THREADS = (FP8 ? 5 + NDEC : 6) * 32;
+    static constexpr uint32_t IDESC_S = idesc_f16(MBF, false, kTcRows, KEYS);
+    static constexpr uint32_t IDESC_PV = idesc_f16(MBF, true, kTcRows, D);
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    static_assert(!FP8 || D == 128, "FP8 pools have head_dim 128");
+    static_assert(!FP8 || NDEC * 32 == KEYS, "one decoder thread per key of a round (scales)");
     static_assert(COL_S + 2 * KEYS <= (int)TMEM_COLS, "tensor-memory columns");
     static_assert(STAGE % 1024 == 0 && QBYTES % 1024 == 0 && TILE % 1024 == 0, "1024-B alignment");
     static_assert(3 * (SMEM + 1024) > 233472, "at most two CTAs per SM (tensor memory)");
 };
 
+// FP8 pools: the decoder warps' part of round t.  Thread dt (0 .. 63) loads 16
+// chunks of 16 codes (chunk i: K rows for i < 8, V rows after; page-head
+// (i & 7) / 2, row (i & 1) * 8 + dt / 8, elements (dt % 8) * 16 ..), a warp
+// reading 512 contiguous bytes per load, and writes each as two 16-B f16
+// units into the tile layout the TMA gives an f16 pool: [column][KEYS rows]
+// [128 B], unit u of key row k at (u ^ (k % 8)) * 16.  Thread dt also stages
+// key dt's K scale (x256) and V scale.  Keys past the sequence's end, in
+// page-heads past npages or in an out-of-range block (flagged) are zero rows
+// with zero scales, so that masked probabilities meet no NaN.
+template <class T>
+__device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t* st, float* scl,
+                                                 const uint32_t* bt, int t, int h, int total, int npages,
+                                                 int dt) {
+    const int pg0 = t * T::R;
+    uint32_t blk[T::R];
+#pragma unroll
+    for (int pg = 0; pg < T::R; ++pg) {
+        blk[pg] = 0xFFFFFFFFu;
+        if (pg0 + pg < npages) {
+            blk[pg] = __ldg(bt + pg0 + pg);
+            if (blk[pg] >= p.num_blocks && dt == 0) atomicOr(p.err, kDevErrBlockId);
+        }
+    }
+    auto head_row = [&](uint32_t bj, int kv) -> size_t {   // first row of the K (kv 0) or V half
+        return ((((size_t)p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 2 + kv) * kBlockSize;
+    };
+    const int e0 = (dt & 7) * 16;
+    uint4 w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int pg = (i & 7) >> 1, rr = (i & 1) * 8 + (dt >> 3);
+        const bool valid = blk[pg] < p.num_blocks && t * T::KEYS + pg * 16 + rr < total;
+        w[i] = valid ? __ldg(reinterpret_cast<const uint4*>(p.kv_data + (head_row(blk[pg], i >> 3) + rr) * T::D + e0))
+                     : make_uint4(0, 0, 0, 0);
+    }
+    {
+        const int pg = dt >> 4, rr = dt & 15;
+        const bool valid = blk[pg] < p.num_blocks && t * T::KEYS + dt < total;
+        scl[dt] = valid ? __ldg(p.kv_scales + head_row(blk[pg], 0) + rr) * 256.0f : 0.0f;
+        scl[T::KEYS + dt] = valid ? __ldg(p.kv_scales + head_row(blk[pg], 1) + rr) : 0.0f;
+    }
+    const int c = e0 >> 6, ua = (e0 & 63) >> 3;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int key = ((i & 7) >> 1) * 16 + (i & 1) * 8 + (dt >> 3);
+        uint8_t* row = st + (i >> 3) * T::TILE + c * (T::KEYS * 128) + key * 128;
+        const uint4 a = make_uint4(fp8x2_to_f16x2_scaled(w[i].x, 0), fp8x2_to_f16x2_scaled(w[i].x, 1),
+                                   fp8x2_to_f16x2_scaled(w[i].y, 0), fp8x2_to_f16x2_scaled(w[i].y, 1));
+        const uint4 bq = make_uint4(fp8x2_to_f16x2_scaled(w[i].z, 0), fp8x2_to_f16x2_scaled(w[i].z, 1),
+                                    fp8x2_to_f16x2_scaled(w[i].w, 0), fp8x2_to_f16x2_scaled(w[i].w, 1));
+        *reinterpret_cast<uint4*>(row + ((ua ^ (key & 7)) << 4)) = a;
+        *reinterpret_cast<uint4*>(row + (((ua + 1) ^ (key & 7)) << 4)) = bq;
+    }
+    // generic-proxy writes, read next by the tensor cores (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // CTA (tile, q head): 128 query tokens of one sequence for one query head.
+//  * FP8 pools: warps 5-6 (decoders) instead of the producer: per round the
+//    code rows of the R page-heads, expanded to f16 tiles (fp8_decode_round),
+//    and the round's scales; the softmax scales S by the K scales and P by the
+//    V scales, and the output by 256.
 //  * warp 5 (producer): per round of R page-heads, two TMA boxes per 128-B
 //    column of each page-head, its 16 K rows into the round's K tile and its 16
 //    V rows into the V tile, so that the keys of the round are R*16 rows with a
@@ -218,7 +291,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* qs = base;
     uint8_t* stages = base + T::QBYTES;
-    int* tpfx = reinterpret_cast<int*>(stages + T::NST * T::STAGE);
+    float* scl = reinterpret_cast<float*>(stages + T::NST * T::STAGE);    // FP8 scales
+    int* tpfx = reinterpret_cast<int*>(stages + T::NST * T::STAGE + T::SCL);
     uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tpfx) + T::TPFX);
     uint64_t* empty = full + T::NST;
     uint64_t* s_full = empty + T::NST;
@@ -230,7 +304,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     const uint64_t deadline = cycles() + kWaitDeadlineCycles;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < T::NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < T::NST; ++s) {
+            mbar_init(&full[s], T::FP8 ? T::NDEC : 1);    // decoder warps, or the TMA transaction
+            mbar_init(&empty[s], 1);
+        }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
             mbar_init(&p_full[b], 4);
@@ -317,6 +394,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 lo = make_uint4(a[0], a[1], a[2], a[3]);
                 hi = make_uint4(c[0], c[1], c[2], c[3]);
             }
+            if constexpr (T::FP8 && T::BF) {           // FP8 pages compute in f16
+                auto cv = [](uint32_t x) {
+                    return pack2<false>(bf16_bits_to_f32(x & 0xFFFFu), bf16_bits_to_f32(x >> 16));
+                };
+                lo = make_uint4(cv(lo.x), cv(lo.y), cv(lo.z), cv(lo.w));
+                hi = make_uint4(cv(hi.x), cv(hi.y), cv(hi.z), cv(hi.w));
+            }
             const int u2 = u + HALF;
             *reinterpret_cast<uint4*>(qs + (u >> 3) * (kTcRows * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4)) = lo;
             *reinterpret_cast<uint4*>(qs + (u2 >> 3) * (kTcRows * 128) + r * 128 + (((u2 & 7) ^ (r & 7)) << 4)) = hi;
@@ -329,7 +413,25 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
 
-    if (warp == 5) {
+    if (T::FP8 && warp >= 5) {
+        // ---- decoders: round t into stage t % NST
+        const int dt = threadIdx.x - 5 * 32;
+        const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
+        bool ok = true;
+        for (int t = 0; t < nrounds; ++t) {
+            const int st_i = t % T::NST;
+            if (t >= T::NST &&
+                !__all_sync(0xffffffffu, mbar_wait(&empty[st_i], ((t / T::NST) - 1) & 1, deadline))) {
+                ok = false;
+                break;
+            }
+            fp8_decode_round<T>(p, stages + st_i * T::STAGE, scl + st_i * 2 * T::KEYS, bt, t, h, total,
+                                npages, dt);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[st_i]);
+        }
+        if (!ok && lane == 0) atomicOr(p.err, kDevErrTimeout);
+    } else if (warp == 5) {
         // ---- producer: round t into stage t % NST, R page-heads
         bool ok = true;
         for (int t = 0; t < nrounds && ok; ++t) {
@@ -394,7 +496,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 for (int pg = 0; pg < T::R && t * T::R + pg < npages; ++pg) {
                     const uint64_t vdesc = vst + (uint64_t)((pg * T::HALF_BOX) >> 4);
                     tc_mma_ts(tbase, pcol + 8 * pg, vdesc, T::IDESC_PV, (t > 0 || pg > 0) ? 1u : 0u);
-                    if constexpr (T::BF) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
+                    if constexpr (T::MBF) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
                 }
                 tc_commit(&empty[st_i]);
                 tc_commit(&p_free[bb]);
@@ -404,7 +506,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 const int bb = t & 1, st_i = t % T::NST;
                 if (!mbar_wait(&full[st_i], (t / T::NST) & 1, deadline)) { ok = false; break; }
                 const int keyl = total - t * T::KEYS;   // keys of the round inside the sequence
-                if (keyl < T::KEYS && keyl > 0 && (keyl & 15)) {
+                if (!T::FP8 && keyl < T::KEYS && keyl > 0 && (keyl & 15)) {
                     // the page-head holding the sequence's last key: its V rows past
                     // the end hold whatever the pool has there; zero them so that
                     // masked probabilities cannot meet NaN or Inf
@@ -446,6 +548,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         for (int t = 0; t < nrounds; ++t) {
             const int bb = t & 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[bb], (t >> 1) & 1, deadline))) { ok = false; break; }
+            const int st_i = t % T::NST;
+            // FP8: the decoders' scales of the round (their writes precede the
+            // stage's full barrier, which has completed before S_t)
+            if (T::FP8 && !__all_sync(0xffffffffu, mbar_wait(&full[st_i], (t / T::NST) & 1, deadline))) {
+                ok = false;
+                break;
+            }
+            const float* ksc = scl + st_i * 2 * T::KEYS;
             tc_fence_after();
             float xs[T::KEYS];
             {
@@ -456,6 +566,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                     tmem_wait_ld();
 #pragma unroll
                     for (int k = 0; k < 16; ++k) xs[16 * c16 + k] = __uint_as_float(sr[k]);
+                }
+            }
+            if constexpr (T::FP8) {
+#pragma unroll
+                for (int k4 = 0; k4 < T::KEYS / 4; ++k4) {
+                    const float4 f = *reinterpret_cast<const float4*>(ksc + 4 * k4);
+                    xs[4 * k4] *= f.x; xs[4 * k4 + 1] *= f.y; xs[4 * k4 + 2] *= f.z; xs[4 * k4 + 3] *= f.w;
                 }
             }
             // keys of page-heads past npages are stale rows; they lie past kend_r.
@@ -504,18 +621,31 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
 #pragma unroll
             for (int c8 = 0; c8 < T::KEYS / 16; ++c8) {
                 uint32_t ph[8], pl[8];
+                float vsc[16];
+                if constexpr (T::FP8) {                 // P carries the V scales (f16 P V)
+#pragma unroll
+                    for (int k4 = 0; k4 < 4; ++k4) {
+                        const float4 f = *reinterpret_cast<const float4*>(ksc + T::KEYS + 16 * c8 + 4 * k4);
+                        vsc[4 * k4] = f.x; vsc[4 * k4 + 1] = f.y; vsc[4 * k4 + 2] = f.z; vsc[4 * k4 + 3] = f.w;
+                    }
+                }
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                     const float p0 = ex2(fmaf(xs[16 * c8 + 2 * k], p.scale_log2, -mu));
                     const float p1 = ex2(fmaf(xs[16 * c8 + 2 * k + 1], p.scale_log2, -mu));
                     ls += p0 + p1;
-                    ph[k] = pack2<T::BF>(p0, p1);
-                    pl[k] = T::BF ? pack2<true>(p0 - bf16_bits_to_f32(ph[k] & 0xFFFFu),
-                                                p1 - bf16_bits_to_f32(ph[k] >> 16))
-                                  : 0u;
+                    if constexpr (T::FP8) {
+                        ph[k] = pack2<false>(p0 * vsc[2 * k], p1 * vsc[2 * k + 1]);
+                        pl[k] = 0u;
+                    } else {
+                        ph[k] = pack2<T::BF>(p0, p1);
+                        pl[k] = T::BF ? pack2<true>(p0 - bf16_bits_to_f32(ph[k] & 0xFFFFu),
+                                                    p1 - bf16_bits_to_f32(ph[k] >> 16))
+                                      : 0u;
+                    }
                 }
                 tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + 8 * c8, ph);
-                if constexpr (T::BF) tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + T::KEYS / 2 + 8 * c8, pl);
+                if constexpr (T::MBF) tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + T::KEYS / 2 + 8 * c8, pl);
             }
             l += ls;
             tmem_wait_st();
@@ -526,7 +656,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         // epilogue: O / l, after the last PV
         if (ok && __all_sync(0xffffffffu, mbar_wait(done, 0, deadline))) {
             tc_fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const float inv = l > 0.0f ? T::VFOLD / l : 0.0f;
             uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + ((size_t)(q_off + tq) * p.Hq + j) * T::D * 2;
 #pragma unroll 1
             for (int c0 = 0; c0 < T::D; c0 += 16) {
@@ -588,11 +718,16 @@ cudaError_t launch_t(const PrefillLaunch& L) {
 int prefill_query_tile() { return kTcRows; }
 
 cudaError_t launch_paged_prefill(const PrefillLaunch& L) {
-    if (L.kv_kind == kFP8) return cudaErrorNotSupported;
+    if (L.kv_kind == kFP8) {
+        if (L.head_dim != 128) return cudaErrorNotSupported;
+        return L.io_kind == kBF16 ? launch_t<TcTraits<128, kBF16, kFP8>>(L)
+                                  : launch_t<TcTraits<128, kF16, kFP8>>(L);
+    }
     if (L.head_dim == 128)
-        return L.io_kind == kBF16 ? launch_t<TcTraits<128, kBF16>>(L) : launch_t<TcTraits<128, kF16>>(L);
+        return L.io_kind == kBF16 ? launch_t<TcTraits<128, kBF16, kBF16>>(L)
+                                  : launch_t<TcTraits<128, kF16, kF16>>(L);
     if (L.head_dim == 64)
-        return L.io_kind == kBF16 ? launch_t<TcTraits<64, kBF16>>(L) : launch_t<TcTraits<64, kF16>>(L);
+        return L.io_kind == kBF16 ? launch_t<TcTraits<64, kBF16, kBF16>>(L) : launch_t<TcTraits<64, kF16, kF16>>(L);
     return cudaErrorNotSupported;
 }
 
