@@ -169,6 +169,9 @@ struct TcTraits {
     // io type; the factor 256 returns through the K scales and the output
     static constexpr bool FP8 = KV_ == kFP8;
     static constexpr bool MBF = BF && !FP8;           // the MMAs' operand type is bf16
+    // P as a pair hi + lo of the MMA type (two PV MMAs): bf16 pages, and FP8
+    // pages whose f16 P carries the V scales
+    static constexpr bool PSPLIT = BF || FP8;
     static constexpr float VFOLD = FP8 ? 256.0f : 1.0f;
     static constexpr int NDEC = FP8 ? 2 : 0;          // decoder warps (FP8 pools)
     static constexpr int CH = D * 2 / 128;            // 128-B columns of a row
@@ -496,7 +499,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 for (int pg = 0; pg < T::R && t * T::R + pg < npages; ++pg) {
                     const uint64_t vdesc = vst + (uint64_t)((pg * T::HALF_BOX) >> 4);
                     tc_mma_ts(tbase, pcol + 8 * pg, vdesc, T::IDESC_PV, (t > 0 || pg > 0) ? 1u : 0u);
-                    if constexpr (T::MBF) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
+                    if constexpr (T::PSPLIT) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
                 }
                 tc_commit(&empty[st_i]);
                 tc_commit(&p_free[bb]);
@@ -635,8 +638,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                     const float p1 = ex2(fmaf(xs[16 * c8 + 2 * k + 1], p.scale_log2, -mu));
                     ls += p0 + p1;
                     if constexpr (T::FP8) {
-                        ph[k] = pack2<false>(p0 * vsc[2 * k], p1 * vsc[2 * k + 1]);
-                        pl[k] = 0u;
+                        const float a0 = p0 * vsc[2 * k], a1 = p1 * vsc[2 * k + 1];
+                        ph[k] = pack2<false>(a0, a1);
+                        pl[k] = pack2<false>(a0 - f16_bits_to_f32(ph[k] & 0xFFFFu), a1 - f16_bits_to_f32(ph[k] >> 16));
                     } else {
                         ph[k] = pack2<T::BF>(p0, p1);
                         pl[k] = T::BF ? pack2<true>(p0 - bf16_bits_to_f32(ph[k] & 0xFFFFu),
@@ -645,7 +649,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                     }
                 }
                 tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + 8 * c8, ph);
-                if constexpr (T::MBF) tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + T::KEYS / 2 + 8 * c8, pl);
+                if constexpr (T::PSPLIT) tmem_st8(tbase + lanes + T::COL_S + T::KEYS * bb + T::KEYS / 2 + 8 * c8, pl);
             }
             l += ls;
             tmem_wait_st();
