@@ -689,7 +689,8 @@ def main():
         e2e = {"value": round(step_bytes_all / (ems * 1e-3) / 1e9, 3), "unit": "GB/s",
                "ms_per_step": round(ems, 4), "tok_per_s": round(total_seqs / (ems * 1e-3), 1),
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(ho.numel() * 2),
-               "path": "vw_decode_step_host (host buffers, pinned)"}
+               "path": "vw_decode_step_host (pinned host buffers; from the second call with "
+                       "the same buffers the step replays as one recorded CUDA graph)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -276,6 +276,25 @@ def test_host_step_and_forward_pass_match_device_path(dev):
                           torch.from_numpy(out.view(np.int16)), rope_theta=theta)
     for layer in range(c.L):
         assert np.array_equal(out[layer], dev_out[layer])
+    # repeated calls: pinned buffers are recorded as a CUDA graph on the second
+    # call with the same arguments and replayed on the third; pageable buffers
+    # stay on the direct path.  Every call gives the device path's outputs.
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    pinned = (pin(c.q.view(np.int16)), pin(c.k_new.view(np.int16)), pin(c.v_new.view(np.int16)),
+              pin(c.block_tables.astype(np.int32)), pin(c.seq_lens.astype(np.int32)),
+              torch.zeros(c.q.shape, dtype=torch.int16).pin_memory())
+    pageable = (torch.from_numpy(c.q.view(np.int16)), torch.from_numpy(c.k_new.view(np.int16)),
+                torch.from_numpy(c.v_new.view(np.int16)), torch.from_numpy(c.block_tables.astype(np.int32)),
+                torch.from_numpy(c.seq_lens.astype(np.int32)), torch.from_numpy(out.view(np.int16)))
+    for name, bufs in (("pinned", pinned), ("pageable", pageable), ("pinned", pinned)):
+        for call in range(3):
+            upload_pool(pool, c)
+            bufs[5].zero_()
+            pool.decode_step_host(*bufs, rope_theta=theta)
+            got = bufs[5].numpy().view(np.uint16)
+            for layer in range(c.L):
+                assert np.array_equal(got[layer], dev_out[layer]), f"{name} call {call} layer {layer}"
+    assert pool.check() == 0
     # the engine-facing symbol: same step through voidweb_forward_pass
     upload_pool(pool, c)
     out2 = np.zeros_like(c.q)

@@ -9,6 +9,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -79,6 +80,18 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
+// Everything a recorded host-buffer step depends on.
+struct StepKey {
+    uint32_t B, Hq, stride, scale_bits, theta_bits;
+    const void *q, *k, *v, *bt, *sl, *out;
+    const uint8_t* stage;
+    bool operator==(const StepKey& o) const {
+        return B == o.B && Hq == o.Hq && stride == o.stride && scale_bits == o.scale_bits &&
+               theta_bits == o.theta_bits && q == o.q && k == o.k && v == o.v && bt == o.bt &&
+               sl == o.sl && out == o.out && stage == o.stage;
+    }
+};
+
 struct vw_pool {
     vw_pool_config cfg{};
     PoolGeom geom{};
@@ -107,9 +120,13 @@ struct vw_pool {
     size_t stage_bytes = 0;
     uint8_t* pstage = nullptr;
     size_t pstage_bytes = 0;
-    cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
+    cudaStream_t s_h2d = nullptr, s_d2h = nullptr, s_cap = nullptr;
     std::vector<cudaEvent_t> ev_in, ev_done;
     cudaEvent_t ev_entry = nullptr, ev_exit = nullptr;
+    // vw_decode_step_host: the step recorded as a CUDA graph for one set of
+    // arguments (host buffers included), made on the second call with them
+    StepKey step_key{}, step_seen{}, step_bad{};
+    cudaGraphExec_t step_exec = nullptr;
 };
 
 namespace {
@@ -123,8 +140,10 @@ void pool_free_all(vw_pool* p) {
     if (p->err) cudaFree(p->err);
     if (p->stage) cudaFree(p->stage);
     if (p->pstage) cudaFree(p->pstage);
+    if (p->step_exec) cudaGraphExecDestroy(p->step_exec);
     if (p->s_h2d) cudaStreamDestroy(p->s_h2d);
     if (p->s_d2h) cudaStreamDestroy(p->s_d2h);
+    if (p->s_cap) cudaStreamDestroy(p->s_cap);
     for (auto e : p->ev_in) cudaEventDestroy(e);
     for (auto e : p->ev_done) cudaEventDestroy(e);
     if (p->ev_entry) cudaEventDestroy(p->ev_entry);
@@ -220,9 +239,9 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
         p->data = static_cast<uint8_t*>(c.kv_data);
     } else {
         if ((e = cudaMalloc(&p->data, p->data_bytes)) != cudaSuccess) {
+            const unsigned long long bytes = p->data_bytes;
             delete p;
-            return fail(VW_ERR_OOM, "vw_pool_create: %llu bytes of pages: %s",
-                        (unsigned long long)p->data_bytes, cudaGetErrorString(e));
+            return fail(VW_ERR_OOM, "vw_pool_create: %llu bytes of pages: %s", bytes, cudaGetErrorString(e));
         }
         p->own_data = true;
     }
@@ -597,9 +616,112 @@ int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block_table,
 
 // ---------------------------------------------------------------------------
 // Host-buffer step: H2D of the step's inputs, append + decode on every layer,
-// D2H of the outputs.  Layers are processed in chunks so the copies of chunk
-// c+1 and the read-back of chunk c-1 overlap the kernels of chunk c.
+// D2H of the outputs, the copies overlapping the kernels.
+//  * Directly on the stream: layers in 4 chunks; the uploads of chunk c+1 and
+//    the read-back of chunk c-1 overlap the kernels of chunk c.  The first
+//    launch of a chunk follows a cross-stream wait, so it does not overlap its
+//    predecessor (programmatic dependent launch needs the kernel just before).
+//  * Recorded as a CUDA graph on the second call with the same arguments and
+//    buffers, and replayed from then on: in a graph the uploads are plain
+//    dependencies, so every launch after the first keeps its overlap with the
+//    one before, the uploads can be fine at the start (layers 1, 1, 2, 4, ...:
+//    the first decode waits for one layer's rows) and each layer's outputs go
+//    back as soon as its combine ends (only the last layer's read-back remains
+//    after the kernels); one graph launch replaces the 2 L kernel launches.
 // ---------------------------------------------------------------------------
+
+static int32_t enqueue_step_host(vw_pool* pool, const vw_step_host_args* a, cudaStream_t cs, bool graph) {
+    const PoolGeom& g = pool->geom;
+    const uint32_t B = a->num_seqs, Hq = a->num_q_heads, L = g.num_layers, D = g.head_dim;
+    const size_t qb = (size_t)B * Hq * D * 2, kb = (size_t)B * g.num_kv_heads * D * 2;
+    const size_t btb = (size_t)B * a->block_table_stride * 4, slb = (size_t)B * 4;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    uint8_t* d_q = pool->stage;
+    uint8_t* d_out = d_q + up(qb * L);
+    uint8_t* d_k = d_out + up(qb * L);
+    uint8_t* d_v = d_k + up(kb * L);
+    uint32_t* d_bt = reinterpret_cast<uint32_t*>(d_v + up(kb * L));
+    uint32_t* d_sl = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(d_bt) + up(btb));
+    // upload chunks [cut[c], cut[c+1]) and read-back groups [back[r], back[r+1])
+    std::vector<uint32_t> cut{0}, back{0};
+    if (graph) {
+        for (uint32_t n = 1; cut.back() < L; n = cut.size() <= 2 ? 1 : n * 2)
+            cut.push_back(std::min(L, cut.back() + n));
+        for (uint32_t l = 1; l <= L; ++l) back.push_back(l);
+    } else {
+        const uint32_t chunks = L < 4 ? L : 4;
+        for (uint32_t c = 1; c <= chunks; ++c) cut.push_back(L * c / chunks);
+        back = cut;
+    }
+    const size_t nev = std::max(cut.size(), back.size());
+    while (pool->ev_in.size() < nev) {
+        cudaEvent_t x, y;
+        if (cudaEventCreateWithFlags(&x, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&y, cudaEventDisableTiming) != cudaSuccess)
+            return fail(VW_ERR_CUDA, "vw_decode_step_host: event creation failed");
+        pool->ev_in.push_back(x);
+        pool->ev_done.push_back(y);
+    }
+    const uint8_t* hq = static_cast<const uint8_t*>(a->q);
+    const uint8_t* hk = static_cast<const uint8_t*>(a->k_new);
+    const uint8_t* hv = static_cast<const uint8_t*>(a->v_new);
+    uint8_t* ho = static_cast<uint8_t*>(a->out);
+    cudaEventRecord(pool->ev_entry, cs);
+    cudaStreamWaitEvent(pool->s_h2d, pool->ev_entry, 0);
+    cudaStreamWaitEvent(pool->s_d2h, pool->ev_entry, 0);
+    cudaMemcpyAsync(d_bt, a->block_tables, btb, cudaMemcpyHostToDevice, pool->s_h2d);
+    cudaMemcpyAsync(d_sl, a->seq_lens, slb, cudaMemcpyHostToDevice, pool->s_h2d);
+    for (size_t c = 0; c + 1 < cut.size(); ++c) {
+        const uint32_t l0 = cut[c], nl = cut[c + 1] - cut[c];
+        cudaMemcpyAsync(d_q + l0 * qb, hq + l0 * qb, nl * qb, cudaMemcpyHostToDevice, pool->s_h2d);
+        cudaMemcpyAsync(d_k + l0 * kb, hk + l0 * kb, nl * kb, cudaMemcpyHostToDevice, pool->s_h2d);
+        cudaMemcpyAsync(d_v + l0 * kb, hv + l0 * kb, nl * kb, cudaMemcpyHostToDevice, pool->s_h2d);
+        cudaEventRecord(pool->ev_in[c], pool->s_h2d);
+    }
+    int32_t rc = VW_OK;
+    size_t c = 0, r = 0;
+    for (uint32_t l = 0; l < L && rc == VW_OK; ++l) {
+        bool waited = false;
+        if (l == cut[c]) {                               // the chunk's rows are on the device
+            cudaStreamWaitEvent(cs, pool->ev_in[c++], 0);
+            waited = true;
+        }
+        vw_decode_args da{};
+        da.layer = l;
+        da.num_seqs = B;
+        da.num_q_heads = Hq;
+        da.block_table_stride = a->block_table_stride;
+        da.q = d_q + l * qb;
+        da.block_tables = d_bt;
+        da.seq_lens = d_sl;
+        da.out = d_out + l * qb;
+        da.k_new = d_k + l * kb;
+        da.v_new = d_v + l * kb;
+        da.scale = a->scale;
+        // the previous launch writes only its own layer's pages and outputs, so
+        // this one may start early and stream its pages
+        if (l > 0 && (graph || !waited)) da.flags = VW_DECODE_PDL | VW_DECODE_EARLY_PAGES;
+        if (a->rope_theta > 0.0f) {
+            da.flags |= VW_DECODE_ROPE;
+            da.rope_theta = a->rope_theta;
+        }
+        rc = decode_validate(pool, &da);
+        if (rc == VW_OK) rc = decode_launch(pool, &da, cs);
+        if (rc == VW_OK && l + 1 == back[r + 1]) {       // read back a finished group
+            const uint32_t l0 = back[r];
+            cudaEventRecord(pool->ev_done[r], cs);
+            cudaStreamWaitEvent(pool->s_d2h, pool->ev_done[r], 0);
+            cudaMemcpyAsync(ho + l0 * qb, d_out + l0 * qb, (l + 1 - l0) * qb, cudaMemcpyDeviceToHost,
+                            pool->s_d2h);
+            ++r;
+        }
+    }
+    // join both side streams back into cs (a recorded graph must end joined)
+    cudaEventRecord(pool->ev_exit, pool->s_d2h);
+    cudaStreamWaitEvent(cs, pool->ev_exit, 0);
+    if (c < cut.size() - 1) cudaStreamWaitEvent(cs, pool->ev_in[cut.size() - 2], 0);
+    return rc;
+}
 
 int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* stream) {
     if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: null argument");
@@ -628,73 +750,46 @@ int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* str
     if (!pool->s_h2d) {
         if (cudaStreamCreateWithFlags(&pool->s_h2d, cudaStreamNonBlocking) != cudaSuccess ||
             cudaStreamCreateWithFlags(&pool->s_d2h, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&pool->s_cap, cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&pool->ev_entry, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&pool->ev_exit, cudaEventDisableTiming) != cudaSuccess)
             return fail(VW_ERR_CUDA, "vw_decode_step_host: stream/event creation failed");
     }
-    const uint32_t chunks = L < 4 ? L : 4;
-    while (pool->ev_in.size() < chunks) {
-        cudaEvent_t x, y;
-        cudaEventCreateWithFlags(&x, cudaEventDisableTiming);
-        cudaEventCreateWithFlags(&y, cudaEventDisableTiming);
-        pool->ev_in.push_back(x);
-        pool->ev_done.push_back(y);
-    }
-    uint8_t* base = pool->stage;
-    uint8_t* d_q = base;
-    uint8_t* d_out = d_q + up(qb * L);
-    uint8_t* d_k = d_out + up(qb * L);
-    uint8_t* d_v = d_k + up(kb * L);
-    uint32_t* d_bt = reinterpret_cast<uint32_t*>(d_v + up(kb * L));
-    uint32_t* d_sl = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(d_bt) + up(btb));
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
-    cudaEventRecord(pool->ev_entry, cs);
-    cudaStreamWaitEvent(pool->s_h2d, pool->ev_entry, 0);
-    cudaMemcpyAsync(d_bt, a->block_tables, btb, cudaMemcpyHostToDevice, pool->s_h2d);
-    cudaMemcpyAsync(d_sl, a->seq_lens, slb, cudaMemcpyHostToDevice, pool->s_h2d);
-    const uint8_t* hq = static_cast<const uint8_t*>(a->q);
-    const uint8_t* hk = static_cast<const uint8_t*>(a->k_new);
-    const uint8_t* hv = static_cast<const uint8_t*>(a->v_new);
-    uint8_t* ho = static_cast<uint8_t*>(a->out);
-    int32_t rc = VW_OK;
-    for (uint32_t c = 0; c < chunks; ++c) {
-        const uint32_t l0 = L * c / chunks, l1 = L * (c + 1) / chunks, nl = l1 - l0;
-        cudaMemcpyAsync(d_q + l0 * qb, hq + l0 * qb, nl * qb, cudaMemcpyHostToDevice, pool->s_h2d);
-        cudaMemcpyAsync(d_k + l0 * kb, hk + l0 * kb, nl * kb, cudaMemcpyHostToDevice, pool->s_h2d);
-        cudaMemcpyAsync(d_v + l0 * kb, hv + l0 * kb, nl * kb, cudaMemcpyHostToDevice, pool->s_h2d);
-        cudaEventRecord(pool->ev_in[c], pool->s_h2d);
-        cudaStreamWaitEvent(cs, pool->ev_in[c], 0);
-        for (uint32_t l = l0; l < l1 && rc == VW_OK; ++l) {
-            vw_decode_args da{};
-            da.layer = l;
-            da.num_seqs = B;
-            da.num_q_heads = Hq;
-            da.block_table_stride = a->block_table_stride;
-            da.q = d_q + l * qb;
-            da.block_tables = d_bt;
-            da.seq_lens = d_sl;
-            da.out = d_out + l * qb;
-            da.k_new = d_k + l * kb;
-            da.v_new = d_v + l * kb;
-            da.scale = a->scale;
-            // consecutive layers of a chunk: the previous launch writes only its own
-            // layer's pages and outputs, so this one may stream pages early
-            if (l > l0) da.flags = VW_DECODE_PDL | VW_DECODE_EARLY_PAGES;
-            if (a->rope_theta > 0.0f) {
-                da.flags |= VW_DECODE_ROPE;
-                da.rope_theta = a->rope_theta;
-            }
-            rc = decode_validate(pool, &da);
-            if (rc == VW_OK) rc = decode_launch(pool, &da, cs);
+    uint32_t sb, tb;
+    std::memcpy(&sb, &a->scale, 4);
+    std::memcpy(&tb, &a->rope_theta, 4);
+    const StepKey key{B, Hq, a->block_table_stride, sb, tb, a->q, a->k_new, a->v_new,
+                      a->block_tables, a->seq_lens, a->out, pool->stage};
+    if (!(pool->step_exec && key == pool->step_key) && key == pool->step_seen && !(key == pool->step_bad)) {
+        // second call with these arguments: record the step once
+        if (pool->step_exec) cudaGraphExecDestroy(pool->step_exec);
+        pool->step_exec = nullptr;
+        int32_t rc = VW_ERR_CUDA;
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(pool->s_cap, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            rc = enqueue_step_host(pool, a, pool->s_cap, true);
+            if (cudaStreamEndCapture(pool->s_cap, &graph) != cudaSuccess) rc = VW_ERR_CUDA;
         }
-        cudaEventRecord(pool->ev_done[c], cs);
-        cudaStreamWaitEvent(pool->s_d2h, pool->ev_done[c], 0);
-        cudaMemcpyAsync(ho + l0 * qb, d_out + l0 * qb, nl * qb, cudaMemcpyDeviceToHost, pool->s_d2h);
-        if (rc != VW_OK) break;
+        if (rc == VW_OK && graph &&
+            cudaGraphInstantiateWithFlags(&pool->step_exec, graph, 0) == cudaSuccess)
+            pool->step_key = key;
+        else {
+            pool->step_exec = nullptr;            // not recordable (e.g. pageable host buffers):
+            pool->step_bad = key;                 // these arguments stay on the direct path
+        }
+        if (graph) cudaGraphDestroy(graph);
+        (void)cudaGetLastError();
     }
-    cudaEventRecord(pool->ev_exit, pool->s_d2h);
-    cudaStreamWaitEvent(cs, pool->ev_exit, 0);
-    e = cudaStreamSynchronize(pool->s_d2h);
+    if (pool->step_exec && key == pool->step_key) {
+        if ((e = cudaGraphLaunch(pool->step_exec, cs)) != cudaSuccess)
+            return cuda_fail(e, "vw_decode_step_host: graph launch");
+        if ((e = cudaStreamSynchronize(cs)) != cudaSuccess) return cuda_fail(e, "vw_decode_step_host");
+        return VW_OK;
+    }
+    pool->step_seen = key;
+    int32_t rc = enqueue_step_host(pool, a, cs, false);
+    e = cudaStreamSynchronize(cs);
     if (rc != VW_OK) return rc;
     if (e != cudaSuccess) return cuda_fail(e, "vw_decode_step_host");
     e = cudaGetLastError();
