@@ -194,10 +194,14 @@ struct TcTraits {
     static constexpr int TPFX = pf_align((kMaxBatchPerLaunch + 1) * 4, 128);
     // FP8 pools: per stage the round's K scales (x256), then its V scales
     static constexpr int SCL = FP8 ? NST * 2 * KEYS * 4 : 0;
-    static constexpr int NBAR = 2 * NST + 7;          // full, empty; s_full/p_full/p_free x2; done
-    static constexpr int SMEM = 1024 + QBYTES + NST * STAGE + SCL + TPFX + NBAR * 8 + 16;
-    // 4 softmax warps, 1 MMA warp, then 1 TMA producer warp or NDEC decoder warps
-    static constexpr int THREADS = (FP8 ? 5 + NDEC : 6) * 32;
+    // the producer's copy of the first IDS block ids of the sequence's table row
+    static constexpr int IDS = FP8 ? 0 : 512;
+    // full_k, full_v, empty_k, empty_v per stage; s_full/p_full/p_free x2; done
+    static constexpr int NBAR = 4 * NST + 7;
+    static constexpr int SMEM = 1024 + QBYTES + NST * STAGE + SCL + IDS * 4 + TPFX + NBAR * 8 + 16;
+    // 4 softmax warps, 1 MMA warp, then 2 TMA producer warps (K tiles, V tiles)
+    // or NDEC decoder warps
+    static constexpr int THREADS = (FP8 ? 5 + NDEC : 7) * 32;
     static constexpr uint32_t IDESC_S = idesc_f16(MBF, false, kTcRows, KEYS);
     static constexpr uint32_t IDESC_PV = idesc_f16(MBF, true, kTcRows, D);
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
@@ -266,14 +270,16 @@ __device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t
 }
 
 // CTA (tile, q head): 128 query tokens of one sequence for one query head.
-//  * FP8 pools: warps 5-6 (decoders) instead of the producer: per round the
+//  * FP8 pools: warps 5-6 (decoders) instead of the producers: per round the
 //    code rows of the R page-heads, expanded to f16 tiles (fp8_decode_round),
 //    and the round's scales; the softmax scales S by the K scales and P by the
 //    V scales, and the output by 256.
-//  * warp 5 (producer): per round of R page-heads, two TMA boxes per 128-B
-//    column of each page-head, its 16 K rows into the round's K tile and its 16
-//    V rows into the V tile, so that the keys of the round are R*16 rows with a
-//    uniform stride in both tiles.
+//  * warps 5 and 6 (producers): per round of R page-heads, warp 5 loads one TMA
+//    box per 128-B column of each page-head's 16 K rows into the round's K
+//    tile, warp 6 its 16 V rows into the V tile, so that the keys of the round
+//    are R*16 rows with a uniform stride in both tiles.  A stage's K tile and
+//    V tile have their own barriers: the K tile is refilled as soon as S of
+//    its round completes, two rounds before the V tile frees.
 //  * warp 4: allocates tensor memory; one lane issues per round t
 //    S_t = Q K_t^T (D/16 MMAs, M = 128, N = R*16 keys, K = 16; both operands
 //    128-B-swizzled K-major shared-memory tiles) into S buffer t%2, then
@@ -295,10 +301,15 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     uint8_t* qs = base;
     uint8_t* stages = base + T::QBYTES;
     float* scl = reinterpret_cast<float*>(stages + T::NST * T::STAGE);    // FP8 scales
-    int* tpfx = reinterpret_cast<int*>(stages + T::NST * T::STAGE + T::SCL);
-    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tpfx) + T::TPFX);
-    uint64_t* empty = full + T::NST;
-    uint64_t* s_full = empty + T::NST;
+    uint32_t* ids = reinterpret_cast<uint32_t*>(stages + T::NST * T::STAGE + T::SCL);
+    int* tpfx = reinterpret_cast<int*>(stages + T::NST * T::STAGE + T::SCL + T::IDS * 4);
+    // a stage's K tile and V tile fill and drain separately: the K tile is free
+    // once S = Q K^T of its round completes, the V tile only after P V
+    uint64_t* full_k = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tpfx) + T::TPFX);
+    uint64_t* full_v = full_k + T::NST;
+    uint64_t* empty_k = full_v + T::NST;
+    uint64_t* empty_v = empty_k + T::NST;
+    uint64_t* s_full = empty_v + T::NST;
     uint64_t* p_full = s_full + 2;
     uint64_t* p_free = p_full + 2;
     uint64_t* done = p_free + 2;
@@ -308,8 +319,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::NST; ++s) {
-            mbar_init(&full[s], T::FP8 ? T::NDEC : 1);    // decoder warps, or the TMA transaction
-            mbar_init(&empty[s], 1);
+            mbar_init(&full_k[s], T::FP8 ? T::NDEC : 1);  // decoder warps, or the TMA transaction
+            mbar_init(&full_v[s], T::FP8 ? T::NDEC : 1);
+            mbar_init(&empty_k[s], 1);
+            mbar_init(&empty_v[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
@@ -411,6 +424,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         // generic-proxy writes, read next by the tensor cores (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
+    if (!T::FP8 && warp >= 5) {
+        // the producers' copy of the sequence's block ids (no TMA issue waits
+        // for a global load)
+        const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
+        const int nids = min(npages, T::IDS);
+#pragma unroll 4
+        for (int i = threadIdx.x - 5 * 32; i < nids; i += 64) ids[i] = __ldg(bt + i);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -423,54 +444,60 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         bool ok = true;
         for (int t = 0; t < nrounds; ++t) {
             const int st_i = t % T::NST;
+            // the V tile's release follows the K tile's (P V is committed after S)
             if (t >= T::NST &&
-                !__all_sync(0xffffffffu, mbar_wait(&empty[st_i], ((t / T::NST) - 1) & 1, deadline))) {
+                !__all_sync(0xffffffffu, mbar_wait(&empty_v[st_i], ((t / T::NST) - 1) & 1, deadline))) {
                 ok = false;
                 break;
             }
             fp8_decode_round<T>(p, stages + st_i * T::STAGE, scl + st_i * 2 * T::KEYS, bt, t, h, total,
                                 npages, dt);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full[st_i]);
+            if (lane == 0) {
+                mbar_arrive(&full_k[st_i]);
+                mbar_arrive(&full_v[st_i]);
+            }
         }
         if (!ok && lane == 0) atomicOr(p.err, kDevErrTimeout);
-    } else if (warp == 5) {
-        // ---- producer: round t into stage t % NST, R page-heads
-        bool ok = true;
-        for (int t = 0; t < nrounds && ok; ++t) {
-            const int st_i = t % T::NST;
-            const int pg0 = t * T::R, m = min(T::R, npages - pg0);
-            uint32_t blk = 0xFFFFFFFFu;
-            if (lane < m) blk = __ldg(p.block_tables + (size_t)b * p.bt_stride + pg0 + lane);
-            if (lane == 0) {
-                if (t >= T::NST && !mbar_wait(&empty[st_i], ((t / T::NST) - 1) & 1, deadline)) ok = false;
-                if (ok) mbar_arrive_expect_tx(&full[st_i], (uint32_t)(m * 2 * T::CH * T::HALF_BOX));
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            uint8_t* kt = stages + st_i * T::STAGE;
-            for (int pg = 0; pg < m && ok; ++pg) {
-                const uint32_t bj = __shfl_sync(0xffffffffu, blk, pg);
-                if (lane == 0) {
+    } else if (warp >= 5) {
+        // ---- producers: warp 5 streams the rounds' K tiles, warp 6 their V tiles,
+        // each into stage t % NST as soon as that tile of the stage is free (a
+        // K tile after S of its round, a V tile only after P V).  One lane each,
+        // in separate warps so that each can sleep in its own barrier wait.
+        if (lane == 0) {
+            const int kv = warp - 5;
+            uint64_t* fbar = kv ? full_v : full_k;
+            uint64_t* ebar = kv ? empty_v : empty_k;
+            const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
+            bool ok = true;
+            int issued = 0;
+            for (int t = 0; t < nrounds; ++t) {
+                const int st_i = t % T::NST;
+                if (t >= T::NST && !mbar_wait(&ebar[st_i], ((t / T::NST) - 1) & 1, deadline)) {
+                    ok = false;
+                    break;
+                }
+                uint64_t* fb = &fbar[st_i];
+                const int pg0 = t * T::R, m = min(T::R, npages - pg0);
+                mbar_arrive_expect_tx(fb, (uint32_t)(m * T::CH * T::HALF_BOX));
+                uint8_t* tile = stages + st_i * T::STAGE + kv * T::TILE;
+                for (int pg = 0; pg < m; ++pg) {
+                    const uint32_t bj = pg0 + pg < T::IDS ? ids[pg0 + pg] : __ldg(bt + pg0 + pg);
                     int row0 = -32;                      // negative rows: TMA zero-fills
                     if (bj < p.num_blocks)
-                        row0 = (int)(((p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 32u);
-                    else
+                        row0 = (int)(((p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 32u) + 16 * kv;
+                    else if (kv == 0)
                         atomicOr(p.err, kDevErrBlockId);
 #pragma unroll
-                    for (int c = 0; c < T::CH; ++c) {
-                        uint8_t* kd = kt + c * (T::KEYS * 128) + pg * T::HALF_BOX;
-                        tma_load_2d(kd, &tmap, &full[st_i], c * 64, row0);
-                        tma_load_2d(kd + T::TILE, &tmap, &full[st_i], c * 64, row0 + 16);
-                    }
+                    for (int c = 0; c < T::CH; ++c)
+                        tma_load_2d(tile + c * (T::KEYS * 128) + pg * T::HALF_BOX, &tmap, fb, c * 64, row0);
                 }
+                issued = t + 1;
             }
-        }
-        if (lane == 0) {
             if (!ok) atomicOr(p.err, kDevErrTimeout);
             // drain: no TMA write may land after the CTA has exited
-            const int issued = ok ? nrounds : 0;
             for (int t = issued > T::NST ? issued - T::NST : 0; t < issued; ++t)
-                if (!mbar_wait(&full[t % T::NST], (t / T::NST) & 1, deadline)) {
+                if (!mbar_wait(&fbar[t % T::NST], (t / T::NST) & 1, deadline)) {
                     atomicOr(p.err, kDevErrTimeout);
                     break;
                 }
@@ -493,21 +520,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
             auto issue_pv = [&](int t) -> bool {
                 const int bb = t & 1, st_i = t % T::NST;
                 if (!mbar_wait(&p_full[bb], (t >> 1) & 1, deadline)) return false;
-                tc_fence_after();
-                const uint32_t pcol = tbase + T::COL_S + T::KEYS * bb;
-                const uint64_t vst = vdesc0 + (uint64_t)((st_i * T::STAGE) >> 4);
-                for (int pg = 0; pg < T::R && t * T::R + pg < npages; ++pg) {
-                    const uint64_t vdesc = vst + (uint64_t)((pg * T::HALF_BOX) >> 4);
-                    tc_mma_ts(tbase, pcol + 8 * pg, vdesc, T::IDESC_PV, (t > 0 || pg > 0) ? 1u : 0u);
-                    if constexpr (T::PSPLIT) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
-                }
-                tc_commit(&empty[st_i]);
-                tc_commit(&p_free[bb]);
-                return true;
-            };
-            for (int t = 0; t < nrounds && ok; ++t) {
-                const int bb = t & 1, st_i = t % T::NST;
-                if (!mbar_wait(&full[st_i], (t / T::NST) & 1, deadline)) { ok = false; break; }
+                if (!mbar_wait(&full_v[st_i], (t / T::NST) & 1, deadline)) return false;
                 const int keyl = total - t * T::KEYS;   // keys of the round inside the sequence
                 if (!T::FP8 && keyl < T::KEYS && keyl > 0 && (keyl & 15)) {
                     // the page-head holding the sequence's last key: its V rows past
@@ -521,6 +534,21 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                                     make_uint4(0, 0, 0, 0);
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
+                tc_fence_after();
+                const uint32_t pcol = tbase + T::COL_S + T::KEYS * bb;
+                const uint64_t vst = vdesc0 + (uint64_t)((st_i * T::STAGE) >> 4);
+                for (int pg = 0; pg < T::R && t * T::R + pg < npages; ++pg) {
+                    const uint64_t vdesc = vst + (uint64_t)((pg * T::HALF_BOX) >> 4);
+                    tc_mma_ts(tbase, pcol + 8 * pg, vdesc, T::IDESC_PV, (t > 0 || pg > 0) ? 1u : 0u);
+                    if constexpr (T::PSPLIT) tc_mma_ts(tbase, pcol + T::KEYS / 2 + 8 * pg, vdesc, T::IDESC_PV, 1u);
+                }
+                tc_commit(&empty_v[st_i]);
+                tc_commit(&p_free[bb]);
+                return true;
+            };
+            for (int t = 0; t < nrounds && ok; ++t) {
+                const int bb = t & 1, st_i = t % T::NST;
+                if (!mbar_wait(&full_k[st_i], (t / T::NST) & 1, deadline)) { ok = false; break; }
                 // buffer bb holds P_{t-2} until its MMAs complete
                 if (t >= 2 && !mbar_wait(&p_free[bb], ((t - 2) >> 1) & 1, deadline)) { ok = false; break; }
                 tc_fence_after();
@@ -530,6 +558,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 for (int kk = 0; kk < T::KSTEPS; ++kk)
                     tc_mma_ss(dcol, qdesc[kk], kst + (uint64_t)(((kk >> 2) * (T::KEYS * 128) + (kk & 3) * 32) >> 4),
                               T::IDESC_S, kk > 0 ? 1u : 0u);
+                tc_commit(&empty_k[st_i]);
                 tc_commit(&s_full[bb]);
                 if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
             }
@@ -554,7 +583,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
             const int st_i = t % T::NST;
             // FP8: the decoders' scales of the round (their writes precede the
             // stage's full barrier, which has completed before S_t)
-            if (T::FP8 && !__all_sync(0xffffffffu, mbar_wait(&full[st_i], (t / T::NST) & 1, deadline))) {
+            if (T::FP8 && !__all_sync(0xffffffffu, mbar_wait(&full_k[st_i], (t / T::NST) & 1, deadline))) {
                 ok = false;
                 break;
             }
