@@ -64,6 +64,7 @@ typedef enum { VW_FP8_REFERENCE = 0, VW_FP8_OCP = 1 } vw_fp8_mode;
 #define VW_DEV_ERR_SEQ_LEN 0x2u   /* seq_len == 0 or longer than its block-table row */
 #define VW_DEV_ERR_TIMEOUT 0x4u   /* a bounded device wait gave up */
 #define VW_DEV_ERR_SLOT 0x8u      /* an append slot was outside the pool */
+#define VW_DEV_ERR_LAUNCH 0x10u   /* a kernel found its launch unusable and did nothing */
 
 typedef struct vw_pool vw_pool;
 

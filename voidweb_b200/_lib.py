@@ -24,6 +24,7 @@ VW_ERR_OOM = 4
 VW_ERR_DEVICE_CHECK = 5
 # device error word bits (vw_pool_check)
 VW_DEV_ERR_BLOCK_ID, VW_DEV_ERR_SEQ_LEN, VW_DEV_ERR_TIMEOUT, VW_DEV_ERR_SLOT = 0x1, 0x2, 0x4, 0x8
+VW_DEV_ERR_LAUNCH = 0x10
 
 VW_F16, VW_BF16, VW_FP8_E4M3 = 0, 1, 2
 VW_FP8_REFERENCE, VW_FP8_OCP = 0, 1

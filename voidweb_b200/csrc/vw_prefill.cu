@@ -178,11 +178,15 @@ struct TcTraits {
     static constexpr int R = kTcPages;                // page-heads per round
     static constexpr int KEYS = 16 * R;               // keys per round: the N of S = Q K^T
     // round stages: the K rows and the V rows of a round's page-heads, each a tile
-    // [CH][KEYS rows][128 B] (128-B swizzled); head_dim 64 keeps more stages so
-    // that shared memory holds two CTAs per SM, which is what tensor memory allows
+    // [CH][KEYS rows][128 B] (128-B swizzled), in a ring of NSTK K tiles and a
+    // ring of NSTV V tiles.  A K tile frees when S of its round completes, two
+    // rounds before the V tile of that round: with f16/bf16 pages at head_dim
+    // 128 the K ring is one deeper, which is what shared memory holds with two
+    // CTAs per SM (what tensor memory allows); head_dim 64 keeps 4 + 4.
     static constexpr int NST = D == 128 ? 2 : 4;
+    static constexpr int NSTK = (D == 128 && !FP8) ? 3 : NST;
+    static constexpr int NSTV = NST;
     static constexpr int TILE = CH * KEYS * 128;      // bytes of one K (or V) tile
-    static constexpr int STAGE = 2 * TILE;            // K tile, then V tile
     static constexpr int HALF_BOX = 16 * 128;         // one TMA box: 16 rows of one column
     static constexpr int QBYTES = kTcRows * D * 2;    // query tile [CH][128 rows][128 B]
     static constexpr int KSTEPS = D / 16;             // MMAs of S = Q K^T per round
@@ -191,14 +195,17 @@ struct TcTraits {
     // probabilities) is written over the S buffer it was computed from.
     static constexpr int COL_S = D;
     static constexpr uint32_t TMEM_COLS = 256u;       // two CTAs per SM share the 512 columns
+    // the query tiles' prefix over the batch, read only in the prologue: it
+    // lives in the last V tile, which nothing writes before the prologue ends
     static constexpr int TPFX = pf_align((kMaxBatchPerLaunch + 1) * 4, 128);
     // FP8 pools: per stage the round's K scales (x256), then its V scales
     static constexpr int SCL = FP8 ? NST * 2 * KEYS * 4 : 0;
-    // the producer's copy of the first IDS block ids of the sequence's table row
-    static constexpr int IDS = FP8 ? 0 : 512;
-    // full_k, full_v, empty_k, empty_v per stage; s_full/p_full/p_free x2; done
-    static constexpr int NBAR = 4 * NST + 7;
-    static constexpr int SMEM = 1024 + QBYTES + NST * STAGE + SCL + IDS * 4 + TPFX + NBAR * 8 + 16;
+    // full_k, empty_k per K tile, full_v, empty_v per V tile; s_full/p_full/p_free
+    // x2; done
+    static constexpr int NBAR = 2 * NSTK + 2 * NSTV + 7;
+    // the dynamic shared memory starts 1024-B aligned on B200 (checked at run
+    // time: the kernel flags kDevErrLaunch and returns otherwise)
+    static constexpr int SMEM = QBYTES + (NSTK + NSTV) * TILE + SCL + NBAR * 8 + 16;
     // 4 softmax warps, 1 MMA warp, then 2 TMA producer warps (K tiles, V tiles)
     // or NDEC decoder warps
     static constexpr int THREADS = (FP8 ? 5 + NDEC : 7) * 32;
@@ -207,12 +214,15 @@ struct TcTraits {
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
     static_assert(!FP8 || D == 128, "FP8 pools have head_dim 128");
     static_assert(!FP8 || NDEC * 32 == KEYS, "one decoder thread per key of a round (scales)");
+    static_assert(!FP8 || NSTK == NSTV, "FP8 decoders fill a round's K and V tiles together");
+    static_assert(TPFX <= TILE, "the tile prefix fits in a V tile");
     static_assert(COL_S + 2 * KEYS <= (int)TMEM_COLS, "tensor-memory columns");
-    static_assert(STAGE % 1024 == 0 && QBYTES % 1024 == 0 && TILE % 1024 == 0, "1024-B alignment");
+    static_assert(QBYTES % 1024 == 0 && TILE % 1024 == 0, "1024-B alignment");
+    static_assert(2 * (SMEM + 1024) <= 233472, "two CTAs per SM");
     static_assert(3 * (SMEM + 1024) > 233472, "at most two CTAs per SM (tensor memory)");
 };
 
-// FP8 pools: the decoder warps' part of round t.  Thread dt (0 .. 63) loads 16
+// FP8 pools: the decoder warps' part of round t, into its K tile kt and V tile vt.  Thread dt (0 .. 63) loads 16
 // chunks of 16 codes (chunk i: K rows for i < 8, V rows after; page-head
 // (i & 7) / 2, row (i & 1) * 8 + dt / 8, elements (dt % 8) * 16 ..), a warp
 // reading 512 contiguous bytes per load, and writes each as two 16-B f16
@@ -222,7 +232,7 @@ struct TcTraits {
 // page-heads past npages or in an out-of-range block (flagged) are zero rows
 // with zero scales, so that masked probabilities meet no NaN.
 template <class T>
-__device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t* st, float* scl,
+__device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t* kt, uint8_t* vt, float* scl,
                                                  const uint32_t* bt, int t, int h, int total, int npages,
                                                  int dt) {
     const int pg0 = t * T::R;
@@ -257,7 +267,7 @@ __device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         const int key = ((i & 7) >> 1) * 16 + (i & 1) * 8 + (dt >> 3);
-        uint8_t* row = st + (i >> 3) * T::TILE + c * (T::KEYS * 128) + key * 128;
+        uint8_t* row = (i >> 3 ? vt : kt) + c * (T::KEYS * 128) + key * 128;
         const uint4 a = make_uint4(fp8x2_to_f16x2_scaled(w[i].x, 0), fp8x2_to_f16x2_scaled(w[i].x, 1),
                                    fp8x2_to_f16x2_scaled(w[i].y, 0), fp8x2_to_f16x2_scaled(w[i].y, 1));
         const uint4 bq = make_uint4(fp8x2_to_f16x2_scaled(w[i].z, 0), fp8x2_to_f16x2_scaled(w[i].z, 1),
@@ -295,21 +305,24 @@ __device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t
 template <class T>
 __global__ void __launch_bounds__(T::THREADS, 2)
 prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* qs = base;
-    uint8_t* stages = base + T::QBYTES;
-    float* scl = reinterpret_cast<float*>(stages + T::NST * T::STAGE);    // FP8 scales
-    uint32_t* ids = reinterpret_cast<uint32_t*>(stages + T::NST * T::STAGE + T::SCL);
-    int* tpfx = reinterpret_cast<int*>(stages + T::NST * T::STAGE + T::SCL + T::IDS * 4);
-    // a stage's K tile and V tile fill and drain separately: the K tile is free
-    // once S = Q K^T of its round completes, the V tile only after P V
-    uint64_t* full_k = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tpfx) + T::TPFX);
-    uint64_t* full_v = full_k + T::NST;
-    uint64_t* empty_k = full_v + T::NST;
-    uint64_t* empty_v = empty_k + T::NST;
-    uint64_t* s_full = empty_v + T::NST;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the 128-B-swizzled tiles need 1024-B alignment; the layout has no slack
+    if (smem_u32(smem_raw) & 1023u) {
+        if (threadIdx.x == 0) atomicOr(p.err, kDevErrLaunch);
+        return;
+    }
+    uint8_t* qs = smem_raw;
+    uint8_t* ktiles = qs + T::QBYTES;                 // ring of NSTK K tiles
+    uint8_t* vtiles = ktiles + T::NSTK * T::TILE;     // ring of NSTV V tiles
+    float* scl = reinterpret_cast<float*>(vtiles + T::NSTV * T::TILE);   // FP8 scales
+    int* tpfx = reinterpret_cast<int*>(vtiles + (T::NSTV - 1) * T::TILE);   // prologue only
+    // K tiles and V tiles fill and drain separately: a K tile is free once
+    // S = Q K^T of its round completes, a V tile only after P V
+    uint64_t* full_k = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scl) + T::SCL);
+    uint64_t* empty_k = full_k + T::NSTK;
+    uint64_t* full_v = empty_k + T::NSTK;
+    uint64_t* empty_v = full_v + T::NSTV;
+    uint64_t* s_full = empty_v + T::NSTV;
     uint64_t* p_full = s_full + 2;
     uint64_t* p_free = p_full + 2;
     uint64_t* done = p_free + 2;
@@ -318,10 +331,12 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     const uint64_t deadline = cycles() + kWaitDeadlineCycles;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < T::NST; ++s) {
+        for (int s = 0; s < T::NSTK; ++s) {
             mbar_init(&full_k[s], T::FP8 ? T::NDEC : 1);  // decoder warps, or the TMA transaction
-            mbar_init(&full_v[s], T::FP8 ? T::NDEC : 1);
             mbar_init(&empty_k[s], 1);
+        }
+        for (int s = 0; s < T::NSTV; ++s) {
+            mbar_init(&full_v[s], T::FP8 ? T::NDEC : 1);
             mbar_init(&empty_v[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -424,14 +439,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         // generic-proxy writes, read next by the tensor cores (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (!T::FP8 && warp >= 5) {
-        // the producers' copy of the sequence's block ids (no TMA issue waits
-        // for a global load)
-        const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
-        const int nids = min(npages, T::IDS);
-#pragma unroll 4
-        for (int i = threadIdx.x - 5 * 32; i < nids; i += 64) ids[i] = __ldg(bt + i);
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -450,8 +457,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 ok = false;
                 break;
             }
-            fp8_decode_round<T>(p, stages + st_i * T::STAGE, scl + st_i * 2 * T::KEYS, bt, t, h, total,
-                                npages, dt);
+            fp8_decode_round<T>(p, ktiles + st_i * T::TILE, vtiles + st_i * T::TILE, scl + st_i * 2 * T::KEYS,
+                                bt, t, h, total, npages, dt);
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&full_k[st_i]);
@@ -460,44 +467,60 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         }
         if (!ok && lane == 0) atomicOr(p.err, kDevErrTimeout);
     } else if (warp >= 5) {
-        // ---- producers: warp 5 streams the rounds' K tiles, warp 6 their V tiles,
-        // each into stage t % NST as soon as that tile of the stage is free (a
-        // K tile after S of its round, a V tile only after P V).  One lane each,
-        // in separate warps so that each can sleep in its own barrier wait.
-        if (lane == 0) {
-            const int kv = warp - 5;
-            uint64_t* fbar = kv ? full_v : full_k;
-            uint64_t* ebar = kv ? empty_v : empty_k;
-            const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
-            bool ok = true;
-            int issued = 0;
-            for (int t = 0; t < nrounds; ++t) {
-                const int st_i = t % T::NST;
-                if (t >= T::NST && !mbar_wait(&ebar[st_i], ((t / T::NST) - 1) & 1, deadline)) {
-                    ok = false;
-                    break;
-                }
-                uint64_t* fb = &fbar[st_i];
-                const int pg0 = t * T::R, m = min(T::R, npages - pg0);
-                mbar_arrive_expect_tx(fb, (uint32_t)(m * T::CH * T::HALF_BOX));
-                uint8_t* tile = stages + st_i * T::STAGE + kv * T::TILE;
-                for (int pg = 0; pg < m; ++pg) {
-                    const uint32_t bj = pg0 + pg < T::IDS ? ids[pg0 + pg] : __ldg(bt + pg0 + pg);
-                    int row0 = -32;                      // negative rows: TMA zero-fills
-                    if (bj < p.num_blocks)
-                        row0 = (int)(((p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 32u) + 16 * kv;
-                    else if (kv == 0)
-                        atomicOr(p.err, kDevErrBlockId);
-#pragma unroll
-                    for (int c = 0; c < T::CH; ++c)
-                        tma_load_2d(tile + c * (T::KEYS * 128) + pg * T::HALF_BOX, &tmap, fb, c * 64, row0);
-                }
-                issued = t + 1;
+        // ---- producers: warp 5 streams the rounds' K tiles into the K ring, warp 6
+        // their V tiles into the V ring, each as soon as the tile it refills is
+        // free (a K tile after S of its round, a V tile only after P V).  Separate
+        // warps, so that each sleeps in its own barrier wait.  The block ids come
+        // in windows of 32 pages (8 rounds), one per lane; the next window is
+        // loaded when the current one starts, so no copy waits for its id.
+        const int kv = warp - 5;
+        const int ns = kv ? T::NSTV : T::NSTK;
+        uint64_t* fbar = kv ? full_v : full_k;
+        uint64_t* ebar = kv ? empty_v : empty_k;
+        uint8_t* tiles = kv ? vtiles : ktiles;
+        const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
+        if (lane == 0) prefetch_tensormap(&tmap);
+        constexpr int WIN = 32 / T::R;                // rounds per id window
+        uint32_t win = lane < npages ? __ldg(bt + lane) : 0xFFFFFFFFu;
+        uint32_t nwin = 32 + lane < npages ? __ldg(bt + 32 + lane) : 0xFFFFFFFFu;
+        bool ok = true;
+        int issued = 0;
+        for (int t = 0; t < nrounds; ++t) {
+            const int st_i = t % ns;
+            if (t > 0 && t % WIN == 0) {
+                win = nwin;
+                const int pn = (t / WIN + 1) * 32 + lane;
+                nwin = pn < npages ? __ldg(bt + pn) : 0xFFFFFFFFu;
             }
+            if (t >= ns && !__all_sync(0xffffffffu, mbar_wait(&ebar[st_i], ((t / ns) - 1) & 1, deadline))) {
+                ok = false;
+                break;
+            }
+            uint64_t* fb = &fbar[st_i];
+            const int pg0 = t * T::R, m = min(T::R, npages - pg0);
+            if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(m * T::CH * T::HALF_BOX));
+            __syncwarp();
+            // one box per lane: lane l copies column l % CH of page-head l / CH
+            // (the producers share their schedulers with the softmax warps, so
+            // the round's copies go out as one warp instruction)
+            const int pg = lane / T::CH, c = lane % T::CH;
+            const uint32_t bj = __shfl_sync(0xffffffffu, win, (t % WIN) * T::R + (pg < T::R ? pg : 0));
+            if (pg < m) {
+                int row0 = -32;                          // negative rows: TMA zero-fills
+                if (bj < p.num_blocks)
+                    row0 = (int)(((p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 32u) + 16 * kv;
+                else if (kv == 0 && c == 0)
+                    atomicOr(p.err, kDevErrBlockId);
+                tma_load_2d(tiles + st_i * T::TILE + c * (T::KEYS * 128) + pg * T::HALF_BOX, &tmap, fb, c * 64,
+                            row0);
+            }
+            issued = t + 1;
+        }
+        if (lane == 0) {
             if (!ok) atomicOr(p.err, kDevErrTimeout);
             // drain: no TMA write may land after the CTA has exited
-            for (int t = issued > T::NST ? issued - T::NST : 0; t < issued; ++t)
-                if (!mbar_wait(&fbar[t % T::NST], (t / T::NST) & 1, deadline)) {
+            for (int t = issued > ns ? issued - ns : 0; t < issued; ++t)
+                if (!mbar_wait(&fbar[t % ns], (t / ns) & 1, deadline)) {
                     atomicOr(p.err, kDevErrTimeout);
                     break;
                 }
@@ -515,18 +538,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 qdesc[kk] = smem_desc_sw128(smem_u32(qs) + (kk >> 2) * (kTcRows * 128) + (kk & 3) * 32, 16, 1024);
             // K tile: K-major, 8-key groups 1024 B apart; V tile: MN-major, 64-element
             // columns KEYS*128 B apart, 8-key groups 1024 B apart
-            const uint64_t kdesc0 = smem_desc_sw128(smem_u32(stages), 16, 1024);
-            const uint64_t vdesc0 = smem_desc_sw128(smem_u32(stages) + T::TILE, T::KEYS * 128, 1024);
+            const uint64_t kdesc0 = smem_desc_sw128(smem_u32(ktiles), 16, 1024);
+            const uint64_t vdesc0 = smem_desc_sw128(smem_u32(vtiles), T::KEYS * 128, 1024);
             auto issue_pv = [&](int t) -> bool {
-                const int bb = t & 1, st_i = t % T::NST;
+                const int bb = t & 1, st_i = t % T::NSTV;
                 if (!mbar_wait(&p_full[bb], (t >> 1) & 1, deadline)) return false;
-                if (!mbar_wait(&full_v[st_i], (t / T::NST) & 1, deadline)) return false;
+                if (!mbar_wait(&full_v[st_i], (t / T::NSTV) & 1, deadline)) return false;
                 const int keyl = total - t * T::KEYS;   // keys of the round inside the sequence
                 if (!T::FP8 && keyl < T::KEYS && keyl > 0 && (keyl & 15)) {
                     // the page-head holding the sequence's last key: its V rows past
                     // the end hold whatever the pool has there; zero them so that
                     // masked probabilities cannot meet NaN or Inf
-                    uint8_t* vt = stages + st_i * T::STAGE + T::TILE;
+                    uint8_t* vt = vtiles + st_i * T::TILE;
                     for (int c = 0; c < T::CH; ++c)
                         for (int row = keyl; row < ((keyl + 15) & ~15); ++row)
                             for (int u = 0; u < 8; ++u)
@@ -536,7 +559,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 }
                 tc_fence_after();
                 const uint32_t pcol = tbase + T::COL_S + T::KEYS * bb;
-                const uint64_t vst = vdesc0 + (uint64_t)((st_i * T::STAGE) >> 4);
+                const uint64_t vst = vdesc0 + (uint64_t)((st_i * T::TILE) >> 4);
                 for (int pg = 0; pg < T::R && t * T::R + pg < npages; ++pg) {
                     const uint64_t vdesc = vst + (uint64_t)((pg * T::HALF_BOX) >> 4);
                     tc_mma_ts(tbase, pcol + 8 * pg, vdesc, T::IDESC_PV, (t > 0 || pg > 0) ? 1u : 0u);
@@ -547,12 +570,12 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
                 return true;
             };
             for (int t = 0; t < nrounds && ok; ++t) {
-                const int bb = t & 1, st_i = t % T::NST;
-                if (!mbar_wait(&full_k[st_i], (t / T::NST) & 1, deadline)) { ok = false; break; }
+                const int bb = t & 1, st_i = t % T::NSTK;
+                if (!mbar_wait(&full_k[st_i], (t / T::NSTK) & 1, deadline)) { ok = false; break; }
                 // buffer bb holds P_{t-2} until its MMAs complete
                 if (t >= 2 && !mbar_wait(&p_free[bb], ((t - 2) >> 1) & 1, deadline)) { ok = false; break; }
                 tc_fence_after();
-                const uint64_t kst = kdesc0 + (uint64_t)((st_i * T::STAGE) >> 4);
+                const uint64_t kst = kdesc0 + (uint64_t)((st_i * T::TILE) >> 4);
                 const uint32_t dcol = tbase + T::COL_S + T::KEYS * bb;
 #pragma unroll
                 for (int kk = 0; kk < T::KSTEPS; ++kk)

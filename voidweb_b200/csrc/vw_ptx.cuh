@@ -15,6 +15,7 @@ enum : uint32_t {
     kDevErrSeqLen = 1u << 1,      // seq_len == 0 or longer than the block table row
     kDevErrTimeout = 1u << 2,     // a bounded wait gave up
     kDevErrSlot = 1u << 3,        // append slot outside the pool
+    kDevErrLaunch = 1u << 4,      // unusable launch (dynamic shared memory not 1024-B aligned)
 };
 
 // Wait deadline in SM cycles: 4e9 cycles is about 2 s at the 1965 MHz maximum
