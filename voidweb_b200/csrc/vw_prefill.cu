@@ -14,18 +14,22 @@
 // seq_kv, without a mask).
 //
 //  * Work split.  CTA (tile, q head): 128 query tokens of one sequence for one
-//    query head; the page-heads of the head's KV head stream through a ring of
-//    shared-memory stages (one TMA box per page-head, the decode's tensor map).
-//  * Math on the fifth-generation tensor cores (tcgen05): per page-head,
-//    S = Q K^T with M = 128 query rows and N = 16 keys (A = the query tile, B =
-//    the staged K rows, both 128-B-swizzled K-major shared-memory operands),
-//    accumulated in tensor memory; four softmax warps (one query row per
-//    thread, no shuffles) read S, apply the causal / length mask and an online
-//    softmax with a lazily raised maximum, and write P back to tensor memory;
-//    then O += P V with P from tensor memory and the staged V rows as an
+//    query head; the keys of the head's KV head stream through shared memory in
+//    rounds of 4 page-heads (64 keys): a ring of K tiles and a ring of V tiles,
+//    filled by TMA through a second tensor map of the pool (boxes of 16 rows of
+//    one 128-B column), so that a round's keys have a uniform row stride.
+//  * Math on the fifth-generation tensor cores (tcgen05): per round, S = Q K^T
+//    with M = 128 query rows and N = 64 keys (A = the query tile, B = the K
+//    tile, both 128-B-swizzled K-major shared-memory operands), accumulated in
+//    tensor memory; four softmax warps (one query row per thread, no shuffles)
+//    read S, apply the causal / length mask and an online softmax with a
+//    lazily raised maximum, and write P back to tensor memory over S; then
+//    O += P V per page-head with P from tensor memory and the V tile as an
 //    MN-major operand (M = 128, N = head_dim, K = 16 keys).  O stays in tensor
 //    memory until the epilogue.  bf16 probabilities are written as a bf16 pair
 //    hi + lo (two PV MMAs) so that P keeps ~2^-18 relative precision.
+//  * FP8 pools: decoder warps expand the codes into the same f16 tiles; the
+//    softmax applies the per-token K and V scales.
 //  * Every wait is bounded; on timeout the kernel records kDevErrTimeout,
 //    drains its TMA loads and returns.
 #include <cuda.h>
