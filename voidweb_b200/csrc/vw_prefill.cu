@@ -226,56 +226,66 @@ struct TcTraits {
     static_assert(3 * (SMEM + 1024) > 233472, "at most two CTAs per SM (tensor memory)");
 };
 
-// FP8 pools: the decoder warps' part of round t, into its K tile kt and V tile vt.  Thread dt (0 .. 63) loads 16
-// chunks of 16 codes (chunk i: K rows for i < 8, V rows after; page-head
-// (i & 7) / 2, row (i & 1) * 8 + dt / 8, elements (dt % 8) * 16 ..), a warp
-// reading 512 contiguous bytes per load, and writes each as two 16-B f16
-// units into the tile layout the TMA gives an f16 pool: [column][KEYS rows]
-// [128 B], unit u of key row k at (u ^ (k % 8)) * 16.  Thread dt also stages
-// key dt's K scale (x256) and V scale.  Keys past the sequence's end, in
-// page-heads past npages or in an out-of-range block (flagged) are zero rows
-// with zero scales, so that masked probabilities meet no NaN.
+// FP8 pools: the decoder warps' part of round t, in two halves so that the
+// global loads of a round are in flight while the decoders wait for its stage.
+// Thread dt (0 .. 63) loads 16 chunks of 16 codes (chunk i: K rows for i < 8,
+// V rows after; page-head (i & 7) / 2, row (i & 1) * 8 + dt / 8, elements
+// (dt % 8) * 16 ..), a warp reading 512 contiguous bytes per load, and key dt's
+// K scale (x256) and V scale; then, once the stage is free, writes each chunk as
+// two 16-B f16 units into the tile layout the TMA gives an f16 pool: [column]
+// [KEYS rows][128 B], unit u of key row k at (u ^ (k % 8)) * 16.  Keys past the
+// sequence's end, in page-heads past npages or in an out-of-range block
+// (flagged) are zero rows with zero scales, so that masked probabilities meet
+// no NaN.
+struct Fp8RoundRegs {
+    uint4 w[16];
+    float ks, vs;
+};
+
 template <class T>
-__device__ __forceinline__ void fp8_decode_round(const PrefillParams& p, uint8_t* kt, uint8_t* vt, float* scl,
-                                                 const uint32_t* bt, int t, int h, int total, int npages,
-                                                 int dt) {
-    const int pg0 = t * T::R;
-    uint32_t blk[T::R];
+__device__ __forceinline__ void fp8_round_ids(const uint32_t* bt, int t, int npages, uint32_t (&blk)[T::R]) {
 #pragma unroll
-    for (int pg = 0; pg < T::R; ++pg) {
-        blk[pg] = 0xFFFFFFFFu;
-        if (pg0 + pg < npages) {
-            blk[pg] = __ldg(bt + pg0 + pg);
-            if (blk[pg] >= p.num_blocks && dt == 0) atomicOr(p.err, kDevErrBlockId);
-        }
-    }
+    for (int pg = 0; pg < T::R; ++pg) blk[pg] = t * T::R + pg < npages ? __ldg(bt + t * T::R + pg) : 0xFFFFFFFFu;
+}
+
+template <class T>
+__device__ __forceinline__ void fp8_load_round(const PrefillParams& p, const uint32_t (&blk)[T::R], int t, int h,
+                                               int total, int npages, int dt, Fp8RoundRegs& r) {
+    if (dt == 0)
+#pragma unroll
+        for (int pg = 0; pg < T::R; ++pg)
+            if (t * T::R + pg < npages && blk[pg] >= p.num_blocks) atomicOr(p.err, kDevErrBlockId);
     auto head_row = [&](uint32_t bj, int kv) -> size_t {   // first row of the K (kv 0) or V half
         return ((((size_t)p.layer * p.num_blocks + bj) * p.Hkv + (uint32_t)h) * 2 + kv) * kBlockSize;
     };
     const int e0 = (dt & 7) * 16;
-    uint4 w[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         const int pg = (i & 7) >> 1, rr = (i & 1) * 8 + (dt >> 3);
         const bool valid = blk[pg] < p.num_blocks && t * T::KEYS + pg * 16 + rr < total;
-        w[i] = valid ? __ldg(reinterpret_cast<const uint4*>(p.kv_data + (head_row(blk[pg], i >> 3) + rr) * T::D + e0))
-                     : make_uint4(0, 0, 0, 0);
+        r.w[i] = valid ? __ldg(reinterpret_cast<const uint4*>(p.kv_data + (head_row(blk[pg], i >> 3) + rr) * T::D + e0))
+                       : make_uint4(0, 0, 0, 0);
     }
-    {
-        const int pg = dt >> 4, rr = dt & 15;
-        const bool valid = blk[pg] < p.num_blocks && t * T::KEYS + dt < total;
-        scl[dt] = valid ? __ldg(p.kv_scales + head_row(blk[pg], 0) + rr) * 256.0f : 0.0f;
-        scl[T::KEYS + dt] = valid ? __ldg(p.kv_scales + head_row(blk[pg], 1) + rr) : 0.0f;
-    }
-    const int c = e0 >> 6, ua = (e0 & 63) >> 3;
+    const int pg = dt >> 4, rr = dt & 15;
+    const bool valid = blk[pg] < p.num_blocks && t * T::KEYS + dt < total;
+    r.ks = valid ? __ldg(p.kv_scales + head_row(blk[pg], 0) + rr) * 256.0f : 0.0f;
+    r.vs = valid ? __ldg(p.kv_scales + head_row(blk[pg], 1) + rr) : 0.0f;
+}
+
+template <class T>
+__device__ __forceinline__ void fp8_store_round(uint8_t* kt, uint8_t* vt, float* scl, int dt,
+                                                const Fp8RoundRegs& r) {
+    scl[dt] = r.ks;
+    scl[T::KEYS + dt] = r.vs;
+    const int e0 = (dt & 7) * 16, c = e0 >> 6, ua = (e0 & 63) >> 3;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         const int key = ((i & 7) >> 1) * 16 + (i & 1) * 8 + (dt >> 3);
         uint8_t* row = (i >> 3 ? vt : kt) + c * (T::KEYS * 128) + key * 128;
-        const uint4 a = make_uint4(fp8x2_to_f16x2_scaled(w[i].x, 0), fp8x2_to_f16x2_scaled(w[i].x, 1),
-                                   fp8x2_to_f16x2_scaled(w[i].y, 0), fp8x2_to_f16x2_scaled(w[i].y, 1));
-        const uint4 bq = make_uint4(fp8x2_to_f16x2_scaled(w[i].z, 0), fp8x2_to_f16x2_scaled(w[i].z, 1),
-                                    fp8x2_to_f16x2_scaled(w[i].w, 0), fp8x2_to_f16x2_scaled(w[i].w, 1));
+        const uint4 a = make_uint4(fp8x2_to_f16x2_scaled(r.w[i].x, 0), fp8x2_to_f16x2_scaled(r.w[i].x, 1),
+                                   fp8x2_to_f16x2_scaled(r.w[i].y, 0), fp8x2_to_f16x2_scaled(r.w[i].y, 1));
+        const uint4 bq = make_uint4(fp8x2_to_f16x2_scaled(r.w[i].z, 0), fp8x2_to_f16x2_scaled(r.w[i].z, 1),
+                                    fp8x2_to_f16x2_scaled(r.w[i].w, 0), fp8x2_to_f16x2_scaled(r.w[i].w, 1));
         *reinterpret_cast<uint4*>(row + ((ua ^ (key & 7)) << 4)) = a;
         *reinterpret_cast<uint4*>(row + (((ua + 1) ^ (key & 7)) << 4)) = bq;
     }
@@ -453,16 +463,23 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         const int dt = threadIdx.x - 5 * 32;
         const uint32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
         bool ok = true;
+        uint32_t nblk[T::R];
+        fp8_round_ids<T>(bt, 0, npages, nblk);
         for (int t = 0; t < nrounds; ++t) {
             const int st_i = t % T::NST;
+            uint32_t blk[T::R];
+#pragma unroll
+            for (int pg = 0; pg < T::R; ++pg) blk[pg] = nblk[pg];
+            Fp8RoundRegs r;
+            fp8_load_round<T>(p, blk, t, h, total, npages, dt, r);   // in flight during the wait
+            fp8_round_ids<T>(bt, t + 1, npages, nblk);
             // the V tile's release follows the K tile's (P V is committed after S)
             if (t >= T::NST &&
                 !__all_sync(0xffffffffu, mbar_wait(&empty_v[st_i], ((t / T::NST) - 1) & 1, deadline))) {
                 ok = false;
                 break;
             }
-            fp8_decode_round<T>(p, ktiles + st_i * T::TILE, vtiles + st_i * T::TILE, scl + st_i * 2 * T::KEYS,
-                                bt, t, h, total, npages, dt);
+            fp8_store_round<T>(ktiles + st_i * T::TILE, vtiles + st_i * T::TILE, scl + st_i * 2 * T::KEYS, dt, r);
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&full_k[st_i]);
