@@ -202,7 +202,15 @@ VW_API int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block
 
 /* One decode step over every layer with HOST buffers (the end-to-end path):
  * copies the step's inputs host->device, runs append + decode per layer, and
- * copies the attention outputs device->host before returning. */
+ * copies the attention outputs device->host before returning (the call
+ * synchronises with `stream`).  The second call with the same arguments and
+ * buffers (same host pointers, sizes, scale and rope_theta) records the step
+ * as a CUDA graph, which later identical calls replay: uploads of 1, 1, 2, 4,
+ * ... layers ahead of the layers that read them, each layer's outputs read
+ * back as soon as it ends.  Calls with other buffers run directly on the
+ * stream; buffers that cannot be recorded (e.g. pageable host memory) stay on
+ * the direct path.  Pinned host buffers reused across steps are the fast
+ * case.  Not for use inside the caller's own stream capture. */
 typedef struct {
     uint32_t num_seqs;
     uint32_t num_q_heads;
