@@ -131,6 +131,24 @@ def test_fused_append_decode(dev, kv, io, mode):
     pool.close()
 
 
+@pytest.mark.parametrize("kv,io", [(BF16, BF16), (FP8, BF16)])
+def test_max_batch_fused_append_decode(dev, kv, io):
+    # the largest batch one launch takes (1024 sequences: the prefix tables the
+    # decode keeps in shared memory at their full size), short ragged contexts
+    c = kvgen.make_case(31 + kv, 1, 2, 128, 8, 1024, 1, 40, kv, io)
+    pool = make_pool(c, dev)
+    got = run_decode(pool, c, 0, dev, fused=True)
+    assert pool.check() == 0
+    data, scales = c.data.copy(), None if c.scales is None else c.scales.copy()
+    oracle.kv_append(c.geom, data, scales, 0, c.k_new[0], c.v_new[0], kvgen.new_token_slots(c))
+    gdata, _ = download_pool(pool, c)
+    assert np.array_equal(gdata, data), "pages after the fused append differ from the oracle"
+    ref = oracle.paged_decode_f64(c.geom, data, scales, 0, c.q[0], c.Hq, c.block_tables, c.seq_lens,
+                                  1.0 / np.sqrt(128))
+    check_close(got, ref, io, f"max batch kv={kv}")
+    pool.close()
+
+
 @pytest.mark.parametrize("kv,io,mode", [(F16, F16, 0), (BF16, BF16, 0), (FP8, BF16, 0),
                                         (FP8, BF16, 1), (FP8, F16, 1)])
 def test_append_bit_exact(dev, kv, io, mode):

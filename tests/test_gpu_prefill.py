@@ -88,6 +88,27 @@ def test_prefill_append_and_attention(dev, kv, io, D, Hq, Hkv, chunks, causal):
     pool.close()
 
 
+@pytest.mark.parametrize("kv", [BF16, FP8])
+def test_prefill_max_batch(dev, kv):
+    # 1024 sequences (the most one launch takes), each a chunk of 0 to 3 tokens
+    # after 0 to 40 cached tokens: the per-sequence query-tile prefix the kernel
+    # builds in shared memory at its full size
+    rng = np.random.default_rng(17 + kv)
+    chunks = [(int(rng.integers(0, 41)), int(rng.integers(0, 4))) for _ in range(1024)]
+    chunks[0] = (0, 1)
+    c, q, k, v, cu, cs = chunk_case(19 + kv, BF16, 128, 8, 2, chunks, L=1, kv=kv)
+    pool = make_pool(c, dev)
+    got = run_prefill(pool, c, 0, q, k, v, cu, cs, dev)
+    assert pool.check() == 0
+    oracle.kv_append(c.geom, c.data, c.scales, 0, k, v, oracle.prefill_slots(c.block_tables, cu, cs))
+    gdata, _ = download_pool(pool, c)
+    assert np.array_equal(gdata, c.data)
+    ref = oracle.paged_prefill_f64(c.geom, c.data, c.scales, 0, q, c.Hq, c.block_tables, cu, cs, True,
+                                   1.0 / np.sqrt(128))
+    check_close(got, ref, BF16, f"max batch prefill kv={kv}")
+    pool.close()
+
+
 def test_prefill_over_cached_pages_without_append(dev):
     # k_new = None: the pages already hold the chunk's rows (e.g. a re-run)
     c, q, _, _, cu, cs = chunk_case(77, BF16, 128, 16, 4, [(50, 80), (0, 3)])

@@ -132,6 +132,10 @@ struct Traits {
     static constexpr int STAGE = 32 * ROW;                   // one page-head: K rows 0-15, V 16-31
     static constexpr int SCAL = KV == kFP8 ? 128 : 0;        // K and V scales of a page-head
     static constexpr bool MMA_BF16 = KV == kBF16;            // FP8 pages compute in f16
+    // P as a pair hi + lo of the MMA type, two P V MMAs: a single bf16 (2^-9)
+    // or f16 x V-scale (2^-11) probability puts outputs whose few large V terms
+    // cancel outside max-abs 2e-3 / rel 1e-2; f16 pools keep a single f16 P
+    static constexpr bool PSPLIT = KV == kBF16 || KV == kFP8;
     static constexpr int KT = D / 16;                        // k-steps of Q K^T
     static constexpr int MT = D / 16;                        // d-tiles of V^T P^T
     // FP8 merge rows of D + 4 floats: a warp's stores of its O^T fragments
@@ -948,7 +952,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                     }
                 }
             }
-            uint32_t pb[T::NT][2];
+            uint32_t pb[T::NT][2], pl[T::NT][2];
 #pragma unroll
             for (int nt = 0; nt < T::NT; ++nt) {
                 const float p00 = ex2(sv[nt][0] - mrun[nt][0]), p01 = ex2(sv[nt][1] - mrun[nt][1]);
@@ -960,8 +964,26 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                     q00 = v0 ? p00 * vs0 : 0.0f; q01 = v0 ? p01 * vs0 : 0.0f;
                     q10 = v1 ? p10 * vs1 : 0.0f; q11 = v1 ? p11 * vs1 : 0.0f;
                 }
-                pb[nt][0] = movmatrix_t(pack2<T::MMA_BF16>(q00, q01));
-                pb[nt][1] = movmatrix_t(pack2<T::MMA_BF16>(q10, q11));
+                if constexpr (T::MMA_BF16) {
+                    // hi = q truncated to bf16 (its top 16 bits), lo = q - hi (exact
+                    // in f32) rounded to bf16
+                    const uint32_t h00 = __float_as_uint(q00) & 0xFFFF0000u, h01 = __float_as_uint(q01) & 0xFFFF0000u;
+                    const uint32_t h10 = __float_as_uint(q10) & 0xFFFF0000u, h11 = __float_as_uint(q11) & 0xFFFF0000u;
+                    pb[nt][0] = movmatrix_t(__byte_perm(h00, h01, 0x7632));
+                    pb[nt][1] = movmatrix_t(__byte_perm(h10, h11, 0x7632));
+                    pl[nt][0] = movmatrix_t(pack2<true>(q00 - __uint_as_float(h00), q01 - __uint_as_float(h01)));
+                    pl[nt][1] = movmatrix_t(pack2<true>(q10 - __uint_as_float(h10), q11 - __uint_as_float(h11)));
+                } else {
+                    const uint32_t a = pack2<false>(q00, q01), c = pack2<false>(q10, q11);
+                    pb[nt][0] = movmatrix_t(a);
+                    pb[nt][1] = movmatrix_t(c);
+                    if constexpr (T::PSPLIT) {
+                        pl[nt][0] = movmatrix_t(pack2<false>(q00 - f16_bits_to_f32(a & 0xFFFFu),
+                                                             q01 - f16_bits_to_f32(a >> 16)));
+                        pl[nt][1] = movmatrix_t(pack2<false>(q10 - f16_bits_to_f32(c & 0xFFFFu),
+                                                             q11 - f16_bits_to_f32(c >> 16)));
+                    }
+                }
             }
 
             // ---- O^T += V^T P^T  (D x 8*NT); V is stage rows 16-31
@@ -980,8 +1002,10 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                     ldsm_x4_t(addr, a0, a1, a2, a3);
                 }
 #pragma unroll
-                for (int nt = 0; nt < T::NT; ++nt)
+                for (int nt = 0; nt < T::NT; ++nt) {
                     mma_16816<T::MMA_BF16>(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+                    if constexpr (T::PSPLIT) mma_16816<T::MMA_BF16>(o[nt][mt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+                }
             }
             __syncwarp();
             if constexpr (T::KV != kFP8) {
