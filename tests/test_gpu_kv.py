@@ -131,11 +131,11 @@ def test_fused_append_decode(dev, kv, io, mode):
     pool.close()
 
 
-@pytest.mark.parametrize("kv,io", [(BF16, BF16), (FP8, BF16)])
-def test_max_batch_fused_append_decode(dev, kv, io):
+@pytest.mark.parametrize("kv,io,D", [(BF16, BF16, 128), (FP8, BF16, 128), (F16, F16, 64)])
+def test_max_batch_fused_append_decode(dev, kv, io, D):
     # the largest batch one launch takes (1024 sequences: the prefix tables the
     # decode keeps in shared memory at their full size), short ragged contexts
-    c = kvgen.make_case(31 + kv, 1, 2, 128, 8, 1024, 1, 40, kv, io)
+    c = kvgen.make_case(31 + kv, 1, 2, D, 8, 1024, 1, 40, kv, io)
     pool = make_pool(c, dev)
     got = run_decode(pool, c, 0, dev, fused=True)
     assert pool.check() == 0
@@ -144,7 +144,7 @@ def test_max_batch_fused_append_decode(dev, kv, io):
     gdata, _ = download_pool(pool, c)
     assert np.array_equal(gdata, data), "pages after the fused append differ from the oracle"
     ref = oracle.paged_decode_f64(c.geom, data, scales, 0, c.q[0], c.Hq, c.block_tables, c.seq_lens,
-                                  1.0 / np.sqrt(128))
+                                  1.0 / np.sqrt(D))
     check_close(got, ref, io, f"max batch kv={kv}")
     pool.close()
 
