@@ -88,6 +88,9 @@ DECODE_CASES = [
     ("f16_d128_g4", 1, 2, 128, 8, 6, 1, 800, F16, F16),
     ("fp8_llama8b_g4", 1, 2, 128, 8, 5, 50, 900, FP8, BF16),
     ("fp8_f16io_g8", 1, 1, 128, 8, 4, 1, 400, FP8, F16),
+    # long contexts (the Llama-3-8B FP8 configuration reaches 32K tokens)
+    ("long_bf16_32k", 1, 2, 128, 8, 3, 16000, 32768, BF16, BF16),
+    ("long_fp8_32k", 1, 2, 128, 8, 3, 16000, 32768, FP8, BF16),
 ]
 
 

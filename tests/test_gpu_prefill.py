@@ -89,6 +89,21 @@ def test_prefill_append_and_attention(dev, kv, io, D, Hq, Hkv, chunks, causal):
 
 
 @pytest.mark.parametrize("kv", [BF16, FP8])
+def test_prefill_long_context(dev, kv):
+    # chunks after 30,000 and 12,345 cached tokens: hundreds of rounds through
+    # the K and V rings and dozens of block-id windows per query tile
+    c, q, k, v, cu, cs = chunk_case(23 + kv, BF16, 128, 8, 2, [(30000, 64), (12345, 130)], L=1, kv=kv)
+    pool = make_pool(c, dev)
+    got = run_prefill(pool, c, 0, q, k, v, cu, cs, dev)
+    assert pool.check() == 0
+    oracle.kv_append(c.geom, c.data, c.scales, 0, k, v, oracle.prefill_slots(c.block_tables, cu, cs))
+    ref = oracle.paged_prefill_f64(c.geom, c.data, c.scales, 0, q, c.Hq, c.block_tables, cu, cs, True,
+                                   1.0 / np.sqrt(128))
+    check_close(got, ref, BF16, f"long-context prefill kv={kv}")
+    pool.close()
+
+
+@pytest.mark.parametrize("kv", [BF16, FP8])
 def test_prefill_max_batch(dev, kv):
     # 1024 sequences (the most one launch takes), each a chunk of 0 to 3 tokens
     # after 0 to 40 cached tokens: the per-sequence query-tile prefix the kernel
