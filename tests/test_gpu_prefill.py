@@ -3,7 +3,8 @@ bit-exact against the oracle's append at the paging rule's slots, and the
 attention is within |gpu - ref| <= 2e-3 + 1e-2 * |ref| of the oracle's fp64
 restatement of flash_attention.bm:31-106 over the pool, causal and not.
 Cases: ragged chunks (1, 16, 63, 64, 65, 129, 300 tokens), cached prefixes
-(ctx_start 0 to 1000), an empty chunk, GQA groups 1 to 7, head_dim 64 and 128,
+(ctx_start 0 to 30,000), an empty chunk, the largest batch (1024 sequences),
+GQA groups 1 to 7, head_dim 64 and 128,
 f16 and bf16 pages, FP8 E4M3 pages with per-token-per-head scales (codes and
 scales of the append bit-exact, the attention against the fp64 oracle over the
 same dequantised codes), NaN garbage past every sequence's end, RoPE, the error
