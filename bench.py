@@ -9,8 +9,9 @@ head_dim 128, bf16 KV, 16 sequences with context lengths uniform in
 Synthetic inputs (no dataset); K/V/Q drawn N(0,1).
 
 N GPUs (torchrun, one process per GPU): every rank holds its own shard of
-sequences (weak scaling: 16 sequences per GPU), and the per-shard attention
-outputs of each step are all-gathered over NCCL.
+sequences (weak scaling: 16 sequences per GPU; with --scaling strong the one
+16-sequence batch of the 1-GPU run is split across the GPUs), and the
+per-shard attention outputs of each step are all-gathered over NCCL.
 
 --impl reference times the reference's CPU implementation of this path (the
 oracle's restatement of paged_attention_decode + append, f32, all host
@@ -458,6 +459,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=DEFAULT, choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: every GPU brings the workload's batch; strong: one batch split across the GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="run only this many layers of the workload (a small case for ncu "
@@ -506,7 +509,16 @@ def main():
     from voidweb_b200.kv import KvPool, PoolSpec
 
     L, Hq, Hkv, D, B = w["L"], w["Hq"], w["Hkv"], w["D"], w["B"]
-    seq_lens = ctx_lengths(w, rank)                  # each rank: its own shard of sequences
+    if args.scaling == "strong":
+        # one fixed batch (the 1-GPU workload's seeded contexts) split across the ranks
+        if B % world:
+            raise SystemExit(f"--scaling strong needs the batch ({B}) divisible by the GPUs ({world})")
+        from voidweb_b200.shard import shard_range
+        s0, s1 = shard_range(B, world, rank)
+        seq_lens = ctx_lengths(w, 0)[s0:s1]
+        B = s1 - s0
+    else:
+        seq_lens = ctx_lengths(w, rank)              # each rank: its own shard of sequences
     pages = (seq_lens + 15) // 16
     NB = int(pages.sum()) + 64
     rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919 + rank))
@@ -712,10 +724,10 @@ def main():
         line = {
             "metric": "paged decode KV GB/s", "value": round(value, 3), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": w["kv"], "data": "synthetic",
             "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv,
-                       "head_dim": D, "seqs_per_gpu": B, "ctx": list(w["ctx"]),
+                       "head_dim": D, "seqs_per_gpu": B, "seqs_total": int(total_seqs), "ctx": list(w["ctx"]),
                        "block_size": 16, "kv_dtype": w["kv"],
                        "parallelism": f"sequence-shard x{world}" if world > 1 else "single",
                        "l2": f"inputs larger than L2 ({bytes_launch * L / 1e9:.2f} GB of KV "
