@@ -669,8 +669,12 @@ static int32_t enqueue_step_host(vw_pool* pool, const vw_step_host_args* a, cuda
     cudaEventRecord(pool->ev_entry, cs);
     cudaStreamWaitEvent(pool->s_h2d, pool->ev_entry, 0);
     cudaStreamWaitEvent(pool->s_d2h, pool->ev_entry, 0);
-    cudaMemcpyAsync(d_bt, a->block_tables, btb, cudaMemcpyHostToDevice, pool->s_h2d);
-    cudaMemcpyAsync(d_sl, a->seq_lens, slb, cudaMemcpyHostToDevice, pool->s_h2d);
+    // the tables go up on the read-back stream (idle until the first layer
+    // ends), beside the first layer's rows on the upload stream
+    cudaMemcpyAsync(d_bt, a->block_tables, btb, cudaMemcpyHostToDevice, pool->s_d2h);
+    cudaMemcpyAsync(d_sl, a->seq_lens, slb, cudaMemcpyHostToDevice, pool->s_d2h);
+    cudaEventRecord(pool->ev_exit, pool->s_d2h);
+    cudaStreamWaitEvent(cs, pool->ev_exit, 0);
     for (size_t c = 0; c + 1 < cut.size(); ++c) {
         const uint32_t l0 = cut[c], nl = cut[c + 1] - cut[c];
         cudaMemcpyAsync(d_q + l0 * qb, hq + l0 * qb, nl * qb, cudaMemcpyHostToDevice, pool->s_h2d);
