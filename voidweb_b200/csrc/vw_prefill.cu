@@ -301,16 +301,17 @@ __device__ __forceinline__ void fp8_store_round(uint8_t* kt, uint8_t* vt, float*
 //  * warps 5 and 6 (producers): per round of R page-heads, warp 5 loads one TMA
 //    box per 128-B column of each page-head's 16 K rows into the round's K
 //    tile, warp 6 its 16 V rows into the V tile, so that the keys of the round
-//    are R*16 rows with a uniform stride in both tiles.  A stage's K tile and
-//    V tile have their own barriers: the K tile is refilled as soon as S of
-//    its round completes, two rounds before the V tile frees.
+//    are R*16 rows with a uniform stride in both tiles.  K tiles and V tiles
+//    are separate rings with their own barriers: a K tile is refilled as soon
+//    as S of its round completes, rounds before the V tile of that round frees.
 //  * warp 4: allocates tensor memory; one lane issues per round t
 //    S_t = Q K_t^T (D/16 MMAs, M = 128, N = R*16 keys, K = 16; both operands
 //    128-B-swizzled K-major shared-memory tiles) into S buffer t%2, then
 //    O += P_{t-1} V_{t-1} (per page-head: M = 128, N = D, K = 16 keys; A = P
 //    from tensor memory, B = the V tile rows as an MN-major operand).  S_t is
 //    issued only after P_{t-2}'s MMAs completed, since P_{t-2} occupies the
-//    buffer.  Commits release the round stage, the buffer and the epilogue.
+//    buffer.  Commits release the round's K tile (after S), its V tile and
+//    the P buffer (after P V), and last the epilogue.
 //  * warps 0-3 (thread r = query row r = tensor-memory lane r): load and
 //    (RoPE-)rotate the query rows into the swizzled K-major tile; per round read
 //    S, mask, run the online softmax with a lazily raised maximum (O in tensor
@@ -626,7 +627,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[bb], (t >> 1) & 1, deadline))) { ok = false; break; }
             const int st_i = t % T::NST;
             // FP8: the decoders' scales of the round (their writes precede the
-            // stage's full barrier, which has completed before S_t)
+            // K tile's full barrier; FP8 rings have NSTK == NSTV == NST)
             if (T::FP8 && !__all_sync(0xffffffffu, mbar_wait(&full_k[st_i], (t / T::NST) & 1, deadline))) {
                 ok = false;
                 break;
