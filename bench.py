@@ -81,7 +81,10 @@ def algorithmic_bytes_per_launch(w, seq_lens):
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch of the
 # default workload, from one ncu --set full capture of that launch; ncu cannot
 # run inside the timed bench, so the figure is carried here.
-NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 70_964_480}
+NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 70_964_480,
+                          # one prefill_kernel launch (one layer), read + write
+                          "qwen2.5-7b-prefill-4x2048": 111_355_904,
+                          "llama3-8b-fp8-prefill-4x2048": 123_923_456}
 
 
 def tensor_peak():
@@ -204,7 +207,8 @@ def run_prefill_bench(args, w):
                    "l2": f"inputs larger than L2 ({NB * Hkv * 2 * 16 * (D * (1 if fp8 else 2) + (4 if fp8 else 0)) * L / 1e9:.2f} GB of pages)"},
         "tok_per_s": round(T / (ms * 1e-3), 1),
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": sustained,
-                     "unit": "TFLOP/s", "frac": round(tflops / sustained, 4), "traffic": None,
+                     "unit": "TFLOP/s", "frac": round(tflops / sustained, 4),
+                     "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
                      "peak_kind": f"{kind} sustained (burst {burst})",
                      "flops_per_step": flops},
         "cpu_baseline": cpu, "e2e": None, "clocks": clk, "gpu_launches": args.steps * L * 2,
