@@ -81,7 +81,7 @@ def algorithmic_bytes_per_launch(w, seq_lens):
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch of the
 # default workload, from one ncu --set full capture of that launch; ncu cannot
 # run inside the timed bench, so the figure is carried here.
-NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 70_964_480,
+NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 71_157_760,
                           # one prefill_kernel launch (one layer), read + write
                           "qwen2.5-7b-prefill-4x2048": 111_355_904,
                           "llama3-8b-fp8-prefill-4x2048": 123_923_456}
