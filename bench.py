@@ -66,7 +66,9 @@ def ctx_lengths(w, rank=0):
 
 
 def algorithmic_bytes_per_launch(w, seq_lens):
-    """Bytes one layer's append + decode must move (SURVEY-defined formula):
+    """Bytes one layer's append + decode must move, counting each page once per
+    KV head (a GQA group shares it), as the paging walk of
+    kernels/attention/flash_attention.bm:132-140 generalised to KV heads reads them:
     KV read ctx*2*Hkv*(D*e+s), append write 2*Hkv*(D*e+s) + new rows read
     2*Hkv*D*2, q read and o write Hq*D*2 each, block table ceil(ctx/16)*4*Hkv."""
     e = 1 if w["kv"] == "fp8" else 2

@@ -407,6 +407,39 @@ VW_API int32_t vw_sched_stats(const vw_sched* s, vw_sched_stat* st);
 /* Message for the last failure on this thread ("" if none). */
 VW_API const char* vw_last_error(void);
 
+/* ---- Failure injection for tests of a caller's error handling ----------------
+ * The engine turns any nonzero status of voidweb_forward_pass into a failed
+ * step (engine/ffi.bm:112-118) and an exhausted block pool into an allocation
+ * error (engine/kv_cache.bm:82-85).  vw_fault_inject arms `count` failures of
+ * one kind (count 0 disarms); each later call of an entry point that can fail
+ * that way consumes one and returns the status at once, before touching the
+ * device or the bookkeeping:
+ *   VW_FAULT_OOM         -> VW_ERR_OOM: vw_pool_create, vw_decode_step_host,
+ *                           voidweb_forward_pass, vw_bm_alloc, vw_bm_alloc_seq, vw_bm_cow
+ *   VW_FAULT_INVALID_ARG -> VW_ERR_INVALID_ARG and
+ *   VW_FAULT_CUDA        -> VW_ERR_CUDA: vw_pool_create, vw_kv_append,
+ *                           vw_paged_decode, vw_paged_decode_static, vw_decode_plan,
+ *                           vw_block_copy, vw_kv_gather, vw_paged_prefill,
+ *                           vw_decode_step_host, voidweb_forward_pass,
+ *                           vw_rms_norm_fp8_out, vw_gemm_fp8
+ * The environment variable VOIDWEB_KV_FAULT ("oom:N,invalid:N,cuda:N") arms
+ * the same counts when the library is loaded.  No counterpart in the reference. */
+#define VW_FAULT_OOM 1u
+#define VW_FAULT_INVALID_ARG 2u
+#define VW_FAULT_CUDA 3u
+VW_API int32_t vw_fault_inject(uint32_t kind, uint32_t count);
+/* Failures of `kind` still armed. */
+VW_API uint32_t vw_fault_pending(uint32_t kind);
+
+/* Test hook for the bounded device waits: the decode launches of this pool
+ * give up every wait for a copy or a consumer after `cycles` SM clock cycles
+ * from the kernel's start (0 restores the default, about 2 s).  A launch whose
+ * wait gives up records VW_DEV_ERR_TIMEOUT, waits (under the default limit)
+ * for the copies it has in flight, and returns; its outputs are undefined.
+ * vw_pool_check clears the word, after which the pool decodes normally.  No
+ * counterpart in the reference. */
+VW_API int32_t vw_debug_set_wait_limit(vw_pool* pool, uint64_t cycles);
+
 /* ---- The symbol the engine dlopens (engine/ffi.bm:15-40, :68, :113) ---- */
 #pragma pack(push, 1)
 typedef struct {

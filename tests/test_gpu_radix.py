@@ -1,5 +1,6 @@
-"""Shared-prefix workload on the GPU (COW copy, LRU eviction and
-compaction moves around a decode): the device pool must equal the oracle's
+"""Shared-prefix workload on the GPU (the copy-on-write decision of
+engine/kv_cache.bm:94-113, the LRU eviction of radix_cache/radix_cache.bm:231-285
+and compaction moves around a decode): the device pool must equal the oracle's
 mirror bit for bit after every phase, and the decode outputs must stay within
 |gpu - ref| <= 2e-3 + 1e-2 * |ref| of the fp64 oracle over the mirror."""
 import numpy as np

@@ -30,6 +30,7 @@ VW_F16, VW_BF16, VW_FP8_E4M3 = 0, 1, 2
 VW_FP8_REFERENCE, VW_FP8_OCP = 0, 1
 VW_DECODE_PDL, VW_DECODE_EARLY_PAGES, VW_DECODE_PLANNED, VW_DECODE_ROPE = 0x1, 0x2, 0x4, 0x8
 VW_PREFILL_CAUSAL, VW_PREFILL_ROPE, VW_PREFILL_PDL = 0x1, 0x2, 0x4
+VW_FAULT_OOM, VW_FAULT_INVALID_ARG, VW_FAULT_CUDA = 1, 2, 3
 
 DEV_ERR_BLOCK_ID, DEV_ERR_SEQ_LEN, DEV_ERR_TIMEOUT, DEV_ERR_SLOT = 1, 2, 4, 8
 
@@ -158,6 +159,9 @@ SIGNATURES = {
     "vw_forward_set_seq_len": (i32, [u64, u32]),
     "vw_forward_release": (i32, [u64]),
     "voidweb_forward_pass": (i32, [ctypes.POINTER(ForwardArgs)]),
+    "vw_fault_inject": (i32, [u32, u32]),
+    "vw_fault_pending": (u32, [u32]),
+    "vw_debug_set_wait_limit": (i32, [vp, u64]),
 }
 
 

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/voidweb_kv.h"
+#include "vw_fault.h"
 #include "vw_internal.h"
 
 using namespace vw;
@@ -43,6 +44,17 @@ int32_t cuda_fail(cudaError_t e, const char* what) {
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// An armed injected failure (vw_fault_inject) of one of `kinds` ends the call
+// here, before anything else happens.
+#define VW_FAULT_POINT(kinds, name)                                                   \
+    do {                                                                              \
+        const char* what_ = "";                                                       \
+        const int32_t rc_ = vw::fault_take((kinds), &what_);                          \
+        if (rc_ != VW_OK) return fail(rc_, "%s: injected fault (%s)", (name), what_); \
+    } while (0)
+constexpr uint32_t kFaultAll = vw::kCanOom | vw::kCanInvalid | vw::kCanCuda;
+constexpr uint32_t kFaultLaunch = vw::kCanInvalid | vw::kCanCuda;
 
 // RAII-free device scope switch: the library never leaves the caller's
 // current device changed.
@@ -109,6 +121,7 @@ struct vw_pool {
     // overlapping launches (programmatic dependent launch) never share one
     size_t scratch_o = 0, scratch_ml = 0;
     uint64_t launches = 0;
+    uint64_t wait_cycles = 0;           // vw_debug_set_wait_limit (0: the default bound)
     // decode plan (vw_decode_plan) and the batch it was made for
     int* plan = nullptr;
     bool plan_ready = false;
@@ -192,6 +205,7 @@ extern "C" {
 const char* vw_last_error(void) { return g_last_error.c_str(); }
 
 int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
+    VW_FAULT_POINT(kFaultAll, "vw_pool_create");
     if (!cfg || !out) return fail(VW_ERR_INVALID_ARG, "vw_pool_create: null argument");
     *out = nullptr;
     const vw_pool_config& c = *cfg;
@@ -302,6 +316,12 @@ int32_t vw_pool_info(const vw_pool* pool, void** kv_data, void** kv_scales, uint
     return VW_OK;
 }
 
+int32_t vw_debug_set_wait_limit(vw_pool* pool, uint64_t cycles) {
+    if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_debug_set_wait_limit: null pool");
+    pool->wait_cycles = cycles;
+    return VW_OK;
+}
+
 int32_t vw_pool_check(vw_pool* pool, uint32_t* device_error) {
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_pool_check: null pool");
     DeviceScope ds(pool->cfg.device);
@@ -318,6 +338,7 @@ int32_t vw_pool_check(vw_pool* pool, uint32_t* device_error) {
 
 int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const void* v_new,
                      const int64_t* slot_mapping, uint32_t num_tokens, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_kv_append");
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_kv_append: null pool");
     if (layer >= pool->geom.num_layers)
         return fail(VW_ERR_INVALID_ARG, "vw_kv_append: layer %u >= %u", layer, pool->geom.num_layers);
@@ -375,7 +396,14 @@ static int32_t decode_validate(const vw_pool* pool, const vw_decode_args* a) {
     return VW_OK;
 }
 
-static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_t s) {
+// Split-K scratch given to a decode launch in place of the pool's own.
+struct DecodeScratch {
+    float* o;
+    float* ml;
+};
+
+static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_t s,
+                             const DecodeScratch* fixed = nullptr) {
     const PoolGeom& g = pool->geom;
     DecodeLaunch L{};
     DecodeParams& p = L.p;
@@ -387,9 +415,14 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
     p.seq_lens = a->seq_lens;
     p.kv_data = pool->data;
     p.kv_scales = pool->scales;
-    const uint64_t set = pool->launches++ & 1;
-    p.part_o = pool->part_o + set * pool->scratch_o;
-    p.part_ml = pool->part_ml + set * pool->scratch_ml;
+    if (fixed) {
+        p.part_o = fixed->o;
+        p.part_ml = fixed->ml;
+    } else {
+        const uint64_t set = pool->launches++ & 1;
+        p.part_o = pool->part_o + set * pool->scratch_o;
+        p.part_ml = pool->part_ml + set * pool->scratch_ml;
+    }
     p.flags = a->flags;
     p.plan = (a->flags & VW_DECODE_PLANNED) ? pool->plan : nullptr;
     p.err = pool->err;
@@ -405,6 +438,7 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.rope_theta = (a->flags & VW_DECODE_ROPE) ? a->rope_theta : 0.0f;
+    p.wait_cycles = pool->wait_cycles;
     L.tmap = &pool->tmap;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;
@@ -416,6 +450,7 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
 }
 
 int32_t vw_paged_decode(vw_pool* pool, const vw_decode_args* args, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_paged_decode");
     int32_t rc = decode_validate(pool, args);
     if (rc != VW_OK) return rc;
     if (args->num_seqs == 0) return VW_OK;
@@ -461,6 +496,7 @@ static int32_t prefill_validate(const vw_pool* pool, const vw_prefill_args* a) {
 }
 
 int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_paged_prefill");
     int32_t rc = prefill_validate(pool, a);
     if (rc != VW_OK) return rc;
     if (a->num_seqs == 0 || a->num_tokens == 0) return VW_OK;
@@ -517,6 +553,7 @@ int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) 
 
 int32_t vw_rms_norm_fp8_out(const void* x, const void* weight, uint8_t* out, uint32_t rows, uint32_t hidden,
                             float scale, float eps, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_rms_norm_fp8_out");
     if (!x || !weight || !out) return fail(VW_ERR_INVALID_ARG, "vw_rms_norm_fp8_out: null pointer");
     if (hidden == 0) return fail(VW_ERR_INVALID_ARG, "vw_rms_norm_fp8_out: hidden must be > 0");
     if (!aligned(x, 2) || !aligned(weight, 2))
@@ -529,6 +566,7 @@ int32_t vw_rms_norm_fp8_out(const void* x, const void* weight, uint8_t* out, uin
 
 int32_t vw_gemm_fp8(const uint8_t* a, const uint8_t* b, void* c, const void* bias, uint32_t M, uint32_t N,
                     uint32_t K, float a_scale, float b_scale, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_gemm_fp8");
     if (!a || !b || !c) return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: null pointer");
     if (M == 0 || N == 0 || K == 0) return fail(VW_ERR_INVALID_ARG, "vw_gemm_fp8: empty shape");
     if (N % 16 || K % 16) return fail(VW_ERR_UNSUPPORTED, "vw_gemm_fp8: N and K must be multiples of 16");
@@ -553,6 +591,7 @@ int32_t vw_fp8_weight_check(uint32_t* device_error) {
 int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32_t* seq_lens,
                        uint32_t num_seqs, uint32_t block_table_stride, uint32_t num_q_heads,
                        void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_decode_plan");
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_decode_plan: null pool");
     const PoolGeom& g = pool->geom;
     if (num_seqs == 0 || num_seqs > pool->cfg.max_batch)
@@ -588,6 +627,7 @@ int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32
 }
 
 int32_t vw_block_copy(vw_pool* pool, const uint32_t* pairs, uint32_t num_pairs, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_block_copy");
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_block_copy: null pool");
     if (num_pairs == 0) return VW_OK;
     if (!pairs || !aligned(pairs, 8)) return fail(VW_ERR_INVALID_ARG, "vw_block_copy: bad pairs");
@@ -600,6 +640,7 @@ int32_t vw_block_copy(vw_pool* pool, const uint32_t* pairs, uint32_t num_pairs, 
 int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block_table, uint32_t seq_len,
                      void* out_k, void* out_v, float* out_k_scales, float* out_v_scales,
                      void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_kv_gather");
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: null pool");
     if (layer >= pool->geom.num_layers) return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: bad layer");
     if (seq_len == 0) return VW_OK;
@@ -728,6 +769,7 @@ static int32_t enqueue_step_host(vw_pool* pool, const vw_step_host_args* a, cuda
 }
 
 int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* stream) {
+    VW_FAULT_POINT(kFaultAll, "vw_decode_step_host");
     if (!pool || !a) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: null argument");
     if (a->reserved) return fail(VW_ERR_INVALID_ARG, "vw_decode_step_host: reserved");
     if (a->rope_theta != 0.0f && !(a->rope_theta > 1.0f && std::isfinite(a->rope_theta)))
@@ -912,6 +954,7 @@ static int32_t forward_prefill(vw_pool* pool, uint32_t L, uint32_t Hq, uint32_t 
 }
 
 int32_t voidweb_forward_pass(const ForwardArgs* args) {
+    VW_FAULT_POINT(kFaultAll, "voidweb_forward_pass");
     if (!args) return fail(VW_ERR_INVALID_ARG, "voidweb_forward_pass: null args");
     ForwardState& s = fwd();
     std::lock_guard<std::mutex> lk(s.mu);
@@ -1102,6 +1145,7 @@ int32_t static_scratch(int dev, StaticScratch* out) {
 extern "C" {
 
 int32_t vw_paged_decode_static(vw_pool* pool, const vw_decode_args* a, void* stream) {
+    VW_FAULT_POINT(kFaultLaunch, "vw_paged_decode_static");
     int32_t rc = decode_validate(pool, a);
     if (rc != VW_OK) return rc;
     const PoolGeom& g = pool->geom;
@@ -1120,39 +1164,10 @@ int32_t vw_paged_decode_static(vw_pool* pool, const vw_decode_args* a, void* str
     StaticScratch sc;
     rc = static_scratch(pool->cfg.device, &sc);
     if (rc != VW_OK) return rc;
-    DecodeLaunch L{};
-    DecodeParams& p = L.p;
-    p.q = a->q;
-    p.out = a->out;
-    p.k_new = a->k_new;
-    p.v_new = a->v_new;
-    p.block_tables = a->block_tables;
-    p.seq_lens = a->seq_lens;
-    p.kv_data = pool->data;
-    p.kv_scales = pool->scales;
-    p.part_o = sc.o;
-    p.part_ml = sc.ml;
-    p.flags = a->flags;
-    p.err = pool->err;
-    p.B = a->num_seqs;
-    p.Hq = a->num_q_heads;
-    p.Hkv = g.num_kv_heads;
-    p.group = a->num_q_heads / g.num_kv_heads;
-    p.num_blocks = g.num_blocks;
-    p.layer = a->layer;
-    p.bt_stride = a->block_table_stride;
-    p.fp8_ocp = g.fp8_ocp;
-    const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
-    p.scale_log2 = scale * 1.4426950408889634f;
-    p.rope_theta = (a->flags & VW_DECODE_ROPE) ? a->rope_theta : 0.0f;
-    L.tmap = &pool->tmap;
-    L.head_dim = g.head_dim;
-    L.kv_kind = g.kv_kind;
-    L.io_kind = g.io_kind;
-    L.grid = pool->grid;
-    L.stream = static_cast<cudaStream_t>(stream);
-    cudaError_t e = launch_paged_decode(L);
-    return e == cudaSuccess ? VW_OK : cuda_fail(e, "vw_paged_decode_static launch");
+    // the same launch as vw_paged_decode (flags, plan, wait bound) with the
+    // static array in place of the pool's scratch
+    const DecodeScratch fixed{sc.o, sc.ml};
+    return decode_launch(pool, a, static_cast<cudaStream_t>(stream), &fixed);
 }
 
 }  // extern "C"

@@ -390,6 +390,7 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     const uint8_t* kbase = reinterpret_cast<const uint8_t*>(p.k_new);
     const uint8_t* vbase = reinterpret_cast<const uint8_t*>(p.v_new);
     int segs_issued = 0;                             // highest segment ordinal issued + 1
+    int issued_hi = -1;                              // last page this lane issued
     bool ok = true;
 
     auto publish = [&](const Resolved& r, int buf) {
@@ -436,6 +437,7 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
             tma_load_2d(st, tmap, &sm.full[s], 0, pi.row0);
         else
             tma_load_3d(st, tmap, &sm.full[s], 0, pi.row0, 0);
+        issued_hi = ii;
         return true;
     };
 
@@ -514,22 +516,27 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
         __syncwarp();
     }
     if (!ok) set_err(p.err, kDevErrTimeout);
-    // Drain: never leave the CTA while a TMA or bulk load may still write its smem.
-    // (each warp waits for the pages its own lanes issued; the query lane for the
-    // query tiles)
-    if (lane == 0) {
-        for (int ii = n > T::S ? n - T::S : 0; ii < n; ++ii) {
-            if ((ii % T::NI) % T::PW != pw) continue;
-            if (!mbar_wait(&sm.full[ii % T::S], (ii / T::S) & 1, deadline)) {
+    // Drain: never leave the CTA while a TMA or bulk load may still write its
+    // shared memory.  A lane issues the pages of its own stages in page order
+    // and stops at its first failed wait, so its copies still in flight are at
+    // most the last S / NI pages it issued (an older page's stage has been
+    // refilled, so that page was consumed); the query lane likewise waits for
+    // its last kQSlots query tiles.  The drain has a deadline of its own: after
+    // a timeout the kernel's deadline has passed, and giving up at once would
+    // leave copies writing into a CTA that has exited.
+    const uint64_t drain_deadline = cycles() + kWaitDeadlineCycles;
+    if (lane < T::IPW) {
+        for (int ii = issued_hi; ii >= 0 && ii > issued_hi - T::S; ii -= T::NI) {
+            if (!mbar_wait(&sm.full[ii % T::S], (ii / T::S) & 1, drain_deadline)) {
                 set_err(p.err, kDevErrTimeout);
                 break;
             }
         }
-        for (int k = segs_issued > kQSlots ? segs_issued - kQSlots : 0; qlane && k < segs_issued; ++k) {
-            if (!mbar_wait(&sm.qfull[k % kQSlots], (k / kQSlots) & 1, deadline)) {
-                set_err(p.err, kDevErrTimeout);
-                break;
-            }
+    }
+    for (int k = segs_issued > kQSlots ? segs_issued - kQSlots : 0; qlane && k < segs_issued; ++k) {
+        if (!mbar_wait(&sm.qfull[k % kQSlots], (k / kQSlots) & 1, drain_deadline)) {
+            set_err(p.err, kDevErrTimeout);
+            break;
         }
     }
 }
@@ -1101,7 +1108,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Smem sm = carve<T>(base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t deadline = cycles() + kWaitDeadlineCycles;
+    const uint64_t deadline = cycles() + (p.wait_cycles ? p.wait_cycles : kWaitDeadlineCycles);
     if (threadIdx.x == 0) VW_TRACE(0, globaltimer());
 #ifdef VW_DECODE_TRACE
     if (threadIdx.x == 0) {

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "../../include/voidweb_kv.h"
+#include "vw_fault.h"
 
 struct vw_block_manager {
     uint32_t block_size = 16, max_blocks = 0, used = 0;
@@ -70,20 +71,33 @@ uint32_t vw_bm_capacity(const vw_block_manager* bm) {
 
 uint32_t vw_bm_free_count(const vw_block_manager* bm) { return (uint32_t)bm->free_blocks.size(); }
 
-int32_t vw_bm_alloc(vw_block_manager* bm, uint32_t* out) {
-    if (bm->free_blocks.empty()) return VW_ERR_OOM;
+}  // extern "C"
+
+namespace {
+// kv_cache.bm:69-78 (the caller checked that a block is free)
+uint32_t bm_pop(vw_block_manager* bm) {
     const uint32_t id = bm->free_blocks.back();
     bm->free_blocks.pop_back();
     bm->ref[id] = 1;
     bm->token_hash[id] = 0;
     bm->used += 1;
-    *out = id;
+    return id;
+}
+}  // namespace
+
+extern "C" {
+
+int32_t vw_bm_alloc(vw_block_manager* bm, uint32_t* out) {
+    if (vw::fault_take(vw::kCanOom, nullptr) != VW_OK) return VW_ERR_OOM;   // vw_fault_inject
+    if (bm->free_blocks.empty()) return VW_ERR_OOM;
+    *out = bm_pop(bm);
     return VW_OK;
 }
 
 int32_t vw_bm_alloc_seq(vw_block_manager* bm, uint32_t n, uint32_t* out) {
+    if (vw::fault_take(vw::kCanOom, nullptr) != VW_OK) return VW_ERR_OOM;   // vw_fault_inject
     if (bm->free_blocks.size() < n) return VW_ERR_OOM;               // kv_cache.bm:82-85
-    for (uint32_t i = 0; i < n; ++i) vw_bm_alloc(bm, out + i);
+    for (uint32_t i = 0; i < n; ++i) out[i] = bm_pop(bm);
     return VW_OK;
 }
 

@@ -31,6 +31,7 @@ struct DecodeParams {
     float scale_log2;           // softmax scale * log2(e)
     float rope_theta;           // > 0: rotate q and the new K row (RoPE) at position seq_len-1
     uint32_t flags;             // kDecodePdl | kDecodeEarlyPages | kDecodePlanned
+    uint64_t wait_cycles;       // bound of the device waits in SM cycles (0: kWaitDeadlineCycles)
 };
 
 constexpr uint32_t kDecodePdl = 0x1u;

@@ -116,6 +116,11 @@ class KvPool:
             C.check(rc)
         return int(w.value)
 
+    def set_wait_limit(self, cycles: int) -> None:
+        """Test hook: bound this pool's decode waits to `cycles` SM cycles (0:
+        the default, about 2 s); see vw_debug_set_wait_limit."""
+        C.check(C.lib().vw_debug_set_wait_limit(self._h, cycles))
+
     # -- operations -------------------------------------------------------------
     def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor,
                slot_mapping: torch.Tensor, stream=None) -> None:
