@@ -58,11 +58,56 @@ L2_BYTES = 126 * 1024 * 1024
 
 
 def ctx_lengths(w, rank=0):
-    rng = np.random.Generator(np.random.PCG64(w["seed"] * 1000 + rank))
+    """Context lengths of one GPU's batch before the step's token: rank 0 draws
+    them from numpy PCG64(seed) (the workload's seed), other ranks of a
+    sequence-sharded run from PCG64(seed * 1000 + rank)."""
+    rng = np.random.Generator(np.random.PCG64(w["seed"] if rank == 0 else w["seed"] * 1000 + rank))
     kind, lo, hi = w["ctx"]
     if kind == "uniform":
         return rng.integers(lo, hi + 1, w["B"]).astype(np.int64)
     return np.rint(np.exp(rng.uniform(math.log(lo), math.log(hi), w["B"]))).astype(np.int64)
+
+
+def verify_layer(pool, w, layer, q, kn, vn, out, bt, seq_lens, threads=0):
+    """One layer of the benchmarked step against the oracle, outside the timed
+    region: the pages of that layer after the step (appends are idempotent, so
+    the oracle's append of the step's rows must leave them unchanged: the
+    fused append was bit-exact, codes and scales included) and the step's
+    attention outputs against the oracle's fp64 paged decode over those pages
+    (|gpu - ref| <= 2e-3 + 1e-2 * |ref|)."""
+    import torch
+    import oracle
+    kvk = {"f16": oracle.F16, "bf16": oracle.BF16, "fp8": oracle.FP8}
+    fp8 = w["kv"] == "fp8"
+    NB, Hkv, D, Hq = pool.spec.num_blocks, w["Hkv"], w["D"], w["Hq"]
+    g = oracle.geom(1, Hkv, D, NB, kvk[w["kv"]], kvk[w["io"]])
+    shape = oracle.pool_shape(g)
+    n = int(np.prod(shape))
+    eb = 1 if fp8 else 2
+    raw = pool.pages_u8()[layer * n * eb:(layer + 1) * n * eb].cpu().numpy()
+    data = raw.view(np.uint8 if fp8 else np.uint16).reshape(shape)
+    scales = None
+    if fp8:
+        ns = n // D
+        scales = pool.scales_f32()[layer * ns:(layer + 1) * ns].cpu().numpy().reshape(shape[:-1])
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    sl = np.asarray(seq_lens, dtype=np.int64)
+    btn = np.asarray(bt, dtype=np.uint32)
+    slots = np.array([int(btn[b, (sl[b] - 1) // 16]) * 16 + int((sl[b] - 1) % 16) for b in range(len(sl))],
+                     dtype=np.int64)
+    want = data.copy()
+    wscales = scales.copy() if fp8 else None
+    oracle.kv_append(g, want, wscales, 0, bits(kn), bits(vn), slots)
+    append_ok = bool(np.array_equal(want, data)) and (
+        not fp8 or bool(np.array_equal(wscales.view(np.uint32), scales.view(np.uint32))))
+    ref = oracle.paged_decode_f64(g, data, scales, 0, bits(q), Hq, btn, sl.astype(np.uint32),
+                                  1.0 / math.sqrt(D), nthreads=threads)
+    got = oracle.io_bits_to_f32(bits(out), kvk[w["io"]]).astype(np.float64)
+    err = np.abs(got - ref)
+    ratio = float((err / (2e-3 + 1e-2 * np.abs(ref))).max())
+    return {"layer": layer, "append_bit_exact": append_ok, "max_abs_err": float(err.max()),
+            "worst_tolerance_ratio": round(ratio, 4), "ok": append_ok and ratio <= 1.0 and
+            bool(np.isfinite(got).all())}
 
 
 def algorithmic_bytes_per_launch(w, seq_lens):
@@ -340,6 +385,17 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
 def cpu_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -414,7 +470,7 @@ def run_reference(args, w):
     if rank != 0:
         return 0
     threads = cpu_threads()
-    seq_lens = ctx_lengths(w, 0)
+    seq_lens = ctx_lengths(w, 0) + 1         # the step's token at position ctx
     cs = CpuSample(w, seq_lens, threads)
     allseq = np.arange(w["B"])
     t0 = time.perf_counter()
@@ -449,7 +505,7 @@ def run_reference(args, w):
                    "ctx": list(w["ctx"]), "block_size": 16, "parallelism": "cpu"},
         "tok_per_s": round(tok_s, 3),
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": sample, "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -467,6 +523,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: every GPU brings the workload's batch; strong: one batch split across the GPUs")
+    ap.add_argument("--placement", default="sequences", choices=["sequences", "kv_heads"],
+                    help="N GPUs: sequences = each GPU its own sequences (every KV head); kv_heads = "
+                         "every GPU the same sequences and block tables with its own KV heads "
+                         "(the workload's kv_heads per GPU: Llama-3-70B one KV head per GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="run only this many layers of the workload (a small case for ncu "
@@ -509,25 +569,36 @@ def main():
         # the per-step output all-gather overlaps the next step's decode: two
         # NCCL channels move 3 MB per rank in time and leave the SMs to the decode
         os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
+        # the communicator's set-up lines (ranks, NVLink/NVLS paths) go to stderr
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
     from voidweb_b200.kv import KvPool, PoolSpec
 
     L, Hq, Hkv, D, B = w["L"], w["Hq"], w["Hkv"], w["D"], w["B"]
+    heads_split = args.placement == "kv_heads"
+    if heads_split and args.scaling == "strong":
+        raise SystemExit("--placement kv_heads is a weak-scaling placement (one KV head per GPU)")
     if args.scaling == "strong":
         # one fixed batch (the 1-GPU workload's seeded contexts) split across the ranks
         if B % world:
             raise SystemExit(f"--scaling strong needs the batch ({B}) divisible by the GPUs ({world})")
         from voidweb_b200.shard import shard_range
         s0, s1 = shard_range(B, world, rank)
-        seq_lens = ctx_lengths(w, 0)[s0:s1]
+        ctx = ctx_lengths(w, 0)[s0:s1]
         B = s1 - s0
+    elif heads_split:
+        ctx = ctx_lengths(w, 0)                      # every rank: the same sequences
     else:
-        seq_lens = ctx_lengths(w, rank)              # each rank: its own shard of sequences
+        ctx = ctx_lengths(w, rank)                   # each rank: its own shard of sequences
+    # the step appends the token at position ctx and decodes over ctx + 1 tokens
+    seq_lens = ctx + 1
     pages = (seq_lens + 15) // 16
     NB = int(pages.sum()) + 64
-    rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919 + rank))
+    # kv_heads: the same block ids on every rank (the bookkeeping is replicated)
+    rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919 + (0 if heads_split else rank)))
     perm = rng.permutation(NB)
     stride = int(pages.max())
     bt = np.zeros((B, stride), dtype=np.int32)
@@ -622,6 +693,12 @@ def main():
             run_step()
         join_gathers()
     stream.synchronize()
+    # one layer of the step (the middle one) against the oracle, untimed
+    vl = L // 2
+    verified = verify_layer(pool, w, vl, q[vl], kn[vl], vn[vl], outs[(args.warmup - 1) % 2][vl], bt,
+                            seq_lens, threads=max(1, cpu_threads() // max(world, 1)))
+    if not verified["ok"]:
+        raise SystemExit(f"rank {rank}: the benchmarked step differs from the oracle: {verified}")
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -653,7 +730,8 @@ def main():
         total_launch_bytes = float(t.item())
         tb = torch.tensor([float(B)], device=dev, dtype=torch.float64)
         dist.all_reduce(tb, op=dist.ReduceOp.SUM)
-        total_seqs = float(tb.item())
+        # kv_heads: the ranks advance the same sequences (each its own heads)
+        total_seqs = float(B) if heads_split else float(tb.item())
     else:
         total_launch_bytes, total_seqs = float(bytes_launch), float(B)
     step_bytes_all = total_launch_bytes * L
@@ -709,6 +787,45 @@ def main():
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(ho.numel() * 2),
                "path": "vw_decode_step_host (pinned host buffers; from the second call with "
                        "the same buffers the step replays as one recorded CUDA graph)"}
+        # the same step through the symbol the engine dlopens: voidweb_forward_pass
+        # with the packed descriptors KernelLib.forward_pass builds (engine/ffi.bm:86-121);
+        # the bound q / new K / new V / output buffers are the pinned ones above
+        from voidweb_b200 import KernelLib
+        Lb = C.lib()
+        kl = KernelLib.open(C.LIB_PATH)
+        Lb.vw_forward_bind(pool.handle, hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr())
+        seqs = [(1000 + b, 7, bt[b, :pages[b]].astype(np.uint32)) for b in range(B)]
+        cfg = dict(num_heads=Hq, num_kv_heads=Hkv, num_layers=L, head_dim=D, rope_theta=0.0)
+
+        def fwd_step():
+            for b in range(B):         # every step decodes the same position (fixed workload)
+                Lb.vw_forward_set_seq_len(1000 + b, int(ctx[b]))
+            kl.forward_pass(cfg, seqs)
+
+        for _ in range(3):
+            fwd_step()
+        if world > 1:
+            dist.barrier()
+        ds = torch.cuda.default_stream(dev)
+        e0.record(ds)
+        for _ in range(args.e2e_steps):
+            fwd_step()
+        e1.record(ds)
+        e1.synchronize()
+        fms = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            m = torch.tensor([fms], device=dev, dtype=torch.float64)
+            dist.all_reduce(m, op=dist.ReduceOp.MAX)
+            fms = float(m.item())
+        Lb.vw_forward_bind(None, None, None, None, None)
+        for b in range(B):
+            Lb.vw_forward_release(1000 + b)
+        e2e["forward_pass"] = {
+            "value": round(step_bytes_all / (fms * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "ms_per_step": round(fms, 4), "tok_per_s": round(total_seqs / (fms * 1e-3), 1),
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(ho.numel() * 2),
+            "path": "voidweb_forward_pass through KernelLib.forward_pass (packed SeqDescriptor / "
+                    "ForwardArgs, host block lists, pinned bound buffers)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -721,6 +838,7 @@ def main():
         del cs_probe
         gbs, ctok, dt, launches = cpu_decode_sample(w, seq_lens, n_launch, threads)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "cpu_model": cpu_model(),
                "tok_per_s": round(ctok, 2),
                "sample": f"{launches} layer launches (1 of {w['L']} layers, same {B} sequences), "
                          f"{dt:.1f} s; oracle f32 reference-order decode + append, OpenMP",
@@ -735,7 +853,9 @@ def main():
             "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv,
                        "head_dim": D, "seqs_per_gpu": B, "seqs_total": int(total_seqs), "ctx": list(w["ctx"]),
                        "block_size": 16, "kv_dtype": w["kv"],
-                       "parallelism": f"sequence-shard x{world}" if world > 1 else "single",
+                       "parallelism": (f"{'kv-head' if heads_split else 'sequence'}-shard x{world}"
+                                       if world > 1 else "single"),
+                       "placement": args.placement,
                        "l2": f"inputs larger than L2 ({bytes_launch * L / 1e9:.2f} GB of KV "
                              f"per step per GPU vs {L2_BYTES / 1e6:.0f} MB L2)",
                        "graph": "one CUDA graph per step: one fused append+decode launch per layer, "
@@ -754,6 +874,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,
+            "oracle_check": verified,
             # per layer: the fused append+decode grid and its split-K combine grid
             "gpu_launches": args.steps * L * 2,
         }

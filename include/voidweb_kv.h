@@ -440,6 +440,11 @@ VW_API uint32_t vw_fault_pending(uint32_t kind);
  * counterpart in the reference. */
 VW_API int32_t vw_debug_set_wait_limit(vw_pool* pool, uint64_t cycles);
 
+/* Number of device (cudaMalloc) and pinned host (cudaHostAlloc) allocations this
+ * library has made since it was loaded: a test can check that a call allocates
+ * nothing by reading it before and after.  No counterpart in the reference. */
+VW_API uint64_t vw_debug_alloc_count(void);
+
 /* ---- The symbol the engine dlopens (engine/ffi.bm:15-40, :68, :113) ---- */
 #pragma pack(push, 1)
 typedef struct {
@@ -471,7 +476,14 @@ typedef struct {
  * library, so the caller binds the pool and the per-layer q / new K / new V
  * rows and the attention output buffer that voidweb_forward_pass reads and
  * writes (host, [L][rows][heads][head_dim] in the io dtype, one row per token
- * of each descriptor, in descriptor order).  The binding is process-wide. */
+ * of each descriptor, in descriptor order).  The binding is process-wide.
+ * With pinned buffers (cudaHostAlloc / cudaHostRegister) the decode part of a
+ * forward pass is the fast path of vw_decode_step_host: the library keeps each
+ * step's block tables and lengths in pinned buffers of its own, reused from
+ * step to step, so from the second step of the same batch size and table
+ * stride every forward pass replays one recorded CUDA graph (uploads,
+ * append + decode of every layer, read-back).  Binding a NULL pool releases
+ * those buffers. */
 VW_API int32_t vw_forward_bind(vw_pool* pool, const void* q, const void* k_new, const void* v_new,
                         void* attn_out);
 /* Number of tokens already cached for seq_id (e.g. after a prefill done

@@ -109,8 +109,13 @@ def geom(L, Hkv, D, NB, kv_dtype, io_dtype, fp8_mode=FP8_REFERENCE) -> Geom:
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     """utils/simd.bm:153-158 round-to-nearest-even on the raw bits."""
-    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    # u32 arithmetic wrapping like the reference's (bits + 0x7FFF + round) >> 16
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = (b >> np.uint32(16)) & np.uint32(1)
+    r += b
+    r += np.uint32(0x7FFF)
+    r >>= np.uint32(16)
+    return r.astype(np.uint16)
 
 
 def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:

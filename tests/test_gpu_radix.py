@@ -21,11 +21,15 @@ def _close(got_bits, ref, what):
     assert np.isfinite(got).all() and not bad.any(), f"{what}: {bad.sum()} outside, max {err.max():.3g}"
 
 
-def test_shared_prefix_cow_evict_compact_decode():
+@pytest.mark.parametrize("layers", [2, 28])
+def test_shared_prefix_cow_evict_compact_decode(layers):
+    """Seed 2, Qwen2.5-7B KV shapes (4 KV heads, head_dim 128, bf16), 64 requests
+    sharing a 128-token prefix, suffixes U[32, 1024]; at 2 layers and at the
+    model's full 28 layers, every layer's decode compared."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from tests.radix_workload import DeviceSide, Workload
-    wl = Workload(seed=2)
+    wl = Workload(seed=2, L=layers)
     dev = DeviceSide(wl, torch)
     pairs = wl.build(dev)
     assert len(pairs) == wl.n_fork

@@ -216,3 +216,29 @@ def test_rope_matches_numpy_restatement(io):
     bound = np.concatenate([amp, amp], axis=-1) + rel * np.abs(want) + 1e-6
     assert (np.abs(g - want) <= bound).all()
     assert np.mean(got == want_bits) > 0.97
+
+
+def test_benchmark_config_inputs_follow_their_definition():
+    """The C1 and C2 configurations as tests/baseline_configs.py builds them:
+    context ranges, pool sizes, distinct pages dealt from one permutation, and
+    the oracle's reference-order f32 decode within the attention tolerance of
+    its fp64 decode on them."""
+    from tests import baseline_configs
+    for name, (lo, hi) in (("C1", (1, 512)), ("C2", (512, 4096))):
+        c = baseline_configs.build(name)
+        assert c.ctx.min() >= lo and c.ctx.max() <= hi
+        if name == "C1":
+            assert c.NB == 512
+        pages = (c.seq_lens.astype(np.int64) + 15) // 16
+        dealt = np.concatenate([c.block_tables[b, :pages[b]] for b in range(c.B)])
+        assert len(set(dealt.tolist())) == dealt.size and dealt.max() < c.NB
+        again = baseline_configs.build(name)
+        assert np.array_equal(again.q, c.q) and np.array_equal(again.block_tables, c.block_tables)
+        sub = slice(0, 4) if name == "C2" else slice(None)
+        f64 = oracle.paged_decode_f64(c.geom, c.data, None, 0, c.q[0][sub], c.Hq,
+                                      c.block_tables[sub], c.seq_lens[sub], 1.0 / np.sqrt(c.D))
+        f32 = oracle.paged_decode_f32(c.geom, c.data, None, 0, c.q[0][sub], c.Hq,
+                                      c.block_tables[sub], c.seq_lens[sub],
+                                      float(np.float32(1.0) / np.sqrt(np.float32(c.D))))
+        got = oracle.io_bits_to_f32(f32, c.io).astype(np.float64)
+        assert (np.abs(got - f64) <= 2e-3 + 1e-2 * np.abs(f64)).all()

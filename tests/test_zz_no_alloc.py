@@ -28,14 +28,19 @@ def _tu32(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a).astype(np.int32)).to(dev)
 
 
-def _call(entry, pool, layer, q, bt, sl, out, kn, vn):
+def _call(entry, pool, layer, q, bt, sl, out, kn, vn, flags=0, stream=None):
     from voidweb_b200 import _lib as C
     a = C.DecodeArgs(layer, q.shape[0], q.shape[1], bt.shape[1], q.data_ptr(), bt.data_ptr(),
                      sl.data_ptr(), out.data_ptr(),
                      kn.data_ptr() if kn is not None else None,
-                     vn.data_ptr() if vn is not None else None, 0.0, 0)
-    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    C.check(getattr(C.lib(), entry)(pool._h, ctypes.byref(a), stream))
+                     vn.data_ptr() if vn is not None else None, 0.0, flags)
+    s = stream if stream is not None else torch.cuda.current_stream()
+    C.check(getattr(C.lib(), entry)(pool._h, ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)))
+
+
+def _allocs():
+    from voidweb_b200 import _lib as C
+    return C.lib().vw_debug_alloc_count()
 
 
 def _close(got_bits, ref_f64, io, what):
@@ -75,11 +80,15 @@ def test_static_scratch_decode_matches_pool_scratch(case):
     _call("vw_paged_decode", pool, 0, q, bt, sl, ref_out, kn, vn)
     _call("vw_paged_decode_static", pool, 0, q, bt, sl, outs[0], kn, vn)   # first call: setup
     torch.cuda.synchronize()
+    # the library's own allocation count must not move; the device's free
+    # memory is only a loose second check (the GPU may be shared)
+    allocs = _allocs()
     free_before = torch.cuda.mem_get_info(dev)[0]
     _call("vw_paged_decode_static", pool, 0, q, bt, sl, outs[1], kn, vn)
     _call("vw_paged_decode_static", pool, 0, q, bt, sl, outs[2], kn, vn)
     torch.cuda.synchronize()
-    assert torch.cuda.mem_get_info(dev)[0] == free_before, "a static-scratch call allocated"
+    assert _allocs() == allocs, "a static-scratch call allocated"
+    assert torch.cuda.mem_get_info(dev)[0] >= free_before - (64 << 20)
     assert pool.check() == 0
 
     # the pages the oracle reads: the upload, plus the fused append's rows
@@ -96,4 +105,57 @@ def test_static_scratch_decode_matches_pool_scratch(case):
         bits = o.cpu().numpy().view(np.uint16)
         _close(bits, pool_f64, BF16, f"static call {i} vs vw_paged_decode")
         _close(bits, ref64, BF16, f"static call {i} vs oracle")
+    pool.close()
+
+
+def test_static_scratch_layer_chain_with_pdl_and_plan():
+    """Consecutive layers through vw_paged_decode_static on one stream as
+    programmatic dependents with early page streaming (one partial set shared
+    by overlapping launches: a launch writes partials only after the one
+    before it has completed), on a batch whose segments are split across
+    decode CTAs; then the same chain with VW_DECODE_PLANNED.  Every layer's
+    pages and outputs against the oracle; the planned chain bit-identical."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from voidweb_b200 import _lib as C
+    from voidweb_b200.kv import KvPool, PoolSpec
+    dev = torch.device("cuda", 0)
+    ctx = [5, 9000, 17, 3000, 1, 4100, 33, 12000, 700]
+    c = kvgen.make_case(23, 5, 2, 128, 14, len(ctx), 0, 0, BF16, BF16, ctx=ctx)
+    pool = KvPool(PoolSpec(**kvgen.pool_spec_kwargs(c)), device=0)
+    pool.pages_u8().copy_(torch.from_numpy(np.ascontiguousarray(c.data).view(np.uint8).ravel()))
+    bt, sl = _tu32(c.block_tables, dev), _tu32(c.seq_lens, dev)
+    qs = [_t16(c.q[l], dev) for l in range(c.L)]
+    ks = [_t16(c.k_new[l], dev) for l in range(c.L)]
+    vs = [_t16(c.v_new[l], dev) for l in range(c.L)]
+    chain = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
+    s = torch.cuda.Stream(device=dev)
+    results = []
+    for planned in (False, True):
+        outs = [torch.zeros_like(qs[0]) for _ in range(c.L)]
+        torch.cuda.synchronize()
+        allocs = _allocs()
+        with torch.cuda.stream(s):
+            if planned:
+                pool.plan(bt, sl, c.Hq, stream=s)
+            for l in range(c.L):
+                f = (chain if l > 0 else 0) | (C.VW_DECODE_PLANNED if planned else 0)
+                _call("vw_paged_decode_static", pool, l, qs[l], bt, sl, outs[l], ks[l], vs[l],
+                      flags=f, stream=s)
+        s.synchronize()
+        # (the plan lives in pool memory made at creation: nothing new either way)
+        assert _allocs() == allocs, "a static-scratch call allocated"
+        assert pool.check() == 0
+        results.append([o.cpu().numpy().view(np.uint16) for o in outs])
+    data = c.data.copy()
+    slots = kvgen.new_token_slots(c)
+    for l in range(c.L):
+        oracle.kv_append(c.geom, data, None, l, c.k_new[l], c.v_new[l], slots)
+    gdata = pool.pages_u8().cpu().numpy().view(np.uint16).reshape(data.shape)
+    assert np.array_equal(gdata, data)
+    for l in range(c.L):
+        ref = oracle.paged_decode_f64(c.geom, data, None, l, c.q[l], c.Hq, c.block_tables,
+                                      c.seq_lens, 1.0 / np.sqrt(128), nthreads=0)
+        _close(results[0][l], ref, BF16, f"static chain layer {l}")
+        assert np.array_equal(results[1][l], results[0][l]), f"planned layer {l}"
     pool.close()

@@ -162,6 +162,7 @@ SIGNATURES = {
     "vw_fault_inject": (i32, [u32, u32]),
     "vw_fault_pending": (u32, [u32]),
     "vw_debug_set_wait_limit": (i32, [vp, u64]),
+    "vw_debug_alloc_count": (u64, []),
 }
 
 

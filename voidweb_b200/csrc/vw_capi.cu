@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -44,6 +45,19 @@ int32_t cuda_fail(cudaError_t e, const char* what) {
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Every device and pinned-host allocation of this library goes through these
+// two, so that vw_debug_alloc_count can tell a caller whether a call allocated.
+std::atomic<uint64_t> g_alloc_calls{0};
+template <class T>
+cudaError_t dev_alloc(T** p, size_t bytes) {
+    g_alloc_calls.fetch_add(1);
+    return cudaMalloc(reinterpret_cast<void**>(p), bytes);
+}
+cudaError_t pinned_alloc(void** p, size_t bytes) {
+    g_alloc_calls.fetch_add(1);
+    return cudaHostAlloc(p, bytes, cudaHostAllocPortable);
+}
 
 // An armed injected failure (vw_fault_inject) of one of `kinds` ends the call
 // here, before anything else happens.
@@ -252,7 +266,7 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
     if (c.kv_data) {
         p->data = static_cast<uint8_t*>(c.kv_data);
     } else {
-        if ((e = cudaMalloc(&p->data, p->data_bytes)) != cudaSuccess) {
+        if ((e = dev_alloc(&p->data, p->data_bytes)) != cudaSuccess) {
             const unsigned long long bytes = p->data_bytes;
             delete p;
             return fail(VW_ERR_OOM, "vw_pool_create: %llu bytes of pages: %s", bytes, cudaGetErrorString(e));
@@ -262,7 +276,7 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
     if (p->scale_bytes) {
         if (c.kv_scales) {
             p->scales = static_cast<float*>(c.kv_scales);
-        } else if ((e = cudaMalloc(&p->scales, p->scale_bytes)) == cudaSuccess) {
+        } else if ((e = dev_alloc(&p->scales, p->scale_bytes)) == cudaSuccess) {
             p->own_scales = true;
         } else {
             pool_free_all(p);
@@ -274,10 +288,10 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
     const size_t n_ml = decode_scratch_floats_ml(p->grid);
     p->scratch_o = n_o;
     p->scratch_ml = n_ml;
-    if ((e = cudaMalloc(&p->part_o, 2 * n_o * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&p->part_ml, 2 * n_ml * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&p->plan, plan_ints(p->grid) * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&p->err, 4)) != cudaSuccess) {
+    if ((e = dev_alloc(&p->part_o, 2 * n_o * 4)) != cudaSuccess ||
+        (e = dev_alloc(&p->part_ml, 2 * n_ml * 4)) != cudaSuccess ||
+        (e = dev_alloc(&p->plan, plan_ints(p->grid) * 4)) != cudaSuccess ||
+        (e = dev_alloc(&p->err, 4)) != cudaSuccess) {
         pool_free_all(p);
         delete p;
         return fail(VW_ERR_OOM, "vw_pool_create: scratch: %s", cudaGetErrorString(e));
@@ -315,6 +329,8 @@ int32_t vw_pool_info(const vw_pool* pool, void** kv_data, void** kv_scales, uint
     if (scale_bytes) *scale_bytes = pool->scale_bytes;
     return VW_OK;
 }
+
+uint64_t vw_debug_alloc_count(void) { return g_alloc_calls.load(); }
 
 int32_t vw_debug_set_wait_limit(vw_pool* pool, uint64_t cycles) {
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_debug_set_wait_limit: null pool");
@@ -789,7 +805,7 @@ int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* str
         if (pool->stage) cudaFree(pool->stage);
         pool->stage = nullptr;
         pool->stage_bytes = 0;
-        if ((e = cudaMalloc(&pool->stage, need)) != cudaSuccess)
+        if ((e = dev_alloc(&pool->stage, need)) != cudaSuccess)
             return fail(VW_ERR_OOM, "vw_decode_step_host: staging: %s", cudaGetErrorString(e));
         pool->stage_bytes = need;
     }
@@ -847,6 +863,34 @@ int32_t vw_decode_step_host(vw_pool* pool, const vw_step_host_args* a, void* str
 // ---------------------------------------------------------------------------
 
 namespace {
+// Pinned host memory kept across forward passes (grow-only): the step's block
+// tables and lengths, and the gathered decode rows of a mixed batch.  Reusing
+// the same pinned buffers keeps vw_decode_step_host's arguments identical from
+// one engine step to the next, so its recorded step graph is replayed instead
+// of the copies and launches being issued one by one.
+struct PinnedBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    void* get(size_t bytes) {
+        if (bytes <= cap) return p;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+        if (pinned_alloc(&p, bytes) != cudaSuccess) {
+            p = nullptr;
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        cap = bytes;
+        return p;
+    }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+
 struct ForwardState {
     std::mutex mu;
     vw_pool* pool = nullptr;
@@ -855,6 +899,7 @@ struct ForwardState {
     const void* v = nullptr;
     void* out = nullptr;
     std::unordered_map<uint64_t, uint32_t> seq_len;   // tokens cached per sequence
+    PinnedBuf table, lens, dq, dk, dv, dout;
 };
 ForwardState& fwd() {
     static ForwardState s;
@@ -866,6 +911,10 @@ int32_t vw_forward_bind(vw_pool* pool, const void* q, const void* k_new, const v
                         void* attn_out) {
     ForwardState& s = fwd();
     std::lock_guard<std::mutex> lk(s.mu);
+    if (!pool && s.pool) {          // unbinding: the pinned staging goes with the pool
+        DeviceScope ds(s.pool->cfg.device);
+        for (PinnedBuf* b : {&s.table, &s.lens, &s.dq, &s.dk, &s.dv, &s.dout}) b->release();
+    }
     s.pool = pool;
     s.q = q;
     s.k = k_new;
@@ -907,7 +956,7 @@ static int32_t forward_prefill(vw_pool* pool, uint32_t L, uint32_t Hq, uint32_t 
         if (pool->pstage) cudaFree(pool->pstage);
         pool->pstage = nullptr;
         pool->pstage_bytes = 0;
-        if ((e = cudaMalloc(&pool->pstage, need)) != cudaSuccess)
+        if ((e = dev_alloc(&pool->pstage, need)) != cudaSuccess)
             return fail(VW_ERR_OOM, "voidweb_forward_pass: prefill staging: %s", cudaGetErrorString(e));
         pool->pstage_bytes = need;
     }
@@ -1041,20 +1090,25 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
 
     if (!dc.empty()) {
         const uint32_t Bd = (uint32_t)dc.size();
-        std::vector<uint32_t> table((size_t)Bd * stride, 0), lens(Bd);
+        DeviceScope ds(s.pool->cfg.device);
+        uint32_t* table = static_cast<uint32_t*>(s.table.get((size_t)Bd * stride * 4));
+        uint32_t* lens = static_cast<uint32_t*>(s.lens.get((size_t)Bd * 4));
+        if (!table || !lens) return fail(VW_ERR_OOM, "voidweb_forward_pass: pinned staging");
+        std::memset(table, 0, (size_t)Bd * stride * 4);
         for (uint32_t k = 0; k < Bd; ++k) {
             table_of(dc[k], &table[(size_t)k * stride]);
             lens[k] = pos[dc[k]] + 1;
         }
         // an all-decode batch uses the bound buffers in place; otherwise the
-        // decode rows are gathered into [L][Bd][...] arrays first
+        // decode rows are gathered into [L][Bd][...] pinned arrays first
         const bool direct = pf.empty();
-        std::vector<uint8_t> q, kk, vv, o;
+        uint8_t *q = nullptr, *kk = nullptr, *vv = nullptr, *o = nullptr;
         if (!direct) {
-            q.resize((size_t)L * Bd * qrow);
-            kk.resize((size_t)L * Bd * krow);
-            vv.resize((size_t)L * Bd * krow);
-            o.resize((size_t)L * Bd * qrow);
+            q = static_cast<uint8_t*>(s.dq.get((size_t)L * Bd * qrow));
+            kk = static_cast<uint8_t*>(s.dk.get((size_t)L * Bd * krow));
+            vv = static_cast<uint8_t*>(s.dv.get((size_t)L * Bd * krow));
+            o = static_cast<uint8_t*>(s.dout.get((size_t)L * Bd * qrow));
+            if (!q || !kk || !vv || !o) return fail(VW_ERR_OOM, "voidweb_forward_pass: pinned staging");
             for (uint32_t l = 0; l < L; ++l)
                 for (uint32_t k = 0; k < Bd; ++k) {
                     const size_t src = (size_t)l * T + row0[dc[k]], dst = (size_t)l * Bd + k;
@@ -1067,12 +1121,12 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
         st.num_seqs = Bd;
         st.num_q_heads = Hq;
         st.block_table_stride = stride;
-        st.q = direct ? s.q : q.data();
-        st.k_new = direct ? s.k : kk.data();
-        st.v_new = direct ? s.v : vv.data();
-        st.block_tables = table.data();
-        st.seq_lens = lens.data();
-        st.out = direct ? s.out : o.data();
+        st.q = direct ? s.q : q;
+        st.k_new = direct ? s.k : kk;
+        st.v_new = direct ? s.v : vv;
+        st.block_tables = table;
+        st.seq_lens = lens;
+        st.out = direct ? s.out : o;
         st.scale = 0.0f;
         // ModelConfig.rope_theta (engine/ffi.bm:37): q and the new K rows are rotated
         // in the decode, as the engine's own kernels would before attention
@@ -1082,7 +1136,7 @@ int32_t voidweb_forward_pass(const ForwardArgs* args) {
         if (!direct)
             for (uint32_t l = 0; l < L; ++l)
                 for (uint32_t k = 0; k < Bd; ++k)
-                    std::memcpy(ho + ((size_t)l * T + row0[dc[k]]) * qrow, &o[((size_t)l * Bd + k) * qrow], qrow);
+                    std::memcpy(ho + ((size_t)l * T + row0[dc[k]]) * qrow, o + ((size_t)l * Bd + k) * qrow, qrow);
     }
     for (uint32_t i = 0; i < a.num_seqs; ++i) s.seq_len[d[i].seq_id] = pos[i] + d[i].num_tokens;
     return VW_OK;
