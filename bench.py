@@ -52,6 +52,19 @@ WORKLOADS = {
                                          ctx=("uniform", 0, 2048), kv="fp8", io="bf16", seed=13),
     # the FP8 weight path's GEMM (gemm_fp8.bm:31-107): E4M3 A [M][K] x B [K][N] -> bf16
     "fp8-gemm-8192": dict(kind="gemm", M=8192, N=8192, K=8192, seed=12),
+    # shared-prefix radix workload at Qwen2.5-7B KV shapes: 64 requests sharing a
+    # 128-token prefix (8 ref-counted pages), suffixes U[32, 1024], 8 forks of
+    # requests with a partial last page (copy-on-write), then 32 requests finish
+    # into the radix tree, 25 % of its unreferenced blocks are LRU-evicted and the
+    # pool is compacted; decode steps before and after
+    # the standalone page kernels at Qwen2.5-7B KV shapes: append of a 2048-token
+    # chunk's rows into one layer, gather of a 4096-token sequence from one layer,
+    # and 64 whole-block copies (all 28 layers each)
+    "qwen2.5-7b-kvops": dict(kind="kvops", L=28, Hkv=4, D=128, append_tokens=2048, gather_tokens=4096,
+                             copy_pairs=64, kv="bf16", io="bf16", seed=5),
+    "qwen2.5-7b-radix-64": dict(kind="radix", L=28, Hq=28, Hkv=4, D=128, n_req=64, prefix=128,
+                                suffix=(32, 1024), n_fork=8, finish=32, evict_frac=0.25,
+                                kv="bf16", io="bf16", seed=2),
 }
 DEFAULT = "qwen2.5-7b-decode-b16"
 L2_BYTES = 126 * 1024 * 1024
@@ -322,6 +335,262 @@ def run_gemm_bench(args, w):
     }))
 
 
+def run_radix_bench(args, w):
+    """The shared-prefix workload on one GPU: host decisions from this library's
+    block manager and radix tree (engine/kv_cache.bm:94-113 copy-on-write,
+    radix_cache/radix_cache.bm:231-285 LRU eviction, then compaction), device
+    copies and decodes through the C ABI.  Timed: the copy-on-write block
+    copies, the compaction moves (GB/s of bytes read + written), and the decode
+    step of every layer before and after the eviction (KV GB/s, logical bytes:
+    a shared page counts once per sequence that reads it)."""
+    import torch
+    from voidweb_b200 import _lib as C
+    from voidweb_b200.blocks import BlockManager, RadixCacheManager
+    from voidweb_b200.kv import KvPool, PoolSpec
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        print(json.dumps({"metric": "paged decode KV GB/s", "error": "single GPU only"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    L, Hq, Hkv, D = w["L"], w["Hq"], w["Hkv"], w["D"]
+    rng = np.random.Generator(np.random.PCG64(w["seed"]))
+    P = w["prefix"] // 16
+    sfx = rng.integers(w["suffix"][0], w["suffix"][1] + 1, w["n_req"])
+    NB = P + int(((sfx + 1 + 15) // 16).sum()) + 4 * w["n_fork"] + 64
+    bm = BlockManager(L, Hkv, D, 16, NB)
+    rx = RadixCacheManager(16, NB)
+    pool = KvPool(PoolSpec(L, Hkv, D, NB, "bf16", "bf16", max_batch=256), device=0)
+    pool.pages_u8().view(torch.bfloat16).normal_()
+    block_bytes = L * Hkv * 2 * 16 * D * 2
+    t_host = {}
+    # -- build: the prefix in the tree, requests sharing its pages
+    th = time.perf_counter()
+    prefix = rng.integers(1000, 30000, w["prefix"]).tolist()
+    ptable = bm.alloc_seq(P)
+    rx.insert(prefix, ptable)
+    for b in ptable:
+        bm.incref(b)                       # the tree's reference
+    bm.free_seq(ptable)                    # the builder's own
+    seqs = []
+    first = rng.permutation(np.arange(40000, 40000 + w["n_req"]))
+    for i in range(w["n_req"]):
+        toks = prefix + [int(first[i])] + rng.integers(1000, 30000, int(sfx[i]) - 1).tolist()
+        matched, reuse = rx.lookup(toks)
+        assert matched == w["prefix"] and len(reuse) == P
+        for b in reuse:
+            bm.incref(b)
+        table = np.array(reuse + bm.alloc_seq(-(-int(sfx[i]) // 16)), dtype=np.uint32)
+        seqs.append({"tokens": toks, "table": table, "len": len(toks)})
+    parents = [s for s in seqs if s["len"] % 16][: w["n_fork"]]
+    cow = []
+    for par in parents:
+        child = {"tokens": list(par["tokens"]), "table": par["table"].copy(), "len": par["len"]}
+        for b in child["table"]:
+            bm.incref(int(b))
+        cow.append(bm.cow(child["table"], child["len"] // 16))
+        seqs.append(child)
+    t_host["build_ms"] = round((time.perf_counter() - th) * 1e3, 3)
+    cow = np.array(cow, dtype=np.uint32).reshape(-1, 2)
+
+    def time_copies(pairs, reps):
+        pt = torch.from_numpy(pairs.astype(np.int32)).to(dev)
+        pool.block_copy(pt)                      # idempotent: the same copy again
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(reps):
+            pool.block_copy(pt)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        # the copies must equal their sources on every layer
+        pg = pool.pages_u8().view(L, NB, block_bytes // L)
+        src = torch.from_numpy(pairs[:, 0].astype(np.int64)).to(dev)
+        dst = torch.from_numpy(pairs[:, 1].astype(np.int64)).to(dev)
+        assert torch.equal(pg[:, src], pg[:, dst]), "block copy differs from its source"
+        return {"pairs": int(len(pairs)), "us": round(us, 3),
+                "GB/s": round(2 * len(pairs) * block_bytes / (us * 1e-6) / 1e9, 2)}
+
+    def decode_phase(live):
+        B = len(live)
+        stride = max(-(-(s["len"] + 1) // 16) for s in live)
+        bt = np.zeros((B, stride), dtype=np.int32)
+        for i, s in enumerate(live):
+            if -(-(s["len"] + 1) // 16) > len(s["table"]):
+                s["table"] = np.concatenate([s["table"], np.array(bm.alloc_seq(1), dtype=np.uint32)])
+            bt[i, :len(s["table"])] = s["table"]
+        seq_lens = np.array([s["len"] + 1 for s in live], dtype=np.int64)
+        q = torch.randn((L, B, Hq, D), device=dev).bfloat16()
+        kn = torch.randn((L, B, Hkv, D), device=dev).bfloat16()
+        vn = torch.randn((L, B, Hkv, D), device=dev).bfloat16()
+        out = torch.zeros_like(q)
+        btd = torch.from_numpy(bt).to(dev)
+        sld = torch.from_numpy(seq_lens.astype(np.int32)).to(dev)
+        st = torch.cuda.Stream(device=dev)
+        flags = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
+
+        def step(sx):
+            for l in range(L):
+                pool.paged_decode(l, q[l], btd, sld, out[l], k_new=kn[l], v_new=vn[l], stream=sx,
+                                  flags=flags if l else 0)
+        with torch.cuda.stream(st):
+            step(st)
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            step(torch.cuda.current_stream())
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        wl = dict(w, B=B)
+        chk = verify_layer(pool, wl, L // 2, q[L // 2], kn[L // 2], vn[L // 2], out[L // 2], bt, seq_lens)
+        assert chk["ok"], f"radix decode differs from the oracle: {chk}"
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        logical = algorithmic_bytes_per_launch(wl, seq_lens) * L
+        pages = {int(b) for s in live for b in s["table"][: -(-(s["len"] + 1) // 16)]}
+        del g
+        return {"seqs": B, "ms_per_step": round(ms, 4), "GB/s": round(logical / (ms * 1e-3) / 1e9, 2),
+                "logical_bytes_per_step": int(logical),
+                "physical_page_bytes": int(len(pages) * block_bytes), "oracle_check": chk}, logical, ms
+
+    assert pool.check() == 0
+    clocks = ClockSampler(0)
+    clocks.start()
+    res = {"cow_copy": time_copies(cow, 200)}
+    dec1, logical1, ms1 = decode_phase(seqs)
+    for s in seqs:
+        s["len"] += 1
+        s["tokens"].append(int(rng.integers(1000, 30000)))
+    # -- finish, evict, compact
+    th = time.perf_counter()
+    done, live = seqs[: w["finish"]], seqs[w["finish"]:]
+    for s in done:
+        freed = rx.insert(s["tokens"][: s["len"]], s["table"].tolist())
+        for b in s["table"][P:]:
+            bm.incref(int(b))              # the tree keeps the suffix pages
+        for b in freed:
+            bm.decref(b)
+        bm.free_seq(s["table"])
+    live_ids = {int(b) for s in live for b in s["table"]}
+    tree_only = [int(b) for s in done for b in s["table"][P:] if int(b) not in live_ids]
+    evicted = rx.evict_lru(max(1, int(len(tree_only) * w["evict_frac"])))
+    for b in evicted:
+        bm.decref(b)
+    moves = bm.compact()
+    m = dict(zip(moves[:, 0].tolist(), moves[:, 1].tolist()))
+    for s in live:
+        s["table"] = np.array([m.get(int(b), int(b)) for b in s["table"]], dtype=np.uint32)
+    rx.remap(moves)
+    t_host["finish_evict_compact_ms"] = round((time.perf_counter() - th) * 1e3, 3)
+    res["compaction_moves"] = time_copies(np.asarray(moves, dtype=np.uint32).reshape(-1, 2), 50)
+    res["evicted_blocks"] = len(evicted)
+    dec2, _, _ = decode_phase(live)
+    clk = clocks.stop()
+    assert pool.check() == 0
+    peak, peak_kind = hbm_peak()
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        cpu = {"value": None, "unit": "ns/op", "cores": 1, "kind": "port", "cpu_model": cpu_model(),
+               "sample": "block bookkeeping ns/op, one thread: the oracle's restatement of the reference "
+                         "(kv_cache.bm / radix_cache.bm) beside this library's own",
+               "block_ops_ns_per_op_1_thread": oracle.bench_block_ops(200000),
+               "block_ops_ns_per_op_product_1_thread": product_block_ops(200000)}
+    print(json.dumps({
+        "metric": "paged decode KV GB/s", "value": dec1["GB/s"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dec1["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv, "head_dim": D,
+                   "requests": w["n_req"], "forks": w["n_fork"], "prefix_tokens": w["prefix"],
+                   "suffix": list(w["suffix"]), "pool_blocks": NB, "parallelism": "single",
+                   "l2": f"inputs larger than L2 ({logical1 / 1e9:.2f} GB logical per step)"},
+        "tok_per_s": round(dec1["seqs"] / (ms1 * 1e-3), 1),
+        "decode_before_eviction": dec1, "decode_after_compaction": dec2, **res, "host_ms": t_host,
+        "roofline": {"bound": "hbm", "achieved": dec1["GB/s"], "peak": peak, "unit": "GB/s",
+                     "frac": round(dec1["GB/s"] / peak, 4), "traffic": None, "peak_kind": peak_kind},
+        "cpu_baseline": cpu, "e2e": None, "clocks": clk,
+        "gpu_launches": args.steps * L * 2 * 2 + 250,
+    }), flush=True)
+    pool.close()
+
+
+def run_kvops_bench(args, w):
+    """vw_kv_append, vw_kv_gather and vw_block_copy alone, each timed with CUDA
+    events over K launches on inputs larger than L2 in total; GB/s of the bytes
+    each launch must read and write."""
+    import torch
+    from voidweb_b200.kv import KvPool, PoolSpec
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        print(json.dumps({"metric": "page kernels GB/s", "error": "single GPU only"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    L, Hkv, D = w["L"], w["Hkv"], w["D"]
+    T, G, NP = w["append_tokens"], w["gather_tokens"], w["copy_pairs"]
+    NB = 2 * NP + (T + G) // 16 * 8 + 64
+    rng = np.random.Generator(np.random.PCG64(w["seed"]))
+    pool = KvPool(PoolSpec(L, Hkv, D, NB, "bf16", "bf16", max_batch=1), device=0)
+    pool.pages_u8().view(torch.bfloat16).normal_()
+    row = Hkv * D * 2
+    perm = rng.permutation(NB)
+    # append: T rows into distinct random slots of one layer (rotating layers)
+    slots = torch.from_numpy((perm[: T // 16 * 2].repeat(16)[:T] * 16 +
+                              np.tile(np.arange(16), T // 16)).astype(np.int64)).to(dev)
+    kn = torch.randn((T, Hkv, D), device=dev).bfloat16()
+    vn = torch.randn((T, Hkv, D), device=dev).bfloat16()
+    gtable = torch.from_numpy(perm[-(G // 16):].astype(np.int32)).to(dev)
+    pairs_np = np.stack([perm[T // 8: T // 8 + NP], perm[T // 8 + NP: T // 8 + 2 * NP]], 1)
+    pairs = torch.from_numpy(pairs_np.astype(np.int32)).to(dev)
+    block_bytes = L * Hkv * 2 * 16 * D * 2
+    ops = {
+        "kv_append_kernel": (lambda i: pool.append(i % L, kn, vn, slots), 2 * T * row * 2),
+        "kv_gather_kernel": (lambda i: pool.gather(i % L, gtable, G), 2 * G * row * 2),
+        "block_copy_kernel": (lambda i: pool.block_copy(pairs), 2 * NP * block_bytes),
+    }
+    res = {}
+    clocks = ClockSampler(0)
+    clocks.start()
+    for name, (fn, nbytes) in ops.items():
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for i in range(args.steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        res[name] = {"bytes_per_launch": nbytes, "us_per_launch": round(us, 3),
+                     "GB/s": round(nbytes / (us * 1e-6) / 1e9, 2)}
+    clk = clocks.stop()
+    assert pool.check() == 0
+    peak, peak_kind = hbm_peak()
+    for v in res.values():
+        v["frac_of_peak"] = round(v["GB/s"] / peak, 4)
+    top = res["block_copy_kernel"]
+    print(json.dumps({
+        "metric": "page kernels GB/s", "value": top["GB/s"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(top["us_per_launch"] / 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "layers": L, "kv_heads": Hkv, "head_dim": D,
+                   "append_tokens": T, "gather_tokens": G, "copy_pairs": NP, "parallelism": "single"},
+        "kernels": res,
+        "roofline": {"bound": "hbm", "achieved": top["GB/s"], "peak": peak, "unit": "GB/s",
+                     "frac": top["frac_of_peak"], "traffic": None, "peak_kind": peak_kind},
+        "cpu_baseline": None, "e2e": None, "clocks": clk, "gpu_launches": 3 * (args.steps + args.warmup),
+    }), flush=True)
+    pool.close()
+
+
 def hbm_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -383,6 +652,17 @@ class ClockSampler:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "samples": len(sm),
                 "reasons": sorted(reasons)}
+
+
+def product_block_ops(iters):
+    """ns/op of this library's own block manager and radix tree (vw_bm_*,
+    vw_radix_*), one thread, from the vw_bench_ops tool built beside it."""
+    exe = os.path.join(ROOT, "voidweb_b200", "vw_bench_ops")
+    try:
+        out = subprocess.run([exe, str(iters)], capture_output=True, text=True, timeout=120, check=True)
+        return json.loads(out.stdout)
+    except Exception as e:          # reported, not fatal: the GPU figures stand alone
+        return {"error": str(e)[:200]}
 
 
 def cpu_model():
@@ -528,6 +808,9 @@ def main():
                          "every GPU the same sequences and block tables with its own KV heads "
                          "(the workload's kv_heads per GPU: Llama-3-70B one KV head per GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--plan", action="store_true",
+                    help="compute the decode plan (vw_decode_plan) once per step and launch every "
+                         "layer with VW_DECODE_PLANNED")
     ap.add_argument("--layers", type=int, default=0,
                     help="run only this many layers of the workload (a small case for ncu "
                          "captures; the JSON line's config.layers says so)")
@@ -543,6 +826,22 @@ def main():
                               "workloads; the gemm line's cpu_baseline is the oracle sample"}))
             return
         return run_gemm_bench(args, w)
+    if w.get("kind") == "kvops":
+        if args.warmup < 3:
+            args.warmup = 3
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the decode "
+                              "workloads"}))
+            return
+        return run_kvops_bench(args, w)
+    if w.get("kind") == "radix":
+        if args.warmup < 3:
+            args.warmup = 3
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the decode "
+                              "workloads; the radix line's cpu_baseline holds the block-op figures"}))
+            return
+        return run_radix_bench(args, w)
     if w.get("kind") == "prefill":
         if args.warmup < 3:
             args.warmup = 3
@@ -646,9 +945,14 @@ def main():
     flags = C.VW_DECODE_PDL | C.VW_DECODE_EARLY_PAGES
 
     def step(s, o):
+        if args.plan:
+            pool.plan(bt_d, sl_d, Hq, stream=s)
         for layer in range(L):
+            f = flags
+            if args.plan:      # the layer right after the plan waits for it in stream order
+                f = C.VW_DECODE_PLANNED | (flags if layer > 0 else 0)
             pool.paged_decode(layer, q[layer], bt_d, sl_d, o[layer], k_new=kn[layer],
-                              v_new=vn[layer], stream=s, flags=flags)
+                              v_new=vn[layer], stream=s, flags=f)
 
     # first launches outside capture (per-device kernel attribute set-up)
     with torch.cuda.stream(stream):
@@ -790,17 +1094,30 @@ def main():
         # the same step through the symbol the engine dlopens: voidweb_forward_pass
         # with the packed descriptors KernelLib.forward_pass builds (engine/ffi.bm:86-121);
         # the bound q / new K / new V / output buffers are the pinned ones above
+        import ctypes
         from voidweb_b200 import KernelLib
         Lb = C.lib()
         kl = KernelLib.open(C.LIB_PATH)
         Lb.vw_forward_bind(pool.handle, hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr())
-        seqs = [(1000 + b, 7, bt[b, :pages[b]].astype(np.uint32)) for b in range(B)]
-        cfg = dict(num_heads=Hq, num_kv_heads=Hkv, num_layers=L, head_dim=D, rope_theta=0.0)
+        # the engine builds its descriptors natively; here they are built once and
+        # the bound symbol is called directly, so that Python adds little per step
+        toks = np.full(B, 7, dtype=np.uint32)
+        tables = [np.ascontiguousarray(bt[b, :pages[b]], dtype=np.uint32) for b in range(B)]
+        descs = (C.SeqDescriptor * B)()
+        for b in range(B):
+            descs[b] = C.SeqDescriptor(1000 + b, toks.ctypes.data + 4 * b, 1, tables[b].ctypes.data,
+                                       tables[b].size, 0)
+        fargs = C.ForwardArgs(ctypes.cast(descs, ctypes.c_void_p), B, 0, Hq, Hkv, L, 1, D, 0.0, 0, None)
+        set_len, fwd = Lb.vw_forward_set_seq_len, kl._forward
+        ids = [1000 + b for b in range(B)]
+        lens = [int(x) for x in ctx]
 
         def fwd_step():
-            for b in range(B):         # every step decodes the same position (fixed workload)
-                Lb.vw_forward_set_seq_len(1000 + b, int(ctx[b]))
-            kl.forward_pass(cfg, seqs)
+            for i, n in zip(ids, lens):   # every step decodes the same position (fixed workload)
+                set_len(i, n)
+            rc = fwd(ctypes.byref(fargs))
+            if rc != 0:
+                raise RuntimeError(f"GPU forward pass failed with code {rc}: {Lb.vw_last_error()}")
 
         for _ in range(3):
             fwd_step()
@@ -824,8 +1141,8 @@ def main():
             "value": round(step_bytes_all / (fms * 1e-3) / 1e9, 3), "unit": "GB/s",
             "ms_per_step": round(fms, 4), "tok_per_s": round(total_seqs / (fms * 1e-3), 1),
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(ho.numel() * 2),
-            "path": "voidweb_forward_pass through KernelLib.forward_pass (packed SeqDescriptor / "
-                    "ForwardArgs, host block lists, pinned bound buffers)"}
+            "path": "voidweb_forward_pass as KernelLib::forward_pass calls it (packed SeqDescriptor / "
+                    "ForwardArgs with host block lists, pinned bound buffers; rope_theta 0)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -842,7 +1159,8 @@ def main():
                "tok_per_s": round(ctok, 2),
                "sample": f"{launches} layer launches (1 of {w['L']} layers, same {B} sequences), "
                          f"{dt:.1f} s; oracle f32 reference-order decode + append, OpenMP",
-               "block_ops_ns_per_op_1_thread": oracle.bench_block_ops(200000)}
+               "block_ops_ns_per_op_1_thread": oracle.bench_block_ops(200000),
+               "block_ops_ns_per_op_product_1_thread": product_block_ops(200000)}
 
     if rank == 0:
         line = {
@@ -859,7 +1177,8 @@ def main():
                        "l2": f"inputs larger than L2 ({bytes_launch * L / 1e9:.2f} GB of KV "
                              f"per step per GPU vs {L2_BYTES / 1e6:.0f} MB L2)",
                        "graph": "one CUDA graph per step: one fused append+decode launch per layer, "
-                                "programmatic dependent launches with early page streaming",
+                                "programmatic dependent launches with early page streaming" +
+                                (", decode plan made once per step" if args.plan else ""),
                        "gather": (f"NCCL all-gather of each step's outputs on a side stream, overlapping "
                                   f"the next step (double-buffered outputs)") if world > 1 else None},
             "tok_per_s": round(tok_s, 1),
@@ -876,7 +1195,7 @@ def main():
             "clocks": clocks,
             "oracle_check": verified,
             # per layer: the fused append+decode grid and its split-K combine grid
-            "gpu_launches": args.steps * L * 2,
+            "gpu_launches": args.steps * (L * 2 + (1 if args.plan else 0)),
         }
         print(json.dumps(line), flush=True)
     del graphs

@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -296,7 +297,8 @@ int32_t vw_pool_create(const vw_pool_config* cfg, vw_pool** out) {
         delete p;
         return fail(VW_ERR_OOM, "vw_pool_create: scratch: %s", cudaGetErrorString(e));
     }
-    if ((e = cudaMemset(p->err, 0, 4)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+    if ((e = cudaMemset(p->err, 0, 4)) != cudaSuccess ||
+        (e = cudaDeviceSynchronize()) != cudaSuccess) {
         pool_free_all(p);
         delete p;
         return cuda_fail(e, "vw_pool_create: memset");
@@ -418,6 +420,29 @@ struct DecodeScratch {
     float* ml;
 };
 
+// Decode launch options fixed for the process, from the environment:
+//  VOIDWEB_KV_DIRECT_Q=1|0          the first segment's query rows read straight
+//                                   from global memory by the consumer warps
+//                                   (default 1: 4455 -> 4503 GB/s on the Qwen step)
+//  VOIDWEB_KV_L2_AHEAD=n            with early pages: n more pages of the first
+//                                   batch prefetched into L2 before the wait
+uint32_t env_l2_ahead() {
+    static const uint32_t v = [] {
+        const char* e = std::getenv("VOIDWEB_KV_L2_AHEAD");
+        return e ? (uint32_t)std::strtoul(e, nullptr, 10) : 0u;
+    }();
+    return v;
+}
+uint32_t env_decode_flags() {
+    static const uint32_t v = [] {
+        uint32_t f = 0;
+        const char* q = std::getenv("VOIDWEB_KV_DIRECT_Q");
+        if (!(q && std::strcmp(q, "0") == 0)) f |= kDecodeDirectQ;
+        return f;
+    }();
+    return v;
+}
+
 static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_t s,
                              const DecodeScratch* fixed = nullptr) {
     const PoolGeom& g = pool->geom;
@@ -439,7 +464,7 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
         p.part_o = pool->part_o + set * pool->scratch_o;
         p.part_ml = pool->part_ml + set * pool->scratch_ml;
     }
-    p.flags = a->flags;
+    p.flags = a->flags | env_decode_flags();
     p.plan = (a->flags & VW_DECODE_PLANNED) ? pool->plan : nullptr;
     p.err = pool->err;
     p.B = a->num_seqs;
@@ -455,6 +480,12 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
     p.scale_log2 = scale * 1.4426950408889634f;
     p.rope_theta = (a->flags & VW_DECODE_ROPE) ? a->rope_theta : 0.0f;
     p.wait_cycles = pool->wait_cycles;
+    if (pool->wait_cycles) {
+        // the bounded-wait test hook: the query tiles are withheld (and read only
+        // from the ring), so the first wait of every consumer warp runs out
+        p.flags = (p.flags | kDecodeWithholdQ) & ~kDecodeDirectQ;
+    }
+    p.l2_ahead = env_l2_ahead();
     L.tmap = &pool->tmap;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;

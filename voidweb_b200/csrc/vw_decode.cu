@@ -146,7 +146,8 @@ struct Traits {
     static constexpr int MERGE = W * G * (MROW + 2) * 4 + (W + 2) * G * 4;
     static constexpr int QTILE = G * D * 2;
     static constexpr int QSLOT = QTILE + 2 * D * 2;          // + the new token's K and V rows
-    static constexpr int PFX = align_up_c(2 * (kMaxBatchPerLaunch + 1) * 4, 128);
+    // prefixes of pages and of sequences with pages [B+1] each, and the seq_lens [B]
+    static constexpr int PFX = align_up_c((3 * kMaxBatchPerLaunch + 2) * 4, 128);
     static constexpr int FIXED = align_up_c(MERGE, 1024) +
                                  align_up_c(kQSlots * QSLOT, 1024) + PFX + PW * 1024 + 1024;
     static constexpr int BUDGET = kSmemPerCta - 1024 /* base alignment slack */ -
@@ -198,6 +199,7 @@ struct Smem {
     uint8_t* qring;      // [kQSlots][QSLOT]: [G][D] query rows, then new K, new V rows (io dtype)
     int* pfx;            // [B+1] exclusive prefix of pages per sequence
     int* nzp;            // [B+1] exclusive prefix of sequences with pages
+    int* slen;           // [B] seq_lens as the prologue read them
     PageInfo* pinfo;     // [PW][2][32] producer batches, one pair per producer warp
     uint64_t* full;      // [S]
     uint64_t* empty;     // [S]
@@ -220,6 +222,7 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     s.qring = p; p += align_up_c(kQSlots * T::QSLOT, 1024);
     s.pfx = reinterpret_cast<int*>(p);
     s.nzp = s.pfx + (kMaxBatchPerLaunch + 1);
+    s.slen = s.nzp + (kMaxBatchPerLaunch + 1);
     p += T::PFX;
     s.pinfo = reinterpret_cast<PageInfo*>(p); p += T::PW * 1024;
     s.full = reinterpret_cast<uint64_t*>(p);
@@ -300,12 +303,12 @@ __device__ __forceinline__ int range_start(const int* pfx, const int* nzp, int B
 __device__ __forceinline__ void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
 
 // Pages per sequence -> exclusive prefixes of pages (pfx) and of sequences with
-// pages (nzp), by one warp, 32 sequences at a time.  A seq_len of 0 gives no
-// pages and one longer than its block-table row is clamped to the row; both
-// are flagged when `report`.
+// pages (nzp), by one warp, 32 sequences at a time, keeping each seq_len in
+// slen when given.  A seq_len of 0 gives no pages and one longer than its
+// block-table row is clamped to the row; both are flagged when `report`.
 __device__ __forceinline__ void warp_prefixes(const uint32_t* seq_lens, int B, int bt_stride,
                                               uint32_t* err, bool report, int* pfx, int* nzp,
-                                              int lane) {
+                                              int* slen, int lane) {
     int run = 0, run_nz = 0;
     if (lane == 0) { pfx[0] = 0; nzp[0] = 0; }
     for (int base_b = 0; base_b < B; base_b += 32) {
@@ -313,6 +316,7 @@ __device__ __forceinline__ void warp_prefixes(const uint32_t* seq_lens, int B, i
         int np = 0;
         if (b < B) {
             const int sl = (int)__ldg(seq_lens + b);
+            if (slen) slen[b] = sl;
             np = (sl + 15) >> 4;
             if (sl <= 0 || np > bt_stride) {
                 if (report) set_err(err, kDevErrSeqLen);
@@ -457,6 +461,13 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     if (lane < T::IPW)
         for (int j = k_me; j < early_n; j += T::NI) issue_page(j, mine[j]);
     if (early_n > 0 && pw == 0) {
+        // pages of the first batch past the ring: into L2 while the predecessor
+        // drains, so their copies after the wait hit L2 (p.l2_ahead of them)
+        const int ahead_end = min(min(32, n), early_n + (int)p.l2_ahead);
+        for (int j = early_n + lane; j < ahead_end; j += 32) {
+            const PageInfo pj = mine[j];
+            if (pj.row0 >= 0) bulk_prefetch_l2(p.kv_data + (size_t)pj.row0 * T::ROW, T::STAGE);
+        }
         // warm L2 with the query tiles (and new K/V rows) of the first batch's
         // segments: the predecessor may still write them, but L2 is where that
         // write lands, so the bulk copies after the wait find them there anyway
@@ -482,7 +493,7 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
             for (int j = qlane ? 0 : k_me; j < m && ok; j += qlane ? 1 : T::NI) {
                 const int ii = i0 + j;
                 const PageInfo pi = mine[buf * 32 + j];
-                if (qlane && pi.qseg >= 0) {
+                if (qlane && pi.qseg >= 0 && !(p.flags & kDecodeWithholdQ)) {
                     // a new segment starts here: its query tile
                     const int k = pi.qseg, qs = k % kQSlots;
                     if (k >= kQSlots &&
@@ -492,13 +503,19 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
                     }
                     uint8_t* slot = sm.qring + qs * T::QSLOT;
                     const bool nkv = pi.kvrow >= 0;
-                    mbar_arrive_expect_tx(&sm.qfull[qs], qbytes + (nkv ? 4 * T::D : 0));
-                    bulk_load(slot, qbase + (size_t)pi.qrow * T::D * 2, qbytes, &sm.qfull[qs]);
-                    if (nkv) {
-                        bulk_load(slot + T::QTILE, kbase + (size_t)pi.kvrow * T::D * 2, T::D * 2,
-                                  &sm.qfull[qs]);
-                        bulk_load(slot + T::QTILE + T::D * 2, vbase + (size_t)pi.kvrow * T::D * 2,
-                                  T::D * 2, &sm.qfull[qs]);
+                    if (k == 0 && (p.flags & kDecodeDirectQ)) {
+                        // the consumers load this segment's rows themselves; the
+                        // slot's phase still completes, so the ring stays in step
+                        mbar_arrive(&sm.qfull[qs]);
+                    } else {
+                        mbar_arrive_expect_tx(&sm.qfull[qs], qbytes + (nkv ? 4 * T::D : 0));
+                        bulk_load(slot, qbase + (size_t)pi.qrow * T::D * 2, qbytes, &sm.qfull[qs]);
+                        if (nkv) {
+                            bulk_load(slot + T::QTILE, kbase + (size_t)pi.kvrow * T::D * 2, T::D * 2,
+                                      &sm.qfull[qs]);
+                            bulk_load(slot + T::QTILE + T::D * 2, vbase + (size_t)pi.kvrow * T::D * 2,
+                                      T::D * 2, &sm.qfull[qs]);
+                        }
                     }
                     segs_issued = k + 1;
                 }
@@ -798,30 +815,41 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         const int cnt = min(np - pg0, end - x);
         const bool complete = pg0 == 0 && cnt == np;
         const int i_base = x - begin;
-        const int seq_len = (int)__ldg(p.seq_lens + b);
+        const int seq_len = sm.slen[b];     // read in the prologue: no load after the release
 
         // query tile of this segment (staged by the producer)
         uint32_t qf[T::NT][T::KT][2];
         uint32_t nkv[2][2] = {{0u, 0u}, {0u, 0u}};
         {
             const int qs = seg_k % kQSlots;
-            // every lane waits, then the warp agrees (and reconverges) before the
-            // warp-collective fragment loads that follow
-            const bool got = !alive || mbar_wait(&sm.qfull[qs], (seg_k / kQSlots) & 1, deadline);
+            // The first segment's rows come straight from global memory (L2, where
+            // the producer prefetched them) when kDecodeDirectQ is set; the others
+            // from the query ring.  Every lane waits, then the warp agrees (and
+            // reconverges) before the warp-collective fragment loads that follow.
+            const bool direct = seg_k == 0 && (p.flags & kDecodeDirectQ);
+            const bool got = !alive || direct ||
+                             mbar_wait(&sm.qfull[qs], (seg_k / kQSlots) & 1, deadline);
             if (!__all_sync(0xffffffffu, got)) {
                 if (lane == 0) set_err(p.err, kDevErrTimeout);
                 alive = false;
             }
-            load_q<T>(p, sm.qring + qs * T::QSLOT, lane, (float)(seq_len - 1), qf);
+            const uint8_t* qsrc = direct ? reinterpret_cast<const uint8_t*>(p.q) +
+                                               (size_t)(b * p.Hq + h * p.group) * T::D * 2
+                                         : sm.qring + qs * T::QSLOT;
+            load_q<T>(p, qsrc, lane, (float)(seq_len - 1), qf);
             if (append && pg0 + cnt == np) {
                 // this range holds the segment's last page: keep the staged new
                 // K/V row pieces of this lane for the append
-                const uint8_t* nrow = sm.qring + qs * T::QSLOT + T::QTILE + lane * (T::D / 32) * 2;
+                const size_t kvoff = (size_t)(b * Hkv + h) * T::D * 2 + lane * (T::D / 32) * 2;
+                const uint8_t* krow = direct ? reinterpret_cast<const uint8_t*>(p.k_new) + kvoff
+                                             : sm.qring + qs * T::QSLOT + T::QTILE + lane * (T::D / 32) * 2;
+                const uint8_t* vrow = direct ? reinterpret_cast<const uint8_t*>(p.v_new) + kvoff
+                                             : krow + T::D * 2;
 #pragma unroll
-                for (int kv = 0; kv < 2; ++kv)
-#pragma unroll
-                    for (int k = 0; k < T::D / 64; ++k)
-                        nkv[kv][k] = reinterpret_cast<const uint32_t*>(nrow + kv * T::D * 2)[k];
+                for (int k = 0; k < T::D / 64; ++k) {
+                    nkv[0][k] = reinterpret_cast<const uint32_t*>(krow)[k];
+                    nkv[1][k] = reinterpret_cast<const uint32_t*>(vrow)[k];
+                }
                 if (p.rope_theta > 0.0f) {
                     // the new K row at position seq_len-1: lane l holds elements
                     // l*D/32 .. +D/32-1, whose partners (d +- D/2) lane l ^ 16 holds
@@ -1147,6 +1175,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         for (int i = threadIdx.x; i <= (int)p.B; i += T::THREADS) {
             sm.pfx[i] = __ldcg(p.plan + kPlanPfx + i);
             sm.nzp[i] = __ldcg(p.plan + kPlanNzp + i);
+            if (i < (int)p.B) sm.slen[i] = (int)__ldg(p.seq_lens + i);
         }
         if (warp >= T::W) {
             // every producer warp takes the first batch into its own buffer
@@ -1163,7 +1192,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
     } else if (warp == T::W) {
         if (lane == 0) prefetch_tensormap(&tmap);
         warp_prefixes(p.seq_lens, (int)p.B, (int)p.bt_stride, p.err, blockIdx.x == 0, sm.pfx, sm.nzp,
-                      lane);
+                      sm.slen, lane);
     }
     __syncthreads();
     if (threadIdx.x == 0) VW_TRACE(1, globaltimer());
@@ -1299,7 +1328,7 @@ __global__ void __launch_bounds__(32) plan_kernel(const DecodeParams p, int* pla
     __shared__ int pfx[kMaxBatchPerLaunch + 1], nzp[kMaxBatchPerLaunch + 1];
     const int lane = threadIdx.x;
     const int B = (int)p.B, Hkv = (int)p.Hkv;
-    warp_prefixes(p.seq_lens, B, (int)p.bt_stride, p.err, blockIdx.x == 0, pfx, nzp, lane);
+    warp_prefixes(p.seq_lens, B, (int)p.bt_stride, p.err, blockIdx.x == 0, pfx, nzp, nullptr, lane);
     __syncwarp();
     if (blockIdx.x == 0) {
         if (lane == 0) {

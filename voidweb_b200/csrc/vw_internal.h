@@ -32,11 +32,20 @@ struct DecodeParams {
     float rope_theta;           // > 0: rotate q and the new K row (RoPE) at position seq_len-1
     uint32_t flags;             // kDecodePdl | kDecodeEarlyPages | kDecodePlanned
     uint64_t wait_cycles;       // bound of the device waits in SM cycles (0: kWaitDeadlineCycles)
+    uint32_t l2_ahead;          // with early pages: first-batch pages past the ring prefetched into L2
 };
 
 constexpr uint32_t kDecodePdl = 0x1u;
 constexpr uint32_t kDecodeEarlyPages = 0x2u;
 constexpr uint32_t kDecodePlanned = 0x4u;
+// The consumer warps read the first segment's query rows (and new K/V rows)
+// straight from global memory after the dependency wait, instead of waiting
+// for the producer's bulk copy of them into the query ring.
+constexpr uint32_t kDecodeDirectQ = 0x200u;
+// Test hook (vw_debug_set_wait_limit): the producer withholds the query-tile
+// copies, so the consumers' first wait is one that nothing completes and runs
+// out at the (shortened) deadline.
+constexpr uint32_t kDecodeWithholdQ = 0x400u;
 
 // Decode plan (int32 words): a header {B, bt_stride, grid, Hkv}, the exclusive
 // prefixes of pages and of sequences with pages over the batch, then one entry
