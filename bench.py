@@ -8,10 +8,12 @@ head_dim 128, bf16 KV, 16 sequences with context lengths uniform in
 [512, 4096] (seed 1), random non-contiguous block tables, 16-token pages.
 Synthetic inputs (no dataset); K/V/Q drawn N(0,1).
 
-N GPUs (torchrun, one process per GPU): every rank holds its own shard of
-sequences (weak scaling: 16 sequences per GPU; with --scaling strong the one
-16-sequence batch of the 1-GPU run is split across the GPUs), and the
-per-shard attention outputs of each step are all-gathered over NCCL.
+N GPUs (torchrun, one process per GPU): every rank holds its own 16 sequences
+with the 1-GPU run's length draw (weak scaling; with --scaling strong the one
+16-sequence batch of the 1-GPU run is split across the GPUs; with --placement
+kv_heads every rank holds the same sequences and its own KV heads, the
+Llama-3-70B placement), and the per-shard attention outputs of each step are
+all-gathered over NCCL.
 
 --impl reference times the reference's CPU implementation of this path (the
 oracle's restatement of paged_attention_decode + append, f32, all host
@@ -141,7 +143,7 @@ def algorithmic_bytes_per_launch(w, seq_lens):
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch of the
 # default workload, from one ncu --set full capture of that launch; ncu cannot
 # run inside the timed bench, so the figure is carried here.
-NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 71_157_760,
+NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 79_998_720,
                           # one prefill_kernel launch (one layer), read + write
                           "qwen2.5-7b-prefill-4x2048": 111_355_904,
                           "llama3-8b-fp8-prefill-4x2048": 123_923_456}
@@ -549,24 +551,45 @@ def run_kvops_bench(args, w):
     pairs_np = np.stack([perm[T // 8: T // 8 + NP], perm[T // 8 + NP: T // 8 + 2 * NP]], 1)
     pairs = torch.from_numpy(pairs_np.astype(np.int32)).to(dev)
     block_bytes = L * Hkv * 2 * 16 * D * 2
+    gk = torch.empty((Hkv, G, D), dtype=torch.int16, device=dev)
+    gv = torch.empty_like(gk)
+    from voidweb_b200 import _lib as C
+    from voidweb_b200.kv import _ptr
+    lib = C.lib()
+    st = torch.cuda.Stream(device=dev)
+    sp = st.cuda_stream
     ops = {
-        "kv_append_kernel": (lambda i: pool.append(i % L, kn, vn, slots), 2 * T * row * 2),
-        "kv_gather_kernel": (lambda i: pool.gather(i % L, gtable, G), 2 * G * row * 2),
-        "block_copy_kernel": (lambda i: pool.block_copy(pairs), 2 * NP * block_bytes),
+        "kv_append_kernel": (lambda i: C.check(lib.vw_kv_append(pool.handle, i % L, _ptr(kn), _ptr(vn),
+                                                                 _ptr(slots), T, sp)), 2 * T * row * 2),
+        "kv_gather_kernel": (lambda i: C.check(lib.vw_kv_gather(pool.handle, i % L, _ptr(gtable), G, _ptr(gk),
+                                                                 _ptr(gv), None, None, sp)), 2 * G * row * 2),
+        "block_copy_kernel": (lambda i: C.check(lib.vw_block_copy(pool.handle, _ptr(pairs), NP, sp)),
+                              2 * NP * block_bytes),
     }
     res = {}
     clocks = ClockSampler(0)
     clocks.start()
     for name, (fn, nbytes) in ops.items():
-        for i in range(args.warmup):
-            fn(i)
+        # the launches are recorded as one CUDA graph and replayed, so that the
+        # timing is the kernels' and not the host's issue rate
+        with torch.cuda.stream(st):
+            for i in range(args.warmup):
+                fn(i)
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(args.steps):
+                fn(i)
+        with torch.cuda.stream(st):
+            g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-        e0.record()
-        for i in range(args.steps):
-            fn(i)
-        e1.record()
+        with torch.cuda.stream(st):       # replay and events on the same stream
+            e0.record(st)
+            g.replay()
+            e1.record(st)
         torch.cuda.synchronize()
+        del g
         us = e0.elapsed_time(e1) * 1e3 / args.steps
         res[name] = {"bytes_per_launch": nbytes, "us_per_launch": round(us, 3),
                      "GB/s": round(nbytes / (us * 1e-6) / 1e9, 2)}
@@ -868,9 +891,10 @@ def main():
         # the per-step output all-gather overlaps the next step's decode: two
         # NCCL channels move 3 MB per rank in time and leave the SMs to the decode
         os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
-        # the communicator's set-up lines (ranks, NVLink/NVLS paths) go to stderr
+        # the communicator's set-up lines (ranks, NVLink/NVLS paths) go to stderr,
+        # so that stdout keeps the one JSON line
         os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
@@ -888,10 +912,12 @@ def main():
         s0, s1 = shard_range(B, world, rank)
         ctx = ctx_lengths(w, 0)[s0:s1]
         B = s1 - s0
-    elif heads_split:
-        ctx = ctx_lengths(w, 0)                      # every rank: the same sequences
     else:
-        ctx = ctx_lengths(w, rank)                   # each rank: its own shard of sequences
+        # kv_heads: every rank the same sequences (its own KV heads); sequences:
+        # each rank its own sequences with the same length draw, so that the
+        # per-GPU work is the 1-GPU workload exactly (weak scaling); the page
+        # contents and block tables differ by rank
+        ctx = ctx_lengths(w, 0)
     # the step appends the token at position ctx and decodes over ctx + 1 tokens
     seq_lens = ctx + 1
     pages = (seq_lens + 15) // 16

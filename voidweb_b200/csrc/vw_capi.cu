@@ -361,6 +361,8 @@ int32_t vw_kv_append(vw_pool* pool, uint32_t layer, const void* k_new, const voi
     if (layer >= pool->geom.num_layers)
         return fail(VW_ERR_INVALID_ARG, "vw_kv_append: layer %u >= %u", layer, pool->geom.num_layers);
     if (num_tokens == 0) return VW_OK;
+    if ((uint64_t)num_tokens * 2 * pool->geom.num_kv_heads >= (1ull << 31))
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_append: num_tokens %u too large", num_tokens);
     if (!k_new || !v_new || !slot_mapping)
         return fail(VW_ERR_INVALID_ARG, "vw_kv_append: null device pointer");
     if (!aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(slot_mapping, 8))
@@ -527,7 +529,7 @@ static int32_t prefill_validate(const vw_pool* pool, const vw_prefill_args* a) {
                     a->num_q_heads, g.num_kv_heads);
     if (a->block_table_stride == 0)
         return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: block_table_stride must be > 0");
-    if (a->num_tokens > (1u << 24))
+    if (a->num_tokens > (1u << 24) || (uint64_t)a->num_tokens * g.num_kv_heads >= (1ull << 31))
         return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: num_tokens %u too large", a->num_tokens);
     if (!a->q || !a->cu_seqlens || !a->ctx_start || !a->block_tables || !a->out)
         return fail(VW_ERR_INVALID_ARG, "vw_paged_prefill: null device pointer");
@@ -691,6 +693,8 @@ int32_t vw_kv_gather(vw_pool* pool, uint32_t layer, const uint32_t* block_table,
     if (!pool) return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: null pool");
     if (layer >= pool->geom.num_layers) return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: bad layer");
     if (seq_len == 0) return VW_OK;
+    if ((uint64_t)seq_len * 2 * pool->geom.num_kv_heads >= (1ull << 31))
+        return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: seq_len %u too large", seq_len);
     if (!block_table || !out_k || !out_v || !aligned(out_k, 16) || !aligned(out_v, 16))
         return fail(VW_ERR_INVALID_ARG, "vw_kv_gather: bad output pointers");
     if (pool->geom.kv_kind == kFP8 && (!out_k_scales || !out_v_scales))

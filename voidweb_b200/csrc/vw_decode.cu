@@ -61,6 +61,9 @@
 #ifndef VW_DECODE_WARPS
 #define VW_DECODE_WARPS 4
 #endif
+#ifndef VW_DECODE_FP8_WARPS
+#define VW_DECODE_FP8_WARPS 4
+#endif
 #ifndef VW_DECODE_CTAS_PER_SM
 #define VW_DECODE_CTAS_PER_SM 2
 #endif
@@ -97,6 +100,7 @@ __device__ unsigned long long g_vw_trace[2 * 1024 * 16];
 namespace {
 
 constexpr int kConsumerWarps = VW_DECODE_WARPS;
+constexpr int kFp8ConsumerWarps = VW_DECODE_FP8_WARPS;
 constexpr int kCtasPerSm = VW_DECODE_CTAS_PER_SM;
 // Issuing lanes per producer warp, and producer warps.  The lanes of one warp
 // that issue copies with different operands run them one after another, so an
@@ -120,7 +124,9 @@ __host__ __device__ constexpr int gcd_c(int a, int b) { return b == 0 ? a : gcd_
 template <int D_, int NT_, int KV_, int IO_>
 struct Traits {
     static constexpr int D = D_, NT = NT_, KV = KV_, IO = IO_;
-    static constexpr int W = kConsumerWarps;
+    // FP8 pages with one query-head tile: more consumer warps (the E4M3
+    // expansion makes the consumers, not the copies, set the pace)
+    static constexpr int W = (KV_ == kFP8 && NT_ == 1) ? kFp8ConsumerWarps : kConsumerWarps;
     static constexpr int PW = KV_ == kFP8 ? kFp8ProducerWarps : 1;   // producer warps W..W+PW-1
     static constexpr int IPW = KV_ == kFP8 ? kFp8Issuers : kIssuers;  // issuing lanes per producer warp
     static constexpr int NI = PW * IPW;                               // issuers in all
@@ -136,6 +142,10 @@ struct Traits {
     // or f16 x V-scale (2^-11) probability puts outputs whose few large V terms
     // cancel outside max-abs 2e-3 / rel 1e-2; f16 pools keep a single f16 P
     static constexpr bool PSPLIT = KV == kBF16 || KV == kFP8;
+    // FP8 pages: the V codes are read after the softmax (not with the K codes)
+    // when registers are short -- two query-head tiles, or more than four
+    // consumer warps -- so that the K and V codes are never live together
+    static constexpr bool LATE_V = KV == kFP8 && (NT != 1 || W > 4);
     static constexpr int KT = D / 16;                        // k-steps of Q K^T
     static constexpr int MT = D / 16;                        // d-tiles of V^T P^T
     // FP8 merge rows of D + 4 floats: a warp's stores of its O^T fragments
@@ -755,15 +765,16 @@ struct Fp8Codes {
     uint4 k[2][2], v[2][2];     // [token row g, g+8][16-B unit]
 };
 
-__device__ __forceinline__ void load_fp8_codes(const uint8_t* st, int lane, Fp8Codes& f) {
+// kv = 0: the K rows (stage rows 0-15) into f.k; kv = 1: the V rows into f.v.
+__device__ __forceinline__ void load_fp8_codes(const uint8_t* st, int lane, int kv, Fp8Codes& f) {
     const int g = lane >> 2, c = lane & 3;
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int off = (g + 8 * rr) * 128 + (((2 * c + hh) ^ g) << 4);
-            f.k[rr][hh] = *reinterpret_cast<const uint4*>(st + off);
-            f.v[rr][hh] = *reinterpret_cast<const uint4*>(st + 16 * 128 + off);
+            if (kv == 0) f.k[rr][hh] = *reinterpret_cast<const uint4*>(st + off);
+            else f.v[rr][hh] = *reinterpret_cast<const uint4*>(st + 16 * 128 + off);
         }
 }
 
@@ -920,12 +931,16 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             Fp8Codes fc;
             if constexpr (T::KV == kFP8) {
                 // this lane's codes and scales are all the page-head it needs:
-                // the stage goes back to the producer before any math
+                // the stage goes back to the producer before any math, or, with
+                // LATE_V, after the V codes are read following the softmax
                 ks0 = sc[t0] * 256.0f; ks1 = sc[t1] * 256.0f;
                 vs0 = sc[16 + t0]; vs1 = sc[16 + t1];
-                load_fp8_codes(st, lane, fc);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.empty[s]);
+                load_fp8_codes(st, lane, 0, fc);
+                if constexpr (!T::LATE_V) {
+                    load_fp8_codes(st, lane, 1, fc);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.empty[s]);
+                }
             }
 
             // ---- S^T = K Q^T  (16 tokens x 8*NT heads), two independent chains
@@ -1022,6 +1037,11 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             }
 
             // ---- O^T += V^T P^T  (D x 8*NT); V is stage rows 16-31
+            if constexpr (T::LATE_V) {
+                load_fp8_codes(st, lane, 1, fc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.empty[s]);
+            }
 #pragma unroll
             for (int mt = 0; mt < T::MT; ++mt) {
                 uint32_t a0, a1, a2, a3;

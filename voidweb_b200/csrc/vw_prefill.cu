@@ -68,24 +68,39 @@ __device__ __forceinline__ int pf_find(const int* pfx, int B, int x) {
     return lo;
 }
 
-// Largest b with cu_q[b] <= i, reading the offsets from global memory.
-__device__ __forceinline__ int pf_find_global(const int32_t* cu_q, int B, int i) {
-    int lo = 0, hi = B - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (__ldg(cu_q + mid) <= i) lo = mid; else hi = mid - 1;
+// Largest b in [0, B) with cu_q[b] <= i (cu_q non-decreasing, cu_q[0] <= i),
+// by the whole warp: each round the 32 lanes probe 32 evenly spaced offsets of
+// the remaining range at once and keep the bracket the last true probe starts,
+// so B <= 32 takes one round of loads and B <= 1024 two (a binary search by
+// one lane is a chain of log2(B) dependent loads).  Every lane gets the result.
+__device__ __forceinline__ int pf_find_warp(const int32_t* cu_q, int B, int i, int lane) {
+    int lo = 0, n = B;
+    while (n > 1) {
+        const int step = (n + 31) / 32;
+        const int idx = lo + lane * step;
+        const bool ok = idx < lo + n && __ldg(cu_q + idx) <= i;
+        const uint32_t m = __ballot_sync(0xffffffffu, ok);      // lanes 0 .. k (monotone)
+        const int k = 31 - __clz((int)m);                         // lane 0 is always true
+        const int nlo = lo + k * step;
+        n = min(step, lo + n - nlo);
+        lo = nlo;
     }
     return lo;
 }
 
 // ------------------------------------------------------------------ append
 
-// One warp per (token i, KV head h): the K and V rows of the token go to slot
+// One warp per token i: its K and V rows of every KV head go to slot
 // block_tables[b][p/16]*16 + p%16, p = ctx_start[b] + i - cu_q[b] (the paging
-// rule of flash_attention.bm:132-140).  With rope_theta > 0 the K row is rotated
-// at position p first (lane l holds elements l*D/32 .. +D/32-1, whose partners
+// rule of flash_attention.bm:132-140).  The token's sequence, position and
+// block are resolved once for all its heads, and the rows of four heads are
+// loaded before any is stored, so a warp keeps eight rows in flight behind one
+// chain of dependent lookups.  With rope_theta > 0 the K row is rotated at
+// position p first (lane l holds elements l*D/32 .. +D/32-1, whose partners
 // d +- D/2 lane l ^ 16 holds), rounded to the io type as a separate RoPE pass
 // would.  FP8 pools quantise each row with its own scale (the decode's codec).
+constexpr uint32_t kAppendHeadGroup = 4;
+
 __global__ void __launch_bounds__(256) prefill_append_kernel(
     PoolGeom g, uint8_t* __restrict__ data, float* __restrict__ scales, uint32_t layer,
     const uint16_t* __restrict__ k_new, const uint16_t* __restrict__ v_new,
@@ -93,13 +108,10 @@ __global__ void __launch_bounds__(256) prefill_append_kernel(
     const uint32_t* __restrict__ block_tables, uint32_t bt_stride, uint32_t B, uint32_t T,
     float rope_theta, uint32_t* err) {
     const uint32_t lane = threadIdx.x & 31;
-    const uint64_t w = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (w >= (uint64_t)T * g.num_kv_heads) return;
-    const uint32_t h = (uint32_t)(w % g.num_kv_heads);
-    const int i = (int)(w / g.num_kv_heads);
-    if (i >= __ldg(cu_q + B)) return;                  // past the last chunk
-    const int b = pf_find_global(cu_q, (int)B, i);
-    const int p = __ldg(ctx_start + b) + (i - __ldg(cu_q + b));
+    const uint32_t i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // token (T <= 2^24)
+    if (i >= T || (int)i >= __ldg(cu_q + B)) return;      // past the last chunk
+    const int b = pf_find_warp(cu_q, (int)B, (int)i, (int)lane);
+    const int p = __ldg(ctx_start + b) + ((int)i - __ldg(cu_q + b));
     if (p < 0 || p >= (int)(bt_stride * kBlockSize)) {
         if (lane == 0) atomicOr(err, kDevErrSeqLen);
         return;
@@ -110,50 +122,70 @@ __global__ void __launch_bounds__(256) prefill_append_kernel(
         return;
     }
     const uint32_t D = g.head_dim, PER = D / 32;       // 2 (D=64) or 4 (D=128) elements per lane
+    const uint32_t Hkv = g.num_kv_heads;
     const float pos = (float)p;
-    for (uint32_t kv = 0; kv < 2; ++kv) {
-        const uint16_t* src = (kv == 0 ? k_new : v_new) + ((size_t)i * g.num_kv_heads + h) * D + lane * PER;
-        uint32_t w2[2] = {0u, 0u};
-        w2[0] = *reinterpret_cast<const uint32_t*>(src);
-        if (PER == 4) w2[1] = *reinterpret_cast<const uint32_t*>(src + 2);
-        if (kv == 0 && rope_theta > 0.0f) {
-            const bool lo = lane < 16;
-            for (uint32_t k = 0; k < PER / 2; ++k) {
-                const uint32_t own = w2[k];
-                const uint32_t other = __shfl_xor_sync(0xffffffffu, own, 16);
-                const uint32_t rw = lo ? own : other, iw = lo ? other : own;
-                float r0 = g.io_kind == kBF16 ? bf16_bits_to_f32(rw & 0xFFFFu) : f16_bits_to_f32(rw & 0xFFFFu);
-                float i0 = g.io_kind == kBF16 ? bf16_bits_to_f32(iw & 0xFFFFu) : f16_bits_to_f32(iw & 0xFFFFu);
-                float r1 = g.io_kind == kBF16 ? bf16_bits_to_f32(rw >> 16) : f16_bits_to_f32(rw >> 16);
-                float i1 = g.io_kind == kBF16 ? bf16_bits_to_f32(iw >> 16) : f16_bits_to_f32(iw >> 16);
-                const int d = (int)((lane & 15) * PER + 2 * k);
-                rope_pair(r0, i0, d, (int)D, rope_theta, pos);
-                rope_pair(r1, i1, d + 1, (int)D, rope_theta, pos);
-                const float a0 = lo ? r0 : i0, a1 = lo ? r1 : i1;
-                const uint32_t b0 = g.io_kind == kBF16 ? f32_to_bf16_bits(a0) : f32_to_f16_bits(a0);
-                const uint32_t b1 = g.io_kind == kBF16 ? f32_to_bf16_bits(a1) : f32_to_f16_bits(a1);
-                w2[k] = b0 | (b1 << 16);
-            }
-        }
-        const uint64_t row = ((((uint64_t)layer * g.num_blocks + blk) * g.num_kv_heads + h) * 2 + kv) *
-                                 kBlockSize + (uint32_t)p % kBlockSize;
-        if (g.kv_kind != kFP8) {
-            uint8_t* dst = data + row * D * 2 + lane * PER * 2;
-            if (PER == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(w2[0], w2[1]);
-            else *reinterpret_cast<uint32_t*>(dst) = w2[0];
-        } else {
-            // FP8 pools have head_dim 128: four elements per lane
-            float v[4];
-            for (int e = 0; e < 4; ++e) {
-                const uint32_t hbits = (w2[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-                v[e] = g.io_kind == kBF16 ? bf16_bits_to_f32(hbits) : f16_bits_to_f32(hbits);
-            }
-            float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    for (uint32_t h0 = 0; h0 < Hkv; h0 += kAppendHeadGroup) {
+        uint32_t w[kAppendHeadGroup][2][2];
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-            const float scale = fp8_row_scale(amax);
-            *reinterpret_cast<uint32_t*>(data + row * D + lane * 4) = fp8_encode4(v, scale, g.fp8_ocp != 0);
-            if (lane == 0) scales[row] = scale;
+        for (uint32_t hh = 0; hh < kAppendHeadGroup; ++hh)
+#pragma unroll
+            for (uint32_t kv = 0; kv < 2; ++kv) {
+                w[hh][kv][0] = w[hh][kv][1] = 0u;
+                if (h0 + hh >= Hkv) continue;
+                const uint16_t* src = (kv == 0 ? k_new : v_new) + ((size_t)i * Hkv + h0 + hh) * D + lane * PER;
+                w[hh][kv][0] = __ldg(reinterpret_cast<const uint32_t*>(src));
+                if (PER == 4) w[hh][kv][1] = __ldg(reinterpret_cast<const uint32_t*>(src + 2));
+            }
+#pragma unroll
+        for (uint32_t hh = 0; hh < kAppendHeadGroup; ++hh) {
+            const uint32_t h = h0 + hh;
+            if (h >= Hkv) break;
+#pragma unroll
+            for (uint32_t kv = 0; kv < 2; ++kv) {
+                uint32_t* w2 = w[hh][kv];
+                if (kv == 0 && rope_theta > 0.0f) {
+                    const bool lo = lane < 16;
+#pragma unroll
+                    for (uint32_t k = 0; k < 2; ++k) {        // PER / 2 words (static indices)
+                        if (k >= PER / 2) break;
+                        const uint32_t own = w2[k];
+                        const uint32_t other = __shfl_xor_sync(0xffffffffu, own, 16);
+                        const uint32_t rw = lo ? own : other, iw = lo ? other : own;
+                        float r0 = g.io_kind == kBF16 ? bf16_bits_to_f32(rw & 0xFFFFu) : f16_bits_to_f32(rw & 0xFFFFu);
+                        float i0 = g.io_kind == kBF16 ? bf16_bits_to_f32(iw & 0xFFFFu) : f16_bits_to_f32(iw & 0xFFFFu);
+                        float r1 = g.io_kind == kBF16 ? bf16_bits_to_f32(rw >> 16) : f16_bits_to_f32(rw >> 16);
+                        float i1 = g.io_kind == kBF16 ? bf16_bits_to_f32(iw >> 16) : f16_bits_to_f32(iw >> 16);
+                        const int d = (int)((lane & 15) * PER + 2 * k);
+                        rope_pair(r0, i0, d, (int)D, rope_theta, pos);
+                        rope_pair(r1, i1, d + 1, (int)D, rope_theta, pos);
+                        const float a0 = lo ? r0 : i0, a1 = lo ? r1 : i1;
+                        const uint32_t b0 = g.io_kind == kBF16 ? f32_to_bf16_bits(a0) : f32_to_f16_bits(a0);
+                        const uint32_t b1 = g.io_kind == kBF16 ? f32_to_bf16_bits(a1) : f32_to_f16_bits(a1);
+                        w2[k] = b0 | (b1 << 16);
+                    }
+                }
+                const uint64_t row = ((((uint64_t)layer * g.num_blocks + blk) * Hkv + h) * 2 + kv) *
+                                         kBlockSize + (uint32_t)p % kBlockSize;
+                if (g.kv_kind != kFP8) {
+                    uint8_t* dst = data + row * D * 2 + lane * PER * 2;
+                    if (PER == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(w2[0], w2[1]);
+                    else *reinterpret_cast<uint32_t*>(dst) = w2[0];
+                } else {
+                    // FP8 pools have head_dim 128: four elements per lane
+                    float v[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t hbits = (w2[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+                        v[e] = g.io_kind == kBF16 ? bf16_bits_to_f32(hbits) : f16_bits_to_f32(hbits);
+                    }
+                    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                    const float scale = fp8_row_scale(amax);
+                    *reinterpret_cast<uint32_t*>(data + row * D + lane * 4) = fp8_encode4(v, scale, g.fp8_ocp != 0);
+                    if (lane == 0) scales[row] = scale;
+                }
+            }
         }
     }
 }
@@ -814,9 +846,8 @@ cudaError_t launch_prefill_append(const PoolGeom& g, uint8_t* data, float* scale
                                   const int32_t* ctx_start, const uint32_t* block_tables,
                                   uint32_t bt_stride, uint32_t B, uint32_t T, float rope_theta,
                                   uint32_t* err, cudaStream_t s) {
-    const uint64_t warps = (uint64_t)T * g.num_kv_heads;
-    if (warps == 0) return cudaSuccess;
-    const uint32_t blocks = (uint32_t)((warps + 7) / 8);
+    if (T == 0) return cudaSuccess;
+    const uint32_t blocks = (T + 7) / 8;                // one warp per token
     prefill_append_kernel<<<blocks, 256, 0, s>>>(g, data, scales, layer,
                                                  static_cast<const uint16_t*>(k_new),
                                                  static_cast<const uint16_t*>(v_new), cu_q, ctx_start,
