@@ -838,6 +838,15 @@ def main():
                     help="run only this many layers of the workload (a small case for ncu "
                          "captures; the JSON line's config.layers says so)")
     args = ap.parse_args()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # set before torch loads NCCL.  The per-step output all-gather overlaps
+        # the next step's decode on a side stream; one NCCL channel keeps its CTA
+        # from taking an SM slot a decode CTA needs (2 B200s: 8909 GB/s with one
+        # channel, 8371 with two).  The communicator's set-up lines (ranks,
+        # NVLink / NVLS paths) go to stderr, so that stdout keeps the JSON line.
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "1")
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     w = dict(WORKLOADS[args.workload])
     if args.layers > 0:
         w["L"] = min(args.layers, w["L"])
@@ -888,13 +897,6 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        # the per-step output all-gather overlaps the next step's decode: two
-        # NCCL channels move 3 MB per rank in time and leave the SMs to the decode
-        os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
-        # the communicator's set-up lines (ranks, NVLink/NVLS paths) go to stderr,
-        # so that stdout keeps the one JSON line
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 

@@ -739,7 +739,15 @@ static int32_t enqueue_step_host(vw_pool* pool, const vw_step_host_args* a, cuda
     if (graph) {
         for (uint32_t n = 1; cut.back() < L; n = cut.size() <= 2 ? 1 : n * 2)
             cut.push_back(std::min(L, cut.back() + n));
-        for (uint32_t l = 1; l <= L; ++l) back.push_back(l);
+        // read-back groups: every layer (default), or (experiment knob
+        // VOIDWEB_KV_STEP_READBACK=n) groups of n layers
+        static const uint32_t group = [] {
+            const char* e = std::getenv("VOIDWEB_KV_STEP_READBACK");
+            const unsigned long v = e ? std::strtoul(e, nullptr, 10) : 1ul;
+            return (uint32_t)(v ? v : 1ul);
+        }();
+        for (uint32_t l = group; l < L; l += group) back.push_back(l);
+        back.push_back(L);
     } else {
         const uint32_t chunks = L < 4 ? L : 4;
         for (uint32_t c = 1; c <= chunks; ++c) cut.push_back(L * c / chunks);

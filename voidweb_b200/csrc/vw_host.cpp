@@ -239,8 +239,18 @@ struct vw_radix {
     }
     void touch(int32_t i) {
         RNode& n = nodes[i];
+        const uint64_t now = ++clock;
+        if (n.in_set && can_evict(i)) {
+            // re-key the set's node in place (no allocation): the newest access
+            // goes last
+            auto nh = evictable.extract({n.last, i});
+            nh.value() = {now, i};
+            evictable.insert(evictable.end(), std::move(nh));
+            n.last = now;
+            return;
+        }
         if (n.in_set) { evictable.erase({n.last, i}); n.in_set = false; }
-        n.last = ++clock;
+        n.last = now;
         refresh(i);
     }
     int32_t child(int32_t i, uint32_t tok) const {
