@@ -426,15 +426,6 @@ struct DecodeScratch {
 //  VOIDWEB_KV_DIRECT_Q=1|0          the first segment's query rows read straight
 //                                   from global memory by the consumer warps
 //                                   (default 1: 4455 -> 4503 GB/s on the Qwen step)
-//  VOIDWEB_KV_L2_AHEAD=n            with early pages: n more pages of the first
-//                                   batch prefetched into L2 before the wait
-uint32_t env_l2_ahead() {
-    static const uint32_t v = [] {
-        const char* e = std::getenv("VOIDWEB_KV_L2_AHEAD");
-        return e ? (uint32_t)std::strtoul(e, nullptr, 10) : 0u;
-    }();
-    return v;
-}
 uint32_t env_decode_flags() {
     static const uint32_t v = [] {
         uint32_t f = 0;
@@ -487,7 +478,6 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
         // from the ring), so the first wait of every consumer warp runs out
         p.flags = (p.flags | kDecodeWithholdQ) & ~kDecodeDirectQ;
     }
-    p.l2_ahead = env_l2_ahead();
     L.tmap = &pool->tmap;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;

@@ -118,6 +118,16 @@ constexpr int kSmemPerCta = (233472 / kCtasPerSm) - 1024;
 constexpr int kStageColumn = 4096;
 constexpr float kRescaleThreshold = 8.0f;             // log2 units: p <= 2^8 vs a stale max
 
+// E4M3 pair -> f16 pair for the MMA fragments: the bit-trick expansion
+// (value / 256) or, with VW_FP8_HW_CVT, the hardware conversion (value).
+#ifdef VW_FP8_HW_CVT
+constexpr float kFp8Fold = 1.0f;
+__device__ __forceinline__ uint32_t fp8_expand(uint32_t w, int sel) { return fp8x2_to_f16x2_hw(w, sel); }
+#else
+constexpr float kFp8Fold = 256.0f;
+__device__ __forceinline__ uint32_t fp8_expand(uint32_t w, int sel) { return fp8x2_to_f16x2_scaled(w, sel); }
+#endif
+
 __host__ __device__ constexpr int align_up_c(int x, int a) { return (x + a - 1) / a * a; }
 __host__ __device__ constexpr int gcd_c(int a, int b) { return b == 0 ? a : gcd_c(b, a % b); }
 
@@ -176,7 +186,7 @@ struct Traits {
     static constexpr int SMEM = 1024 + S * STAGE + align_up_c(S * SCAL, 1024) + FIXED;
     // FP8: probabilities carry the V scale but not the 1/256 of the f16 code
     // expansion; the output is multiplied back by 256
-    static constexpr float VFOLD = KV == kFP8 ? 256.0f : 1.0f;
+    static constexpr float VFOLD = KV == kFP8 ? kFp8Fold : 1.0f;
     // Register budget: the f16/bf16 kernels with one query-head tile fit in 128
     // registers (the bound of 3 CTAs' worth of threads), which leaves every SM
     // sub-partition room for the single-warp combine CTAs that wait beside the
@@ -471,13 +481,6 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     if (lane < T::IPW)
         for (int j = k_me; j < early_n; j += T::NI) issue_page(j, mine[j]);
     if (early_n > 0 && pw == 0) {
-        // pages of the first batch past the ring: into L2 while the predecessor
-        // drains, so their copies after the wait hit L2 (p.l2_ahead of them)
-        const int ahead_end = min(min(32, n), early_n + (int)p.l2_ahead);
-        for (int j = early_n + lane; j < ahead_end; j += 32) {
-            const PageInfo pj = mine[j];
-            if (pj.row0 >= 0) bulk_prefetch_l2(p.kv_data + (size_t)pj.row0 * T::ROW, T::STAGE);
-        }
         // warm L2 with the query tiles (and new K/V rows) of the first batch's
         // segments: the predecessor may still write them, but L2 is where that
         // write lands, so the bulk copies after the wait find them there anyway
@@ -933,7 +936,7 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 // this lane's codes and scales are all the page-head it needs:
                 // the stage goes back to the producer before any math, or, with
                 // LATE_V, after the V codes are read following the softmax
-                ks0 = sc[t0] * 256.0f; ks1 = sc[t1] * 256.0f;
+                ks0 = sc[t0] * kFp8Fold; ks1 = sc[t1] * kFp8Fold;
                 vs0 = sc[16 + t0]; vs1 = sc[16 + t1];
                 load_fp8_codes(st, lane, 0, fc);
                 if constexpr (!T::LATE_V) {
@@ -954,8 +957,8 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 uint32_t a0, a1, a2, a3;
                 if constexpr (T::KV == kFP8) {
                     const uint32_t w0 = run_word(fc.k[0], kt), w1 = run_word(fc.k[1], kt);
-                    a0 = fp8x2_to_f16x2_scaled(w0, 0); a1 = fp8x2_to_f16x2_scaled(w1, 0);
-                    a2 = fp8x2_to_f16x2_scaled(w0, 1); a3 = fp8x2_to_f16x2_scaled(w1, 1);
+                    a0 = fp8_expand(w0, 0); a1 = fp8_expand(w1, 0);
+                    a2 = fp8_expand(w0, 1); a3 = fp8_expand(w1, 1);
                 } else {
                     const uint32_t addr = tbase + (kt >> 2) * kStageColumn + k_tok * 128 +
                                           ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4);
@@ -1047,10 +1050,10 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 uint32_t a0, a1, a2, a3;
                 if constexpr (T::KV == kFP8) {
                     const uint32_t w0 = run_word(fc.v[0], mt), w1 = run_word(fc.v[1], mt);
-                    a0 = movmatrix_t(fp8x2_to_f16x2_scaled(w0, 0));
-                    a1 = movmatrix_t(fp8x2_to_f16x2_scaled(w0, 1));
-                    a2 = movmatrix_t(fp8x2_to_f16x2_scaled(w1, 0));
-                    a3 = movmatrix_t(fp8x2_to_f16x2_scaled(w1, 1));
+                    a0 = movmatrix_t(fp8_expand(w0, 0));
+                    a1 = movmatrix_t(fp8_expand(w0, 1));
+                    a2 = movmatrix_t(fp8_expand(w1, 0));
+                    a3 = movmatrix_t(fp8_expand(w1, 1));
                 } else {
                     const uint32_t addr = tbase + (mt >> 2) * kStageColumn + (16 + v_tok) * 128 +
                                           ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4);

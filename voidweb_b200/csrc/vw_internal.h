@@ -32,7 +32,6 @@ struct DecodeParams {
     float rope_theta;           // > 0: rotate q and the new K row (RoPE) at position seq_len-1
     uint32_t flags;             // kDecodePdl | kDecodeEarlyPages | kDecodePlanned
     uint64_t wait_cycles;       // bound of the device waits in SM cycles (0: kWaitDeadlineCycles)
-    uint32_t l2_ahead;          // with early pages: first-batch pages past the ring prefetched into L2
 };
 
 constexpr uint32_t kDecodePdl = 0x1u;
