@@ -838,13 +838,17 @@ def main():
                     help="run only this many layers of the workload (a small case for ncu "
                          "captures; the JSON line's config.layers says so)")
     args = ap.parse_args()
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if world_env > 1:
         # set before torch loads NCCL.  The per-step output all-gather overlaps
-        # the next step's decode on a side stream; one NCCL channel keeps its CTA
-        # from taking an SM slot a decode CTA needs (2 B200s: 8909 GB/s with one
-        # channel, 8371 with two).  The communicator's set-up lines (ranks,
-        # NVLink / NVLS paths) go to stderr, so that stdout keeps the JSON line.
-        os.environ.setdefault("NCCL_MAX_NCHANNELS", "1")
+        # the next step's decode on a side stream; every NCCL channel is a CTA
+        # that can take an SM slot a decode CTA needs (2 B200s: 8909 GB/s with one
+        # channel, 8371 with two), while the bytes each rank receives per step
+        # grow with the ranks (N - 1 times 3.2 MB on the Qwen step): one channel
+        # up to 2 GPUs, then one per two GPUs.  The communicator's set-up lines
+        # (ranks, NVLink / NVLS paths) go to stderr, so that stdout keeps the
+        # JSON line.
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, world_env // 2)))
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     w = dict(WORKLOADS[args.workload])

@@ -118,15 +118,10 @@ constexpr int kSmemPerCta = (233472 / kCtasPerSm) - 1024;
 constexpr int kStageColumn = 4096;
 constexpr float kRescaleThreshold = 8.0f;             // log2 units: p <= 2^8 vs a stale max
 
-// E4M3 pair -> f16 pair for the MMA fragments: the bit-trick expansion
-// (value / 256) or, with VW_FP8_HW_CVT, the hardware conversion (value).
-#ifdef VW_FP8_HW_CVT
-constexpr float kFp8Fold = 1.0f;
-__device__ __forceinline__ uint32_t fp8_expand(uint32_t w, int sel) { return fp8x2_to_f16x2_hw(w, sel); }
-#else
+// E4M3 pair -> f16 pair for the MMA fragments (value / 256; the 256 is folded
+// into the K scales and the output).
 constexpr float kFp8Fold = 256.0f;
 __device__ __forceinline__ uint32_t fp8_expand(uint32_t w, int sel) { return fp8x2_to_f16x2_scaled(w, sel); }
-#endif
 
 __host__ __device__ constexpr int align_up_c(int x, int a) { return (x + a - 1) / a * a; }
 __host__ __device__ constexpr int gcd_c(int a, int b) { return b == 0 ? a : gcd_c(b, a % b); }

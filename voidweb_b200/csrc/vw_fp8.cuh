@@ -53,21 +53,11 @@ __device__ __forceinline__ float fp8_row_scale(float amax) {
 }
 
 // Codes b0,b1 (bytes 0,1 of w when sel == 0; bytes 2,3 when sel == 1) ->
-// binary16 pair holding decode(b) (unscaled), b0 in the low half, by the
-// hardware E4M3 conversion.  It reads 0x7F / 0xFF as NaN, where the
-// reference decoder has +-480; min(|x|, 480) with x's sign
-// (min.xorsign.abs) maps NaN to +-480 and leaves every finite code, whose
-// magnitude is at most 448, as it is.  Exact for every code the encoders write.
-__device__ __forceinline__ uint32_t fp8x2_to_f16x2_hw(uint32_t w, int sel) {
-    const uint16_t pair = (uint16_t)(sel ? (w >> 16) : (w & 0xFFFFu));
-    uint32_t h, r;
-    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(pair));
-    asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x5F805F80u));
-    return r;
-}
-
-// Codes b0,b1 (bytes 0,1 of w when sel == 0; bytes 2,3 when sel == 1) ->
-// binary16 pair holding decode(b)/256, b0 in the low half.
+// binary16 pair holding decode(b)/256, b0 in the low half: a byte permute, a
+// shift and one three-input logic op.  (The hardware conversion
+// cvt.rn.f16x2.e4m3x2 turns both 0x7F and 0xFF into the same positive NaN, so
+// giving them the reference decoder's +-480 needs a min and the code's sign
+// put back: four instructions per pair instead of three.)
 __device__ __forceinline__ uint32_t fp8x2_to_f16x2_scaled(uint32_t w, int sel) {
     // place b0 in bits 8..15 and b1 in bits 24..31
     uint32_t x = __byte_perm(w, 0u, sel ? 0x3424u : 0x1404u);
