@@ -42,9 +42,9 @@
 //  * FP8 pools.  Pages hold E4M3 codes plus one f32 scale per token per head;
 //    each lane of a consumer warp reads its share of the page's codes from the
 //    stage into registers and expands them into binary16 MMA fragments (the
-//    d order permuted so that a lane's fragments are runs of adjacent codes,
-//    V transposed with movmatrix); the scales fold into the scores and the
-//    probabilities.
+//    d order permuted so that a lane's fragments come from four 16-B loads
+//    per K or V half and need no transpose); the scales fold into the scores
+//    and the probabilities.
 //
 // Every wait is bounded (vw_ptx.cuh); on timeout the kernel records
 // kDevErrTimeout and unwinds after draining its outstanding TMA loads.
@@ -66,6 +66,11 @@
 #endif
 #ifndef VW_DECODE_CTAS_PER_SM
 #define VW_DECODE_CTAS_PER_SM 2
+#endif
+// decode CTAs per SM in a launch's grid (at most the resident count above; a
+// smaller grid leaves slots free for the next launch's CTAs)
+#ifndef VW_DECODE_GRID_PER_SM
+#define VW_DECODE_GRID_PER_SM VW_DECODE_CTAS_PER_SM
 #endif
 #ifndef VW_DECODE_ISSUERS
 #define VW_DECODE_ISSUERS 4
@@ -112,16 +117,15 @@ constexpr int kFp8Issuers = VW_DECODE_FP8_ISSUERS;
 constexpr int kQSlots = 4;                            // query tiles in flight (one per segment)
 constexpr int kMaxStages = VW_DECODE_MAX_STAGES;
 // per-CTA shared memory: an SM holds 228 KB and reserves 1 KB per resident CTA
-constexpr int kSmemPerCta = (233472 / kCtasPerSm) - 1024;
+__host__ __device__ constexpr int smem_per_cta(int ctas) { return 233472 / ctas - 1024; }
 // 2-byte pages feed ldmatrix in place from the stage, [CHUNKS][32 rows][128 B]
 // (column stride 4096 B); FP8 pages are read as codes straight into registers
 constexpr int kStageColumn = 4096;
 constexpr float kRescaleThreshold = 8.0f;             // log2 units: p <= 2^8 vs a stale max
 
-// E4M3 pair -> f16 pair for the MMA fragments (value / 256; the 256 is folded
-// into the K scales and the output).
+// E4M3 codes -> f16 pairs for the MMA fragments hold value / 256; the 256 is
+// folded into the K scales and the output.
 constexpr float kFp8Fold = 256.0f;
-__device__ __forceinline__ uint32_t fp8_expand(uint32_t w, int sel) { return fp8x2_to_f16x2_scaled(w, sel); }
 
 __host__ __device__ constexpr int align_up_c(int x, int a) { return (x + a - 1) / a * a; }
 __host__ __device__ constexpr int gcd_c(int a, int b) { return b == 0 ? a : gcd_c(b, a % b); }
@@ -165,7 +169,11 @@ struct Traits {
     static constexpr int PFX = align_up_c((3 * kMaxBatchPerLaunch + 2) * 4, 128);
     static constexpr int FIXED = align_up_c(MERGE, 1024) +
                                  align_up_c(kQSlots * QSLOT, 1024) + PFX + PW * 1024 + 1024;
-    static constexpr int BUDGET = kSmemPerCta - 1024 /* base alignment slack */ -
+    // resident CTAs per SM the shared memory is sized for: FP8 pages and two
+    // query-head tiles need the larger stages and registers of two
+    static constexpr int RES = (NT == 1 && KV != kFP8) ? kCtasPerSm : 2;
+    static constexpr int SMEM_CAP = smem_per_cta(RES);
+    static constexpr int BUDGET = SMEM_CAP - 1024 /* base alignment slack */ -
                                   (SCAL ? 1024 : 0) /* scale ring alignment */;
     // Stage count: as many as fit, rounded down to a multiple of the consumer
     // warps and of the issuers.  Page i lives in stage i % S, is issued by
@@ -191,7 +199,7 @@ struct Traits {
     static_assert(S >= 4, "too few pipeline stages");
     static_assert(S % W == 0 && S % NI == 0, "stage ownership needs S % W == S % issuers == 0");
     static_assert(32 % NI == 0 && IPW <= 32, "issuers must divide the 32-page batch");
-    static_assert(SMEM <= kSmemPerCta, "shared memory over the per-CTA limit");
+    static_assert(SMEM <= SMEM_CAP, "shared memory over the per-CTA limit");
     static_assert(STAGE % 1024 == 0, "1024-B tile alignment");
 };
 
@@ -620,7 +628,8 @@ __device__ __forceinline__ void merge_unit(const DecodeParams& p, int b, int h, 
 // position pos happens here in registers, rounded to the io type as a separate
 // RoPE pass would.  FP8 pages: k-step kt of lane c = lane%4 holds elements
 // 32c+4kt .. 32c+4kt+3 (the order of the K fragments, see Fp8Codes), so the
-// RoPE partner d +- D/2 of an element is in lane c ^ 2.
+// RoPE partner d +- D/2 of an element is in lane c ^ 2; the rotation runs
+// before the pairs are put in fragment order.
 template <class T>
 __device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qtile, int lane,
                                        float pos, uint32_t (&qf)[T::NT][T::KT][2]) {
@@ -657,7 +666,12 @@ __device__ __forceinline__ void load_q(const DecodeParams& p, const uint8_t* qti
             for (int m = 0; m < 16; ++m) {
                 if constexpr (T::IO == kBF16)       // pages compute in f16
                     w[m] = pack2<false>(bf16_bits_to_f32(w[m] & 0xFFFFu), bf16_bits_to_f32(w[m] >> 16));
-                qf[nt][m >> 1][m & 1] = w[m];
+            }
+            // k-step kt: elements 32c+4kt+1, +3 first, then +0, +2 (the K pairs)
+#pragma unroll
+            for (int kt = 0; kt < T::KT; ++kt) {
+                qf[nt][kt][0] = __byte_perm(w[2 * kt], w[2 * kt + 1], 0x7632u);
+                qf[nt][kt][1] = __byte_perm(w[2 * kt], w[2 * kt + 1], 0x5410u);
             }
         } else {
 #pragma unroll
@@ -749,50 +763,65 @@ __device__ __forceinline__ void zero_tail(uint8_t* stage, int valid, int lane) {
     }
 }
 
-// FP8 page-head fragments, read as codes straight from the stage.  Lane
-// (g = lane/4, c = lane%4) takes the 32 codes 32c .. 32c+31 of token rows g and
-// g+8 of K (stage rows 0-15) and of V (rows 16-31): two 16-B units per row,
-// 128-B swizzled.  The order of the reduction over d inside a k-step of
-// S^T = K Q^T is free, so k-step kt uses codes 4kt .. 4kt+3 of each lane's run
-// (fragment columns 2c+e and 2c+8+e hold d = 32c+4kt+e and 32c+4kt+2+e) and
-// load_q orders the query pairs the same way.  For O^T = V^T P^T the output
-// rows are permuted instead: the code pair j (d = 32c+2j, +1) of rows g and
-// g+8 forms 8x8 blocks that movmatrix transposes into V^T fragments, so row r
-// of d-tile mt of O^T is d = 32*(r%8/2) + 4*mt + 2*(r/8) + r%2 (fp8_out_d).
+// FP8 page-head fragments, read as codes straight from the stage (128-B
+// swizzled rows, 16-B unit u of stage row r at (u ^ (r & 7)) * 16).
+//  * K: lane (g = lane/4, c = lane%4) takes the 32 codes 32c .. 32c+31 of token
+//    rows g and g+8, two 16-B units per row.  The order of the reduction over
+//    d inside a k-step of S^T = K Q^T is free, so k-step kt uses word kt of
+//    each lane's run (codes 32c+4kt .. +3): fragment columns 2c, 2c+1 hold its
+//    odd bytes (d = 32c+4kt+1, +3), columns 2c+8, 2c+9 its even bytes
+//    (d = 32c+4kt, +2), which the expansion reaches without a byte permute;
+//    load_q orders the query pairs the same way.
+//  * V: for O^T = V^T P^T the A fragment of lane (g, c) holds tokens 2c, 2c+1,
+//    2c+8, 2c+9 (the k index is the token, as in the P fragments); the output
+//    rows of each d-tile are free, so row r of d-tile mt is
+//    d = 16*(r%8) + 8*(r/8) + mt (fp8_out_d) and the lane reads 16-B unit g of
+//    its four token rows: every fragment pair is one byte of two of them, with
+//    no transpose.
 struct Fp8Codes {
-    uint4 k[2][2], v[2][2];     // [token row g, g+8][16-B unit]
+    uint4 k[2][2];     // [token row g, g+8][16-B unit 2c, 2c+1]
+    uint4 v[4];        // unit g of token rows 2c, 2c+1, 2c+8, 2c+9
 };
 
 // kv = 0: the K rows (stage rows 0-15) into f.k; kv = 1: the V rows into f.v.
+// Both are conflict-free: the 8 lanes of a 16-B load phase read 8 different
+// units.
 __device__ __forceinline__ void load_fp8_codes(const uint8_t* st, int lane, int kv, Fp8Codes& f) {
     const int g = lane >> 2, c = lane & 3;
+    if (kv == 0) {
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr)
+        for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int off = (g + 8 * rr) * 128 + (((2 * c + hh) ^ g) << 4);
-            if (kv == 0) f.k[rr][hh] = *reinterpret_cast<const uint4*>(st + off);
-            else f.v[rr][hh] = *reinterpret_cast<const uint4*>(st + 16 * 128 + off);
+            for (int hh = 0; hh < 2; ++hh)
+                f.k[rr][hh] = *reinterpret_cast<const uint4*>(st + (g + 8 * rr) * 128 + (((2 * c + hh) ^ g) << 4));
+    } else {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int tok = 2 * c + (r & 1) + 8 * (r >> 1);
+            f.v[r] = *reinterpret_cast<const uint4*>(st + (16 + tok) * 128 + ((g ^ (tok & 7)) << 4));
         }
+    }
 }
 
-// Word i (0..7) of a lane's 32-byte run held as two uint4.
-__device__ __forceinline__ uint32_t run_word(const uint4 (&u)[2], int i) {
-    const uint4& h = u[i >> 2];
-    const int k = i & 3;
+__device__ __forceinline__ uint32_t word_of(const uint4& h, int k) {
     return k == 0 ? h.x : k == 1 ? h.y : k == 2 ? h.z : h.w;
 }
 
+// Word i (0..7) of a lane's 32-byte run held as two uint4.
+__device__ __forceinline__ uint32_t run_word(const uint4 (&u)[2], int i) { return word_of(u[i >> 2], i & 3); }
+
 __host__ __device__ __forceinline__ int fp8_out_d(int r, int mt) {
-    return 32 * ((r & 7) >> 1) + 4 * mt + 2 * (r >> 3) + (r & 1);
+    return 16 * (r & 7) + 8 * (r >> 3) + mt;
 }
 
 // Column of output element d in a merge row.  The FP8 fragments put d values
-// 32 apart in one store; flipping bits 1-2 of d by its 32-block keeps them on
-// different banks (a permutation inside each block of 32).
+// 16 apart in one store (lanes g = 0..7); flipping bits 0-2 of d by bits 4-6
+// spreads them over the banks, and with the rows of D + 4 floats of the four
+// query-head pairs a store's 32 lanes meet 32 different banks (a permutation
+// inside each block of 16).
 template <class T>
 __device__ __forceinline__ int merge_col(int d) {
-    return T::KV == kFP8 ? d ^ (((d >> 5) & 3) << 1) : d;
+    return T::KV == kFP8 ? d ^ ((d >> 4) & 7) : d;
 }
 
 template <class T>
@@ -952,8 +981,8 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 uint32_t a0, a1, a2, a3;
                 if constexpr (T::KV == kFP8) {
                     const uint32_t w0 = run_word(fc.k[0], kt), w1 = run_word(fc.k[1], kt);
-                    a0 = fp8_expand(w0, 0); a1 = fp8_expand(w1, 0);
-                    a2 = fp8_expand(w0, 1); a3 = fp8_expand(w1, 1);
+                    a0 = fp8_pair_odd(w0); a1 = fp8_pair_odd(w1);
+                    a2 = fp8_pair_even(w0); a3 = fp8_pair_even(w1);
                 } else {
                     const uint32_t addr = tbase + (kt >> 2) * kStageColumn + k_tok * 128 +
                                           ((((kt & 3) * 2 + k_hs) ^ (k_tok & 7)) << 4);
@@ -1044,11 +1073,12 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             for (int mt = 0; mt < T::MT; ++mt) {
                 uint32_t a0, a1, a2, a3;
                 if constexpr (T::KV == kFP8) {
-                    const uint32_t w0 = run_word(fc.v[0], mt), w1 = run_word(fc.v[1], mt);
-                    a0 = movmatrix_t(fp8_expand(w0, 0));
-                    a1 = movmatrix_t(fp8_expand(w0, 1));
-                    a2 = movmatrix_t(fp8_expand(w1, 0));
-                    a3 = movmatrix_t(fp8_expand(w1, 1));
+                    // byte mt of unit g: d = 16g + mt (rows g) and 16g + 8 + mt (rows g + 8)
+                    const int lo = mt >> 2, hi = 2 + (mt >> 2), j = mt & 3;
+                    a0 = fp8_pair_cross(word_of(fc.v[0], lo), word_of(fc.v[1], lo), j);
+                    a1 = fp8_pair_cross(word_of(fc.v[0], hi), word_of(fc.v[1], hi), j);
+                    a2 = fp8_pair_cross(word_of(fc.v[2], lo), word_of(fc.v[3], lo), j);
+                    a3 = fp8_pair_cross(word_of(fc.v[2], hi), word_of(fc.v[3], hi), j);
                 } else {
                     const uint32_t addr = tbase + (mt >> 2) * kStageColumn + (16 + v_tok) * 128 +
                                           ((((mt & 3) * 2 + v_hs) ^ (v_tok & 7)) << 4);
@@ -1454,7 +1484,9 @@ cudaError_t launch_d(const DecodeLaunch& L) {
 
 }  // namespace
 
-int decode_ctas_per_sm() { return kCtasPerSm; }
+static_assert(VW_DECODE_GRID_PER_SM >= 1 && VW_DECODE_GRID_PER_SM <= VW_DECODE_CTAS_PER_SM,
+              "grid CTAs per SM must be resident together");
+int decode_ctas_per_sm() { return VW_DECODE_GRID_PER_SM; }
 size_t decode_scratch_floats_o(int grid, int head_dim) { return (size_t)grid * 2 * 16 * head_dim; }
 size_t decode_scratch_floats_ml(int grid) { return (size_t)grid * 2 * 16 * 2; }
 

@@ -64,4 +64,22 @@ __device__ __forceinline__ uint32_t fp8x2_to_f16x2_scaled(uint32_t w, int sel) {
     return ((x >> 1) & 0x3F803F80u) | (x & 0x80008000u);
 }
 
+// The same expansion without a byte permute where the codes already sit in
+// bytes 1 and 3: codes b1,b3 of w -> pair (b1 low, b3 high), a shift and a
+// three-input logic op.  Bytes 0 and 2 do not reach the result.
+__device__ __forceinline__ uint32_t fp8_pair_odd(uint32_t w) {
+    return ((w >> 1) & 0x3F803F80u) | (w & 0x80008000u);
+}
+
+// Codes b0,b2 of w -> pair (b0 low, b2 high).
+__device__ __forceinline__ uint32_t fp8_pair_even(uint32_t w) {
+    return ((w << 7) & 0x3F803F80u) | ((w << 8) & 0x80008000u);
+}
+
+// Byte j of wa (low half) and byte j of wb (high half): one permute that puts
+// them in bytes 1 and 3, then fp8_pair_odd.
+__device__ __forceinline__ uint32_t fp8_pair_cross(uint32_t wa, uint32_t wb, int j) {
+    return fp8_pair_odd(__byte_perm(wa, wb, (uint32_t)(((4 + j) << 12) | (j << 4))));
+}
+
 }  // namespace vw
