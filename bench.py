@@ -44,6 +44,9 @@ WORKLOADS = {
                            kv="f16", io="f16", seed=0),
     "llama3-8b-fp8-b64": dict(L=32, Hq=32, Hkv=8, D=128, B=64, ctx=("loguniform", 1024, 32768),
                               kv="fp8", io="bf16", seed=3),
+    # the FP8 batch with bf16 pages: the same page walk with 8 KB page-heads
+    "llama3-8b-bf16-b64": dict(L=32, Hq=32, Hkv=8, D=128, B=64, ctx=("loguniform", 1024, 32768),
+                               kv="bf16", io="bf16", seed=3),
     "llama3-70b-1kvhead-b256": dict(L=80, Hq=8, Hkv=1, D=128, B=256, ctx=("uniform", 2048, 8192),
                                     kv="bf16", io="bf16", seed=4),
     # chunked prefill (vw_paged_prefill): B sequences, each a `chunk`-token chunk
