@@ -830,7 +830,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: every GPU brings the workload's batch; strong: one batch split across the GPUs")
-    ap.add_argument("--placement", default="sequences", choices=["sequences", "kv_heads"],
+    ap.add_argument("--placement", default="sequences", choices=["sequences", "kv_heads", "kv_heads_seqs"],
                     help="N GPUs: sequences = each GPU its own sequences (every KV head); kv_heads = "
                          "every GPU the same sequences and block tables with its own KV heads "
                          "(the workload's kv_heads per GPU: Llama-3-70B one KV head per GPU)")
@@ -914,7 +914,23 @@ def main():
     heads_split = args.placement == "kv_heads"
     if heads_split and args.scaling == "strong":
         raise SystemExit("--placement kv_heads is a weak-scaling placement (one KV head per GPU)")
-    if args.scaling == "strong":
+    seq_slice = rank            # which sequence slice (and block-table draw) this rank holds
+    head_groups = 1
+    if args.placement == "kv_heads_seqs":
+        # the one batch of the 1-GPU run cut into KV-head groups x sequence slices
+        # (Qwen2.5-7B on 8 GPUs: one KV head and 8 sequences per GPU)
+        if args.scaling != "strong":
+            raise SystemExit("--placement kv_heads_seqs splits the 1-GPU batch: use --scaling strong")
+        from voidweb_b200.shard import ShardPlan
+        plan = ShardPlan("kv_heads_seqs", world, rank, B, Hq, Hkv)
+        s0, s1 = plan.seqs()
+        h0, h1 = plan.kv_heads()
+        g0, g1 = plan.q_heads()
+        ctx = ctx_lengths(w, 0)[s0:s1]
+        B, Hkv, Hq = s1 - s0, h1 - h0, g1 - g0
+        w = dict(w, B=B, Hkv=Hkv, Hq=Hq)
+        seq_slice, head_groups = rank % plan.seq_groups, plan.head_groups
+    elif args.scaling == "strong":
         # one fixed batch (the 1-GPU workload's seeded contexts) split across the ranks
         if B % world:
             raise SystemExit(f"--scaling strong needs the batch ({B}) divisible by the GPUs ({world})")
@@ -933,7 +949,7 @@ def main():
     pages = (seq_lens + 15) // 16
     NB = int(pages.sum()) + 64
     # kv_heads: the same block ids on every rank (the bookkeeping is replicated)
-    rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919 + (0 if heads_split else rank)))
+    rng = np.random.Generator(np.random.PCG64(w["seed"] * 7919 + (0 if heads_split else seq_slice)))
     perm = rng.permutation(NB)
     stride = int(pages.max())
     bt = np.zeros((B, stride), dtype=np.int32)
@@ -1070,8 +1086,9 @@ def main():
         total_launch_bytes = float(t.item())
         tb = torch.tensor([float(B)], device=dev, dtype=torch.float64)
         dist.all_reduce(tb, op=dist.ReduceOp.SUM)
-        # kv_heads: the ranks advance the same sequences (each its own heads)
-        total_seqs = float(B) if heads_split else float(tb.item())
+        # kv_heads: the ranks advance the same sequences (each its own heads);
+        # kv_heads_seqs: each head group advances the whole batch
+        total_seqs = float(B) if heads_split else float(tb.item()) / head_groups
     else:
         total_launch_bytes, total_seqs = float(bytes_launch), float(B)
     step_bytes_all = total_launch_bytes * L
@@ -1207,8 +1224,9 @@ def main():
             "config": {"workload": args.workload, "layers": L, "q_heads": Hq, "kv_heads": Hkv,
                        "head_dim": D, "seqs_per_gpu": B, "seqs_total": int(total_seqs), "ctx": list(w["ctx"]),
                        "block_size": 16, "kv_dtype": w["kv"],
-                       "parallelism": (f"{'kv-head' if heads_split else 'sequence'}-shard x{world}"
-                                       if world > 1 else "single"),
+                       "parallelism": ({"sequences": "sequence", "kv_heads": "kv-head",
+                                        "kv_heads_seqs": "kv-head x sequence"}[args.placement] +
+                                       f"-shard x{world}" if world > 1 else "single"),
                        "placement": args.placement,
                        "l2": f"inputs larger than L2 ({bytes_launch * L / 1e9:.2f} GB of KV "
                              f"per step per GPU vs {L2_BYTES / 1e6:.0f} MB L2)",

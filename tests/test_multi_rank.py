@@ -1,5 +1,5 @@
-"""The N>1 placement logic on CPU: two gloo ranks, each running the oracle on
-its shard (append + decode + a block-copy list), must reproduce the
+"""The N>1 placement logic on CPU: two (or four) gloo ranks, each running the
+oracle on its shard (append + decode + a block-copy list), must reproduce the
 single-process result bit for bit once the shards are gathered."""
 import os
 import socket
@@ -21,8 +21,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _case(kv):
-    return kvgen.make_case(77 + kv, 2, 4, 128, 16, 7, 1, 400, kv, BF16)
+def _case(kv, hkv=4):
+    return kvgen.make_case(77 + kv, 2, hkv, 128, 4 * hkv, 7, 1, 400, kv, BF16)
 
 
 def _full_result(c, pairs):
@@ -38,14 +38,14 @@ def _full_result(c, pairs):
     return np.stack(outs), data, scales
 
 
-def _rank_main(rank, world, port, mode, kv):
+def _rank_main(rank, world, port, mode, kv, hkv=4):
     import torch.distributed as dist
     from voidweb_b200.shard import ShardPlan, gather_outputs
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        c = _case(kv)
+        c = _case(kv, hkv)
         pairs = np.array([[int(c.block_tables[0, 0]), c.NB - 1]], dtype=np.uint32)
         plan = ShardPlan(mode, world, rank, c.B, c.Hq, c.Hkv)
         s0, s1 = plan.seqs()
@@ -86,7 +86,7 @@ def _rank_main(rank, world, port, mode, kv):
             for b in range(s0, s1):
                 p = int(c.seq_lens[b]) - 1
                 blk = int(c.block_tables[b, p // 16])
-                assert np.array_equal(data[:, blk, :, :, p % 16], ref_data[:, blk, :, :, p % 16])
+                assert np.array_equal(data[:, blk, :, :, p % 16], ref_data[:, blk, h0:h1, :, p % 16])
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -96,6 +96,31 @@ def _rank_main(rank, world, port, mode, kv):
 def test_two_rank_shards_match_single_process(mode, kv):
     import torch.multiprocessing as mp
     mp.spawn(_rank_main, args=(2, _free_port(), mode, kv), nprocs=2, join=True)
+
+
+def test_four_rank_heads_and_sequences_match_single_process():
+    """Two head groups of two sequence slices each (2 KV heads on 4 ranks)."""
+    import torch.multiprocessing as mp
+    mp.spawn(_rank_main, args=(4, _free_port(), "kv_heads_seqs", BF16, 2), nprocs=4, join=True)
+
+
+def test_placements_cover_every_segment_once():
+    from voidweb_b200.shard import MODES, ShardPlan
+    for mode in MODES:
+        for world in (1, 2, 4, 8):
+            for hkv in (1, 2, 4, 8):
+                if mode == "kv_heads" and hkv < world:
+                    with pytest.raises(ValueError):
+                        ShardPlan(mode, world, 0, 16, 4 * hkv, hkv)
+                    continue
+                seen = np.zeros((16, hkv), dtype=int)
+                for r in range(world):
+                    p = ShardPlan(mode, world, r, 16, 4 * hkv, hkv)
+                    s0, s1 = p.seqs()
+                    h0, h1 = p.kv_heads()
+                    seen[s0:s1, h0:h1] += 1
+                    assert p.q_heads() == (h0 * 4, h1 * 4)
+                assert (seen == 1).all(), (mode, world, hkv)
 
 
 def test_shard_range_covers_everything():

@@ -13,6 +13,12 @@ data path:
   same block ids (the host block manager and radix tree run replicated, and a
   block-copy list is replayed on every rank).  This is the placement for a
   model too large for one GPU's HBM (Llama-3-70B: one KV head per GPU on 8).
+* ``"kv_heads_seqs"``: both at once, for more ranks than KV heads: the ranks
+  form gcd(world, KV heads) head groups of world / that many ranks each; rank
+  r takes head slice r // seq_groups and sequence slice r % seq_groups
+  (Qwen2.5-7B's 4 KV heads on 8 GPUs: one KV head and half the batch each).
+  Ranks of one head group keep the block ids of their own sequences; the
+  ranks that share a sequence slice keep the same ones.
 
 Outputs stay on the rank that computed them (the next operation of a
 tensor-parallel layer consumes its own heads); ``gather_outputs`` assembles
@@ -21,6 +27,9 @@ the whole [B][Hq][D] tensor when a caller wants it, with one all-gather.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from math import gcd
+
+MODES = ("sequences", "kv_heads", "kv_heads_seqs")
 
 
 def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -35,7 +44,7 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
 
 @dataclass(frozen=True)
 class ShardPlan:
-    mode: str            # "sequences" or "kv_heads"
+    mode: str            # one of MODES
     world: int
     rank: int
     num_seqs: int
@@ -43,7 +52,7 @@ class ShardPlan:
     num_kv_heads: int
 
     def __post_init__(self):
-        if self.mode not in ("sequences", "kv_heads"):
+        if self.mode not in MODES:
             raise ValueError(f"unknown placement {self.mode!r}")
         if self.num_kv_heads <= 0 or self.num_q_heads % self.num_kv_heads:
             raise ValueError("num_q_heads must be a positive multiple of num_kv_heads")
@@ -54,15 +63,25 @@ class ShardPlan:
     def group(self) -> int:
         return self.num_q_heads // self.num_kv_heads
 
+    @property
+    def head_groups(self) -> int:
+        """How many slices the KV heads are cut into."""
+        if self.mode == "kv_heads":
+            return self.world
+        if self.mode == "kv_heads_seqs":
+            return gcd(self.world, self.num_kv_heads)
+        return 1
+
+    @property
+    def seq_groups(self) -> int:
+        """How many slices the batch is cut into."""
+        return self.world // self.head_groups
+
     def seqs(self) -> tuple[int, int]:
-        if self.mode == "sequences":
-            return shard_range(self.num_seqs, self.world, self.rank)
-        return 0, self.num_seqs
+        return shard_range(self.num_seqs, self.seq_groups, self.rank % self.seq_groups)
 
     def kv_heads(self) -> tuple[int, int]:
-        if self.mode == "kv_heads":
-            return shard_range(self.num_kv_heads, self.world, self.rank)
-        return 0, self.num_kv_heads
+        return shard_range(self.num_kv_heads, self.head_groups, self.rank // self.seq_groups)
 
     def q_heads(self) -> tuple[int, int]:
         h0, h1 = self.kv_heads()
@@ -94,25 +113,17 @@ def gather_outputs(plan: ShardPlan, local_out, group=None):
     if world == 1:
         return local_out
     D = local_out.shape[-1]
-    if plan.mode == "sequences":
-        n_max = -(-plan.num_seqs // world)
-        pad = torch.zeros((n_max, plan.num_q_heads, D), dtype=local_out.dtype,
-                          device=local_out.device)
-        pad[:local_out.shape[0]] = local_out
-    else:
-        n_max = -(-plan.num_kv_heads // world) * plan.group
-        pad = torch.zeros((plan.num_seqs, n_max, D), dtype=local_out.dtype,
-                          device=local_out.device)
-        pad[:, :local_out.shape[1]] = local_out
+    n_seq = -(-plan.num_seqs // plan.seq_groups)
+    n_head = -(-plan.num_kv_heads // plan.head_groups) * plan.group
+    pad = torch.zeros((n_seq, n_head, D), dtype=local_out.dtype, device=local_out.device)
+    pad[:local_out.shape[0], :local_out.shape[1]] = local_out
     parts = [torch.empty_like(pad) for _ in range(world)]
     dist.all_gather(parts, pad.contiguous(), group=group)
-    pieces = []
+    out = torch.empty((plan.num_seqs, plan.num_q_heads, D), dtype=local_out.dtype,
+                      device=local_out.device)
     for r in range(world):
         p = ShardPlan(plan.mode, world, r, plan.num_seqs, plan.num_q_heads, plan.num_kv_heads)
-        if plan.mode == "sequences":
-            s0, s1 = p.seqs()
-            pieces.append(parts[r][:s1 - s0])
-        else:
-            g0, g1 = p.q_heads()
-            pieces.append(parts[r][:, :g1 - g0])
-    return torch.cat(pieces, dim=0 if plan.mode == "sequences" else 1)
+        s0, s1 = p.seqs()
+        g0, g1 = p.q_heads()
+        out[s0:s1, g0:g1] = parts[r][:s1 - s0, :g1 - g0]
+    return out
