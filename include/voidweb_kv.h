@@ -431,15 +431,16 @@ VW_API int32_t vw_fault_inject(uint32_t kind, uint32_t count);
 /* Failures of `kind` still armed. */
 VW_API uint32_t vw_fault_pending(uint32_t kind);
 
-/* Test hook for the bounded device waits: the decode launches of this pool
- * give up every wait for a copy or a consumer after `cycles` SM clock cycles
- * from the kernel's start (0 restores the default, about 2 s and the normal
- * launch), and they withhold their query-tile copies, so the consumers' first
- * wait is one that nothing satisfies.  Such a launch records
- * VW_DEV_ERR_TIMEOUT, waits (under the default limit) for the copies it has in
- * flight, and returns; its outputs are undefined.  vw_pool_check clears the
- * word, after which the pool decodes normally.  No counterpart in the
- * reference. */
+/* Test hook for the bounded device waits: the decode and prefill launches of
+ * this pool give up every wait for a copy or a consumer after `cycles` SM
+ * clock cycles from the kernel's start (0 restores the default, about 2 s and
+ * the normal launch), and they withhold copies -- the decode its query tiles,
+ * the prefill its K/V tiles -- so that their first waits are ones that nothing
+ * satisfies.  Such a launch records VW_DEV_ERR_TIMEOUT, waits (under the
+ * default limit) for the copies and tensor-core operations it has in flight,
+ * frees its tensor memory, and returns; its outputs are undefined (a prefill's
+ * chunk append still runs).  vw_pool_check clears the word, after which the
+ * pool runs normally.  No counterpart in the reference. */
 VW_API int32_t vw_debug_set_wait_limit(vw_pool* pool, uint64_t cycles);
 
 /* Number of device (cudaMalloc) and pinned host (cudaHostAlloc) allocations this

@@ -1,12 +1,15 @@
-"""Failure detection on the GPU without a fault: the decode's bounded waits.
+"""Failure detection on the GPU without a fault: the bounded waits of the
+decode and prefill kernels.
 
-Every wait of the decode kernel (for a page copy, a query tile, a free stage)
+Every wait (for a page copy, a query tile, a free stage, a tensor-core result)
 gives up after a deadline; the launch then records VW_DEV_ERR_TIMEOUT, waits
-for the copies it has in flight, and returns, leaving the context usable.  The
-test hook vw_debug_set_wait_limit shortens the deadline to one SM cycle so that
-the first wait runs out; nothing else is changed (no trap, no bad address, no
-endless loop).  The pool must then report the timeout, and after vw_pool_check
-the next normal launch must give the oracle's results."""
+for the copies and MMAs it has in flight, frees its tensor memory, and
+returns, leaving the context usable.  The test hook vw_debug_set_wait_limit
+shortens the deadline to one SM cycle and withholds the copies the first waits
+need (query tiles for the decode, K/V tiles for the prefill), so those waits
+run out; nothing else is changed (no trap, no bad address, no endless loop).
+The pool must then report the timeout, and after vw_pool_check the next normal
+launch must give the oracle's results."""
 import numpy as np
 import pytest
 
@@ -57,4 +60,25 @@ def test_decode_wait_timeout_unwinds_and_pool_recovers(dev, kv, chained):
     ref = oracle.paged_decode_f64(c.geom, data, scales, 0, c.q[0], c.Hq, c.block_tables,
                                   c.seq_lens, 1.0 / np.sqrt(128))
     check_close(got, ref, BF16, f"after timeout kv={kv}")
+    pool.close()
+
+
+@pytest.mark.parametrize("kv", [BF16, FP8])
+def test_prefill_wait_timeout_unwinds_and_pool_recovers(dev, kv):
+    from voidweb_b200 import _lib as C
+    from tests.test_gpu_prefill import chunk_case, run_prefill
+    c, q, k, v, cu, cs = chunk_case(91 + kv, BF16, 128, 8, 2, [(700, 130), (0, 64)], L=1, kv=kv)
+    pool = make_pool(c, dev)
+    pool.set_wait_limit(1)
+    run_prefill(pool, c, 0, q, k, v, cu, cs, dev)
+    err = pool.check()
+    assert err == C.DEV_ERR_TIMEOUT, f"device word 0x{err:x}"
+    pool.set_wait_limit(0)
+    upload_pool(pool, c)
+    got = run_prefill(pool, c, 0, q, k, v, cu, cs, dev)
+    assert pool.check() == 0
+    oracle.kv_append(c.geom, c.data, c.scales, 0, k, v, oracle.prefill_slots(c.block_tables, cu, cs))
+    ref = oracle.paged_prefill_f64(c.geom, c.data, c.scales, 0, q, c.Hq, c.block_tables, cu, cs, True,
+                                   1.0 / np.sqrt(128))
+    check_close(got, ref, BF16, f"prefill after timeout kv={kv}")
     pool.close()

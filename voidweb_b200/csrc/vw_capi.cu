@@ -575,6 +575,7 @@ int32_t vw_paged_prefill(vw_pool* pool, const vw_prefill_args* a, void* stream) 
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt((float)g.head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.rope_theta = theta;
+    p.wait_cycles = pool->wait_cycles;
     L.tmap = &pool->tmap_half;
     L.head_dim = g.head_dim;
     L.kv_kind = g.kv_kind;

@@ -139,8 +139,10 @@ gemm_fp8_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict__ B, ui
                 tc_commit(&empty[s]);
             }
             if (!ok) atomicOr(err, kDevErrTimeout);
+            // every issued MMA completes before the tensor memory is freed; they
+            // finish in bounded time, so the wait has a deadline of its own
             tc_commit(done);
-            if (!mbar_wait(done, 0, deadline)) atomicOr(err, kDevErrTimeout);
+            if (!mbar_wait(done, 0, cycles() + kWaitDeadlineCycles)) atomicOr(err, kDevErrTimeout);
         }
     } else {
         // ---- decoders: thread t takes row t of the A slice and half a row of

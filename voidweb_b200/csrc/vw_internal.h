@@ -88,6 +88,10 @@ struct PrefillParams {
     uint32_t B, T, Hq, Hkv, group, num_blocks, layer, bt_stride, causal, flags;
     float scale_log2;           // softmax scale * log2(e)
     float rope_theta;           // > 0: rotate q at its position (RoPE)
+    // bound of the device waits in SM cycles (0: kWaitDeadlineCycles); when set
+    // (vw_debug_set_wait_limit) the K/V tiles are withheld, so the first waits
+    // are ones that nothing completes and run out
+    uint64_t wait_cycles;
 };
 
 struct PrefillLaunch {

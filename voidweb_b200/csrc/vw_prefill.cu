@@ -375,7 +375,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
     uint64_t* done = p_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t deadline = cycles() + kWaitDeadlineCycles;
+    const uint64_t deadline = cycles() + (p.wait_cycles ? p.wait_cycles : kWaitDeadlineCycles);
+    // test hook (vw_debug_set_wait_limit): no K/V tile is filled, so the MMA
+    // issuer's and the softmax warps' first waits run out
+    const bool withhold = p.wait_cycles != 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::NSTK; ++s) {
@@ -498,7 +501,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         bool ok = true;
         uint32_t nblk[T::R];
         fp8_round_ids<T>(bt, 0, npages, nblk);
-        for (int t = 0; t < nrounds; ++t) {
+        for (int t = 0; t < nrounds && !withhold; ++t) {
             const int st_i = t % T::NST;
             uint32_t blk[T::R];
 #pragma unroll
@@ -539,7 +542,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         uint32_t nwin = 32 + lane < npages ? __ldg(bt + 32 + lane) : 0xFFFFFFFFu;
         bool ok = true;
         int issued = 0;
-        for (int t = 0; t < nrounds; ++t) {
+        for (int t = 0; t < nrounds && !withhold; ++t) {
             const int st_i = t % ns;
             if (t > 0 && t % WIN == 0) {
                 win = nwin;
@@ -572,9 +575,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
         }
         if (lane == 0) {
             if (!ok) atomicOr(p.err, kDevErrTimeout);
-            // drain: no TMA write may land after the CTA has exited
+            // drain: no TMA write may land after the CTA has exited.  The copies
+            // still in flight are this warp's last ns rounds; they land in bounded
+            // time, so the drain has a deadline of its own (the kernel's may have
+            // run out already)
+            const uint64_t drain_deadline = cycles() + kWaitDeadlineCycles;
             for (int t = issued > ns ? issued - ns : 0; t < issued; ++t)
-                if (!mbar_wait(&fbar[t % ns], (t / ns) & 1, deadline)) {
+                if (!mbar_wait(&fbar[t % ns], (t / ns) & 1, drain_deadline)) {
                     atomicOr(p.err, kDevErrTimeout);
                     break;
                 }
@@ -642,9 +649,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillParams p) 
             if (ok && nrounds > 0) ok = issue_pv(nrounds - 1);
             if (!ok) atomicOr(p.err, kDevErrTimeout);
             // every MMA issued here completes before the epilogue reads O and
-            // before the tensor memory is freed
+            // before the tensor memory is freed: the issued MMAs finish in bounded
+            // time, so this wait has a deadline of its own (after a timeout the
+            // kernel's may have run out)
             tc_commit(done);
-            if (!mbar_wait(done, 0, deadline)) atomicOr(p.err, kDevErrTimeout);
+            if (!mbar_wait(done, 0, cycles() + kWaitDeadlineCycles)) atomicOr(p.err, kDevErrTimeout);
         }
     } else {
         // ---- softmax warps: thread r owns query row r
