@@ -830,6 +830,11 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: every GPU brings the workload's batch; strong: one batch split across the GPUs")
+    ap.add_argument("--gather", default="auto", choices=["auto", "overlap", "serial"],
+                    help="N>1: all-gather each step's outputs on a side stream while the next step "
+                         "runs (few NCCL channels), or inside the step's graph after its last layer "
+                         "(NCCL's own channel count); auto: serial from 16 MB of outputs per rank "
+                         "and step")
     ap.add_argument("--placement", default="sequences", choices=["sequences", "kv_heads", "kv_heads_seqs"],
                     help="N GPUs: sequences = each GPU its own sequences (every KV head); kv_heads = "
                          "every GPU the same sequences and block tables with its own KV heads "
@@ -843,6 +848,17 @@ def main():
                          "captures; the JSON line's config.layers says so)")
     args = ap.parse_args()
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gather == "auto":
+        # Measured on B200s: an overlapped gather keeps its NCCL CTAs resident
+        # while the next step runs, and a decode CTA that cannot start beside them
+        # holds back its layer: cheap while the gather is short (Qwen step, 3.2 MB
+        # per rank: 8940 GB/s on 2 GPUs against 8304 serial), costly when it is
+        # long (Llama-3-70B one KV head, 42 MB per rank: 11308 overlapped against
+        # 12065 serial on 2 GPUs, 20948 against 24249 on 4)
+        wl = WORKLOADS[args.workload]
+        out_bytes = (wl.get("L", 0) * wl.get("B", 0) * wl.get("Hq", 0) * wl.get("D", 0) * 2
+                     if "B" in wl else 0)
+        args.gather = "serial" if out_bytes >= 16 << 20 else "overlap"
     if world_env > 1:
         # set before torch loads NCCL.  The per-step output all-gather overlaps
         # the next step's decode on a side stream; every NCCL channel is a CTA
@@ -852,7 +868,8 @@ def main():
         # up to 2 GPUs, then one per two GPUs.  The communicator's set-up lines
         # (ranks, NVLink / NVLS paths) go to stderr, so that stdout keeps the
         # JSON line.
-        os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, world_env // 2)))
+        if args.gather == "overlap":
+            os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, world_env // 2)))
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     w = dict(WORKLOADS[args.workload])
@@ -1011,14 +1028,25 @@ def main():
         step(stream, outs[0])
     stream.synchronize()
     assert pool.check() == 0, "device bounds check tripped"
+    gathered = [torch.empty((world, L, B, Hq, D), device=dev, dtype=iod) for _ in range(2)] \
+        if world > 1 else None
+    serial = world > 1 and args.gather == "serial"
+    if serial:
+        # one eager collective first: the communicator exists before the capture
+        with torch.cuda.stream(stream):
+            dist.all_gather_into_tensor(gathered[0], outs[0])
+        stream.synchronize()
     graphs = []
-    for o in outs:
+    for i, o in enumerate(outs):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             step(torch.cuda.current_stream(), o)
+            if serial:
+                # the step's all-gather, recorded in the step's graph after its last layer
+                dist.all_gather_into_tensor(gathered[i], o)
         graphs.append(g)
-    gathered = [torch.empty((world, L, B, Hq, D), device=dev, dtype=iod) for _ in range(2)] \
-        if world > 1 else None
+    del g       # the graphs hold NCCL work when serial: only `graphs` keeps them, and it is
+                # released before the process group is destroyed
     gather_stream = torch.cuda.Stream(device=dev) if world > 1 else None
     gather_done = [torch.cuda.Event(), torch.cuda.Event()]
     pending = [False, False]
@@ -1030,7 +1058,7 @@ def main():
         if pending[i]:
             stream.wait_event(gather_done[i])    # the gather reading outs[i] has finished
         graphs[i].replay()
-        if world > 1:
+        if world > 1 and not serial:
             ready = torch.cuda.Event()
             ready.record(stream)
             gather_stream.wait_event(ready)
@@ -1233,8 +1261,11 @@ def main():
                        "graph": "one CUDA graph per step: one fused append+decode launch per layer, "
                                 "programmatic dependent launches with early page streaming" +
                                 (", decode plan made once per step" if args.plan else ""),
-                       "gather": (f"NCCL all-gather of each step's outputs on a side stream, overlapping "
-                                  f"the next step (double-buffered outputs)") if world > 1 else None},
+                       "gather": (None if world == 1 else
+                                  "NCCL all-gather of each step's outputs in the step's CUDA graph after "
+                                  "its last layer" if args.gather == "serial" else
+                                  "NCCL all-gather of each step's outputs on a side stream, overlapping "
+                                  "the next step (double-buffered outputs)")},
             "tok_per_s": round(tok_s, 1),
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
