@@ -865,13 +865,12 @@ def main():
         # that can take an SM slot a decode CTA needs (2 B200s: 8909 GB/s with one
         # channel, 8371 with two), while the bytes each rank receives per step
         # grow with the ranks (N - 1 times 3.2 MB on the Qwen step): one channel
-        # up to 2 GPUs, then one per two GPUs.  The communicator's set-up lines
-        # (ranks, NVLink / NVLS paths) go to stderr, so that stdout keeps the
-        # JSON line.
+        # up to 2 GPUs, then one per two GPUs.  (NCCL's set-up lines -- ranks,
+        # NVLink / NVLS paths -- come with NCCL_DEBUG=INFO and an NCCL_DEBUG_FILE
+        # set by the caller; without a file they would go to stdout, which keeps
+        # the JSON line alone.)
         if args.gather == "overlap":
             os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, world_env // 2)))
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     w = dict(WORKLOADS[args.workload])
     if args.layers > 0:
         w["L"] = min(args.layers, w["L"])
