@@ -833,7 +833,7 @@ def main():
     ap.add_argument("--gather", default="auto", choices=["auto", "overlap", "serial"],
                     help="N>1: all-gather each step's outputs on a side stream while the next step "
                          "runs (few NCCL channels), or inside the step's graph after its last layer "
-                         "(NCCL's own channel count); auto: serial from 16 MB of outputs per rank "
+                         "(NCCL's own channel count); auto: serial from 8 MB received per rank "
                          "and step")
     ap.add_argument("--placement", default="sequences", choices=["sequences", "kv_heads", "kv_heads_seqs"],
                     help="N GPUs: sequences = each GPU its own sequences (every KV head); kv_heads = "
@@ -852,13 +852,14 @@ def main():
         # Measured on B200s: an overlapped gather keeps its NCCL CTAs resident
         # while the next step runs, and a decode CTA that cannot start beside them
         # holds back its layer: cheap while the gather is short (Qwen step, 3.2 MB
-        # per rank: 8940 GB/s on 2 GPUs against 8304 serial), costly when it is
-        # long (Llama-3-70B one KV head, 42 MB per rank: 11308 overlapped against
-        # 12065 serial on 2 GPUs, 20948 against 24249 on 4)
+        # received per rank on 2 GPUs: 8940 GB/s against 8304 serial), costly when
+        # it is long (22 MB on 8 GPUs: 26480 against 30995; Llama-3-70B one KV
+        # head, 42 MB on 2 GPUs: 11308 against 12065, 126 MB on 4: 20948 against
+        # 24249).  Serial from 8 MB received per rank and step.
         wl = WORKLOADS[args.workload]
         out_bytes = (wl.get("L", 0) * wl.get("B", 0) * wl.get("Hq", 0) * wl.get("D", 0) * 2
                      if "B" in wl else 0)
-        args.gather = "serial" if out_bytes >= 16 << 20 else "overlap"
+        args.gather = "serial" if (world_env - 1) * out_bytes >= 8 << 20 else "overlap"
     if world_env > 1:
         # set before torch loads NCCL.  The per-step output all-gather overlaps
         # the next step's decode on a side stream; every NCCL channel is a CTA
