@@ -1172,6 +1172,10 @@ def main():
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(ho.numel() * 2),
                "path": "vw_decode_step_host (pinned host buffers; from the second call with "
                        "the same buffers the step replays as one recorded CUDA graph)"}
+        if world > 1:
+            # no device-side gather here: the step's result is each rank's shard of
+            # the outputs in that rank's host memory
+            e2e["outputs"] = "each rank's shard, read back to its own host"
         # the same step through the symbol the engine dlopens: voidweb_forward_pass
         # with the packed descriptors KernelLib.forward_pass builds (engine/ffi.bm:86-121);
         # the bound q / new K / new V / output buffers are the pinned ones above
