@@ -40,6 +40,10 @@ WORKLOADS = {
     # name: layers, q heads, kv heads, head_dim, seqs per GPU, ctx rule, kv / io dtype, seed
     "qwen2.5-7b-decode-b16": dict(L=28, Hq=28, Hkv=4, D=128, B=16, ctx=("uniform", 512, 4096),
                                   kv="bf16", io="bf16", seed=1),
+    # the Qwen batch's pages with 16 query heads per KV head (the two-tile
+    # decode variant): same KV bytes, twice the query heads per page
+    "g16-bf16-b16": dict(L=28, Hq=64, Hkv=4, D=128, B=16, ctx=("uniform", 512, 4096),
+                         kv="bf16", io="bf16", seed=1),
     "plumbing-l1-b8": dict(L=1, Hq=14, Hkv=2, D=64, B=8, ctx=("uniform", 1, 512),
                            kv="f16", io="f16", seed=0),
     "llama3-8b-fp8-b64": dict(L=32, Hq=32, Hkv=8, D=128, B=64, ctx=("loguniform", 1024, 32768),
