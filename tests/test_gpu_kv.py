@@ -84,6 +84,12 @@ DECODE_CASES = [
     ("qwen_bf16_d128_g7", 1, 4, 128, 28, 6, 300, 1500, BF16, BF16),
     ("llama70b_bf16_g8", 1, 2, 128, 16, 5, 100, 900, BF16, BF16),
     ("g16_two_ntiles", 1, 1, 128, 16, 4, 20, 700, BF16, BF16),
+    # two query-head tiles, the second one partly padded (group 12), and the
+    # two-tile variants of the other page types
+    ("g12_bf16_padded_tile", 1, 2, 128, 24, 5, 1, 900, BF16, BF16),
+    ("g16_f16", 1, 2, 128, 32, 4, 20, 700, F16, F16),
+    ("g16_fp8", 1, 1, 128, 16, 4, 20, 900, FP8, BF16),
+    ("g12_fp8_f16io", 1, 2, 128, 24, 3, 1, 600, FP8, F16),
     ("bf16_d64", 1, 3, 64, 12, 7, 1, 300, BF16, BF16),
     ("f16_d128_g4", 1, 2, 128, 8, 6, 1, 800, F16, F16),
     ("fp8_llama8b_g4", 1, 2, 128, 8, 5, 50, 900, FP8, BF16),

@@ -114,7 +114,6 @@ constexpr int kCtasPerSm = VW_DECODE_CTAS_PER_SM;
 constexpr int kIssuers = VW_DECODE_ISSUERS;
 constexpr int kFp8ProducerWarps = VW_DECODE_FP8_PRODUCERS;
 constexpr int kFp8Issuers = VW_DECODE_FP8_ISSUERS;
-constexpr int kQSlots = 4;                            // query tiles in flight (one per segment)
 constexpr int kMaxStages = VW_DECODE_MAX_STAGES;
 // per-CTA shared memory: an SM holds 228 KB and reserves 1 KB per resident CTA
 __host__ __device__ constexpr int smem_per_cta(int ctas) { return 233472 / ctas - 1024; }
@@ -162,13 +161,18 @@ struct Traits {
     // different banks.  2-byte pages keep rows of D (a 4-way conflict measured
     // cheaper than the padded rows).
     static constexpr int MROW = KV == kFP8 ? D + 4 : D;
-    static constexpr int MERGE = W * G * (MROW + 2) * 4 + (W + 2) * G * 4;
+    // the warp states are merged one 8-head tile at a time: [W][8] rows of
+    // MROW + 2 floats (o, max, sum), then [W + 2][8] weights, max and sum
+    static constexpr int MERGE = W * 8 * (MROW + 2) * 4 + (W + 2) * 8 * 4;
     static constexpr int QTILE = G * D * 2;
     static constexpr int QSLOT = QTILE + 2 * D * 2;          // + the new token's K and V rows
+    // query tiles in flight (one per segment); two with two query-head tiles,
+    // whose larger slots would otherwise cost pipeline stages
+    static constexpr int QS = NT == 1 ? 4 : 2;
     // prefixes of pages and of sequences with pages [B+1] each, and the seq_lens [B]
     static constexpr int PFX = align_up_c((3 * kMaxBatchPerLaunch + 2) * 4, 128);
     static constexpr int FIXED = align_up_c(MERGE, 1024) +
-                                 align_up_c(kQSlots * QSLOT, 1024) + PFX + PW * 1024 + 1024;
+                                 align_up_c(QS * QSLOT, 1024) + PFX + PW * 1024 + 1024;
     // resident CTAs per SM the shared memory is sized for: FP8 pages and two
     // query-head tiles need the larger stages and registers of two
     static constexpr int RES = (NT == 1 && KV != kFP8) ? kCtasPerSm : 2;
@@ -215,19 +219,19 @@ struct PageInfo {
 struct Smem {
     uint8_t* stages;     // [S][STAGE]
     float* scal;         // [S][32] FP8 scales (K 16, V 16)
-    float* mo;           // [W][G][MROW]
-    float* mm;           // [W][G]
-    float* ml;           // [W][G]
-    float* mf;           // [W][G] warp weights, then [G] max, [G] sum
-    uint8_t* qring;      // [kQSlots][QSLOT]: [G][D] query rows, then new K, new V rows (io dtype)
+    float* mo;           // [W][8][MROW] one 8-head tile of the warp states
+    float* mm;           // [W][8]
+    float* ml;           // [W][8]
+    float* mf;           // [W][8] warp weights, then [8] max, [8] sum
+    uint8_t* qring;      // [QS][QSLOT]: [G][D] query rows, then new K, new V rows (io dtype)
     int* pfx;            // [B+1] exclusive prefix of pages per sequence
     int* nzp;            // [B+1] exclusive prefix of sequences with pages
     int* slen;           // [B] seq_lens as the prologue read them
     PageInfo* pinfo;     // [PW][2][32] producer batches, one pair per producer warp
     uint64_t* full;      // [S]
     uint64_t* empty;     // [S]
-    uint64_t* qfull;     // [kQSlots]
-    uint64_t* qempty;    // [kQSlots]
+    uint64_t* qfull;     // [QS]
+    uint64_t* qempty;    // [QS]
     int* flag;           // [1] abort marker, [2..4] planned begin, end, first ordinal
 };
 
@@ -238,11 +242,11 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     s.stages = p; p += T::S * T::STAGE;
     s.scal = reinterpret_cast<float*>(p); p += align_up_c(T::S * T::SCAL, 1024);
     s.mo = reinterpret_cast<float*>(p);
-    s.mm = s.mo + T::W * T::G * T::MROW;
-    s.ml = s.mm + T::W * T::G;
-    s.mf = s.ml + T::W * T::G;
+    s.mm = s.mo + T::W * 8 * T::MROW;
+    s.ml = s.mm + T::W * 8;
+    s.mf = s.ml + T::W * 8;
     p += align_up_c(T::MERGE, 1024);
-    s.qring = p; p += align_up_c(kQSlots * T::QSLOT, 1024);
+    s.qring = p; p += align_up_c(T::QS * T::QSLOT, 1024);
     s.pfx = reinterpret_cast<int*>(p);
     s.nzp = s.pfx + (kMaxBatchPerLaunch + 1);
     s.slen = s.nzp + (kMaxBatchPerLaunch + 1);
@@ -251,8 +255,8 @@ __device__ __forceinline__ Smem carve(uint8_t* base) {
     s.full = reinterpret_cast<uint64_t*>(p);
     s.empty = s.full + T::S;
     s.qfull = s.empty + T::S;
-    s.qempty = s.qfull + kQSlots;
-    s.flag = reinterpret_cast<int*>(s.qempty + kQSlots);
+    s.qempty = s.qfull + T::QS;
+    s.flag = reinterpret_cast<int*>(s.qempty + T::QS);
     return s;
 }
 
@@ -511,9 +515,9 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
                 const PageInfo pi = mine[buf * 32 + j];
                 if (qlane && pi.qseg >= 0 && !(p.flags & kDecodeWithholdQ)) {
                     // a new segment starts here: its query tile
-                    const int k = pi.qseg, qs = k % kQSlots;
-                    if (k >= kQSlots &&
-                        !mbar_wait(&sm.qempty[qs], ((k / kQSlots) - 1) & 1, deadline)) {
+                    const int k = pi.qseg, qs = k % T::QS;
+                    if (k >= T::QS &&
+                        !mbar_wait(&sm.qempty[qs], ((k / T::QS) - 1) & 1, deadline)) {
                         ok = false;
                         break;
                     }
@@ -554,7 +558,7 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
     // and stops at its first failed wait, so its copies still in flight are at
     // most the last S / NI pages it issued (an older page's stage has been
     // refilled, so that page was consumed); the query lane likewise waits for
-    // its last kQSlots query tiles.  The drain has a deadline of its own: after
+    // its last QS query tiles.  The drain has a deadline of its own: after
     // a timeout the kernel's deadline has passed, and giving up at once would
     // leave copies writing into a CTA that has exited.
     const uint64_t drain_deadline = cycles() + kWaitDeadlineCycles;
@@ -566,8 +570,8 @@ __device__ void producer(const CUtensorMap* tmap, const DecodeParams& p, const S
             }
         }
     }
-    for (int k = segs_issued > kQSlots ? segs_issued - kQSlots : 0; qlane && k < segs_issued; ++k) {
-        if (!mbar_wait(&sm.qfull[k % kQSlots], (k / kQSlots) & 1, drain_deadline)) {
+    for (int k = segs_issued > T::QS ? segs_issued - T::QS : 0; qlane && k < segs_issued; ++k) {
+        if (!mbar_wait(&sm.qfull[k % T::QS], (k / T::QS) & 1, drain_deadline)) {
             set_err(p.err, kDevErrTimeout);
             break;
         }
@@ -859,14 +863,14 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
         uint32_t qf[T::NT][T::KT][2];
         uint32_t nkv[2][2] = {{0u, 0u}, {0u, 0u}};
         {
-            const int qs = seg_k % kQSlots;
+            const int qs = seg_k % T::QS;
             // The first segment's rows come straight from global memory (L2, where
             // the producer prefetched them) when kDecodeDirectQ is set; the others
             // from the query ring.  Every lane waits, then the warp agrees (and
             // reconverges) before the warp-collective fragment loads that follow.
             const bool direct = seg_k == 0 && (p.flags & kDecodeDirectQ);
             const bool got = !alive || direct ||
-                             mbar_wait(&sm.qfull[qs], (seg_k / kQSlots) & 1, deadline);
+                             mbar_wait(&sm.qfull[qs], (seg_k / T::QS) & 1, deadline);
             if (!__all_sync(0xffffffffu, got)) {
                 if (lane == 0) set_err(p.err, kDevErrTimeout);
                 alive = false;
@@ -1096,10 +1100,19 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
             }
         }
 
-        // ---- merge the W warps' states for this segment
+        // ---- merge the W warps' states for this segment, one 8-head tile at a
+        // time (three barriers per tile)
         if (ctid == 0 && x + cnt >= end) VW_TRACE(5, globaltimer());
         if (!alive && lane == 0) sm.flag[1] = 1;  // abort marker, read by all warps below
-        float* mo = sm.mo + warp * T::G * T::MROW;
+        float* mo = sm.mo + warp * 8 * T::MROW;
+        const int g = (int)p.group;
+        // A segment wholly inside this range is written out here; a piece of a
+        // segment split across ranges leaves (o, max, sum) for the combine kernel.
+        uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
+        const int slot = (x == begin) ? 0 : 1;
+        float* po = p.part_o + ((size_t)blockIdx.x * 2 + slot) * T::G * T::D;
+        float* pml = p.part_ml + ((size_t)blockIdx.x * 2 + slot) * T::G * 2;
+        bool abort = false;
 #pragma unroll
         for (int nt = 0; nt < T::NT; ++nt) {
 #pragma unroll
@@ -1107,69 +1120,64 @@ __device__ void consumer(const DecodeParams& p, const Smem& sm, int begin, int e
                 lrun[nt][0] += __shfl_xor_sync(0xffffffffu, lrun[nt][0], off);
                 lrun[nt][1] += __shfl_xor_sync(0xffffffffu, lrun[nt][1], off);
             }
-            const int j0 = nt * 8 + 2 * (lane & 3);
+            const int jl = 2 * (lane & 3);        // this lane's heads in the tile: jl, jl + 1
 #pragma unroll
             for (int mt = 0; mt < T::MT; ++mt) {
                 // O^T rows lane/4 and lane/4 + 8 of d-tile mt
                 const int dA = T::KV == kFP8 ? fp8_out_d(lane >> 2, mt) : mt * 16 + (lane >> 2);
                 const int dB = T::KV == kFP8 ? fp8_out_d((lane >> 2) + 8, mt) : dA + 8;
-                mo[j0 * T::MROW + merge_col<T>(dA)] = o[nt][mt][0];
-                mo[(j0 + 1) * T::MROW + merge_col<T>(dA)] = o[nt][mt][1];
-                mo[j0 * T::MROW + merge_col<T>(dB)] = o[nt][mt][2];
-                mo[(j0 + 1) * T::MROW + merge_col<T>(dB)] = o[nt][mt][3];
+                mo[jl * T::MROW + merge_col<T>(dA)] = o[nt][mt][0];
+                mo[(jl + 1) * T::MROW + merge_col<T>(dA)] = o[nt][mt][1];
+                mo[jl * T::MROW + merge_col<T>(dB)] = o[nt][mt][2];
+                mo[(jl + 1) * T::MROW + merge_col<T>(dB)] = o[nt][mt][3];
             }
             if (lane < 4) {
-                sm.mm[warp * T::G + j0] = mrun[nt][0];
-                sm.mm[warp * T::G + j0 + 1] = mrun[nt][1];
-                sm.ml[warp * T::G + j0] = lrun[nt][0];
-                sm.ml[warp * T::G + j0 + 1] = lrun[nt][1];
+                sm.mm[warp * 8 + jl] = mrun[nt][0];
+                sm.mm[warp * 8 + jl + 1] = mrun[nt][1];
+                sm.ml[warp * 8 + jl] = lrun[nt][0];
+                sm.ml[warp * 8 + jl + 1] = lrun[nt][1];
             }
-        }
-        named_bar_sync(1, NTH);
-        // every consumer warp reads the same marker after the barrier, so all of
-        // them leave the segment loop together and no named barrier is orphaned
-        const bool abort = sm.flag[1] != 0;
-        const int g = (int)p.group;
-        // per-head weights of the W warp states: max, sum, and one factor per
-        // warp (warps without pages in this segment carry -inf and get 0)
-        if (ctid < g) {
-            const int j = ctid;
-            float M = -INFINITY;
+            named_bar_sync(1, NTH);
+            // every consumer warp reads the same marker after the barrier, so all
+            // of them leave the segment loop together and no named barrier is
+            // orphaned
+            abort = sm.flag[1] != 0;
+            const int jn = min(8, g - nt * 8);    // live query heads of the tile
+            // per-head weights of the W warp states: max, sum, and one factor per
+            // warp (warps without pages in this segment carry -inf and get 0)
+            if (ctid < jn) {
+                const int j = ctid;
+                float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < W; ++w) M = fmaxf(M, sm.mm[w * T::G + j]);
-            float Ls = 0.0f;
+                for (int w = 0; w < W; ++w) M = fmaxf(M, sm.mm[w * 8 + j]);
+                float Ls = 0.0f;
 #pragma unroll
-            for (int w = 0; w < W; ++w) {
-                const float mw = sm.mm[w * T::G + j];
-                const float f = mw > -INFINITY ? ex2(mw - M) : 0.0f;
-                Ls += sm.ml[w * T::G + j] * f;
-                sm.mf[w * T::G + j] = f;
+                for (int w = 0; w < W; ++w) {
+                    const float mw = sm.mm[w * 8 + j];
+                    const float f = mw > -INFINITY ? ex2(mw - M) : 0.0f;
+                    Ls += sm.ml[w * 8 + j] * f;
+                    sm.mf[w * 8 + j] = f;
+                }
+                sm.mf[W * 8 + j] = M;
+                sm.mf[(W + 1) * 8 + j] = Ls;
             }
-            sm.mf[W * T::G + j] = M;
-            sm.mf[(W + 1) * T::G + j] = Ls;
-        }
-        named_bar_sync(1, NTH);
-        // A segment wholly inside this range is written out here; a piece of a
-        // segment split across ranges leaves (o, max, sum) for the combine kernel.
-        uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
-        const int slot = (x == begin) ? 0 : 1;
-        float* po = p.part_o + ((size_t)blockIdx.x * 2 + slot) * T::G * T::D;
-        float* pml = p.part_ml + ((size_t)blockIdx.x * 2 + slot) * T::G * 2;
-        for (int idx = ctid; idx < g * T::D && !abort; idx += NTH) {
-            const int j = idx / T::D, d = idx - j * T::D;
-            float Os = 0.0f;
+            named_bar_sync(1, NTH);
+            for (int idx = ctid; idx < jn * T::D && !abort; idx += NTH) {
+                const int jt = idx / T::D, d = idx - jt * T::D, j = nt * 8 + jt;
+                float Os = 0.0f;
 #pragma unroll
-            for (int w = 0; w < W; ++w)
-                Os += sm.mo[(w * T::G + j) * T::MROW + merge_col<T>(d)] * sm.mf[w * T::G + j];
-            if (complete) {
-                out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
-                    f32_to_io<T::IO>(Os / sm.mf[(W + 1) * T::G + j] * T::VFOLD);
-            } else {
-                po[j * T::D + d] = Os;
-                if (d == 0) { pml[j * 2] = sm.mf[W * T::G + j]; pml[j * 2 + 1] = sm.mf[(W + 1) * T::G + j]; }
+                for (int w = 0; w < W; ++w)
+                    Os += sm.mo[(w * 8 + jt) * T::MROW + merge_col<T>(d)] * sm.mf[w * 8 + jt];
+                if (complete) {
+                    out[((size_t)b * p.Hq + (size_t)h * g + j) * T::D + d] =
+                        f32_to_io<T::IO>(Os / sm.mf[(W + 1) * 8 + jt] * T::VFOLD);
+                } else {
+                    po[j * T::D + d] = Os;
+                    if (d == 0) { pml[j * 2] = sm.mf[W * 8 + jt]; pml[j * 2 + 1] = sm.mf[(W + 1) * 8 + jt]; }
+                }
             }
+            named_bar_sync(1, NTH);
         }
-        named_bar_sync(1, NTH);
         x += cnt;
         if (abort) break;
     }
@@ -1196,7 +1204,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::S; ++s) { mbar_init(&sm.full[s], 1); mbar_init(&sm.empty[s], 1); }
-        for (int s = 0; s < kQSlots; ++s) { mbar_init(&sm.qfull[s], 1); mbar_init(&sm.qempty[s], T::W); }
+        for (int s = 0; s < T::QS; ++s) { mbar_init(&sm.qfull[s], 1); mbar_init(&sm.qempty[s], T::W); }
         fence_mbar_init();
         sm.flag[0] = 0;
         sm.flag[1] = 0;
