@@ -132,6 +132,19 @@ def verify_layer(pool, w, layer, q, kn, vn, out, bt, seq_lens, threads=0):
             bool(np.isfinite(got).all())}
 
 
+def choose_gather(w, world):
+    """How a multi-GPU decode run all-gathers each step's outputs.  Measured on
+    B200s: an overlapped gather keeps its NCCL CTAs resident while the next
+    step runs, and a decode CTA that cannot start beside them holds back its
+    layer: cheap while the gather is short (Qwen step, 3.2 MB received per rank
+    on 2 GPUs: 8940 GB/s against 8304 serial), costly when it is long (22 MB on
+    8 GPUs: 26480 against 30995; Llama-3-70B one KV head, 42 MB on 2 GPUs:
+    11308 against 12065, 126 MB on 4: 20948 against 24249).  Serial from 8 MB
+    received per rank and step."""
+    out_bytes = w["L"] * w["B"] * w["Hq"] * w["D"] * 2 if "B" in w and "Hq" in w else 0
+    return "serial" if (world - 1) * out_bytes >= 8 << 20 else "overlap"
+
+
 def algorithmic_bytes_per_launch(w, seq_lens):
     """Bytes one layer's append + decode must move, counting each page once per
     KV head (a GQA group shares it), as the paging walk of
@@ -853,17 +866,7 @@ def main():
     args = ap.parse_args()
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     if args.gather == "auto":
-        # Measured on B200s: an overlapped gather keeps its NCCL CTAs resident
-        # while the next step runs, and a decode CTA that cannot start beside them
-        # holds back its layer: cheap while the gather is short (Qwen step, 3.2 MB
-        # received per rank on 2 GPUs: 8940 GB/s against 8304 serial), costly when
-        # it is long (22 MB on 8 GPUs: 26480 against 30995; Llama-3-70B one KV
-        # head, 42 MB on 2 GPUs: 11308 against 12065, 126 MB on 4: 20948 against
-        # 24249).  Serial from 8 MB received per rank and step.
-        wl = WORKLOADS[args.workload]
-        out_bytes = (wl.get("L", 0) * wl.get("B", 0) * wl.get("Hq", 0) * wl.get("D", 0) * 2
-                     if "B" in wl else 0)
-        args.gather = "serial" if (world_env - 1) * out_bytes >= 8 << 20 else "overlap"
+        args.gather = choose_gather(WORKLOADS[args.workload], world_env)
     if world_env > 1:
         # set before torch loads NCCL.  The per-step output all-gather overlaps
         # the next step's decode on a side stream; every NCCL channel is a CTA
