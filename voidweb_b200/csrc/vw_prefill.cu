@@ -32,6 +32,11 @@
 //    softmax applies the per-token K and V scales.
 //  * Every wait is bounded; on timeout the kernel records kDevErrTimeout,
 //    drains its TMA loads and returns.
+
+// The prefill's barrier waits keep the hardware's own suspend limit: with a
+// 200 ns hint the FP8 prefill measured 332 against 339 TFLOP/s and the bf16
+// one 590 against 593 (the decode gains from the hint).
+#define VW_MBAR_SUSPEND_HINT_NS 0
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <atomic>

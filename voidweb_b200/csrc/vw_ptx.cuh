@@ -59,9 +59,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Suspend-time hint of the waits, in ns: a waiting thread sleeps at most this
+// long before it rechecks (0: the hardware's own limit).  With the hint the
+// FP8 decode of the Llama-3-8B batch measured 4028 against 3751 GB/s and the
+// Qwen decode 4535 against 4512 (20, 200 and 2000 ns alike).
+#ifndef VW_MBAR_SUSPEND_HINT_NS
+#define VW_MBAR_SUSPEND_HINT_NS 200
+#endif
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-#ifdef VW_MBAR_SUSPEND_HINT_NS
+#if VW_MBAR_SUSPEND_HINT_NS > 0
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
