@@ -163,8 +163,8 @@ def algorithmic_bytes_per_launch(w, seq_lens):
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch (one
 # layer) of the named decode workloads, from one ncu --set full capture of that
 # launch; ncu cannot run inside the timed bench, so the figure is carried here.
-NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 79_998_720,
-                          "llama3-8b-fp8-b64": 1_180_684_288,
+NCU_TRAFFIC_PER_LAUNCH = {"qwen2.5-7b-decode-b16": 79_991_808,
+                          "llama3-8b-fp8-b64": 1_180_007_936,
                           # one prefill_kernel launch (one layer), read + write
                           "qwen2.5-7b-prefill-4x2048": 111_355_904,
                           "llama3-8b-fp8-prefill-4x2048": 123_923_456}
