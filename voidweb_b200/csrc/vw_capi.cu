@@ -436,6 +436,21 @@ uint32_t env_decode_flags() {
     return v;
 }
 
+// Virtual pages charged per segment boundary when the decode CTAs split a
+// batch (the gap of the split in vw_decode.cu).  Measured on B200s: 2-byte
+// pages 18 (the Qwen2.5-7B batch-16 step 4658 GB/s against 4531 at 12, 4665
+// at 21, 4609 at 24, 4032 at 6; the Llama-3-70B batch within noise), FP8
+// pages 12 (the Llama-3-8B batch 4040 against 3996 at 18).
+// VOIDWEB_KV_SEGMENT_COST=n overrides it (at most kMaxSegmentCost).
+uint32_t segment_cost(const PoolGeom& g) {
+    static const long env = [] {
+        const char* e = std::getenv("VOIDWEB_KV_SEGMENT_COST");
+        return e ? std::strtol(e, nullptr, 10) : -1L;
+    }();
+    if (env >= 0) return (uint32_t)std::min<long>(env, kMaxSegmentCost);
+    return g.kv_kind == kFP8 ? 12u : 18u;
+}
+
 static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_t s,
                              const DecodeScratch* fixed = nullptr) {
     const PoolGeom& g = pool->geom;
@@ -458,6 +473,7 @@ static int32_t decode_launch(vw_pool* pool, const vw_decode_args* a, cudaStream_
         p.part_ml = pool->part_ml + set * pool->scratch_ml;
     }
     p.flags = a->flags | env_decode_flags();
+    p.seg_cost = segment_cost(g);
     p.plan = (a->flags & VW_DECODE_PLANNED) ? pool->plan : nullptr;
     p.err = pool->err;
     p.B = a->num_seqs;
@@ -655,6 +671,7 @@ int32_t vw_decode_plan(vw_pool* pool, const uint32_t* block_tables, const uint32
     p.group = num_q_heads / g.num_kv_heads;
     p.num_blocks = g.num_blocks;
     p.bt_stride = block_table_stride;
+    p.seg_cost = segment_cost(g);
     cudaError_t e = launch_decode_plan(p, pool->grid, pool->plan, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "vw_decode_plan launch");
     pool->plan_ready = true;

@@ -286,22 +286,18 @@ __device__ __forceinline__ int find_seq(const int* pfx, int B, int Hkv, long lon
 // ordered by (b, h), lie end to end.  A CTA that crosses a segment boundary
 // pays for a second query tile, a merge of its warps' states and a partial
 // write, and it is the one that finishes last; so each segment is followed by
-// a gap of kSegmentCost virtual pages and the virtual line is cut into equal
-// lengths vper.  12 was the best gap in a sweep of 0-20 on the Qwen2.5-7B
-// batch-16 decode (30 pages per CTA).  Page x of the segment with ordinal k
-// (among segments with pages) sits at v(x) = x + kSegmentCost * k; CTA c takes
-// the pages whose v falls in [c * vper, (c + 1) * vper), so the CTA holding
-// page x is v(x) / vper.  With kSegmentCost = 0 this is the plain equal split.
-#ifndef VW_SEGMENT_COST
-#define VW_SEGMENT_COST 12
-#endif
-constexpr int kSegmentCost = VW_SEGMENT_COST;
+// a gap of `cost` virtual pages (DecodeParams::seg_cost) and the virtual line
+// is cut into equal lengths vper.  Page x of the segment with ordinal k (among
+// segments with pages) sits at v(x) = x + cost * k; CTA c takes the pages
+// whose v falls in [c * vper, (c + 1) * vper), so the CTA holding page x is
+// v(x) / vper.  With cost 0 this is the plain equal split.  The decode, its
+// combine grid and the plan all cut with the launch's cost.
 
 // Virtual positions stay far below 2^31: a launch covers fewer than 2^26 pages
-// (the pool's rows are checked against 2^31 at creation) plus kSegmentCost per
-// segment.
-__host__ __device__ __forceinline__ int virtual_total(int total_pages, int segments) {
-    return total_pages + kSegmentCost * segments;
+// (the pool's rows are checked against 2^31 at creation) plus at most
+// kMaxSegmentCost per segment.
+__host__ __device__ __forceinline__ int virtual_total(int total_pages, int segments, int cost) {
+    return total_pages + cost * segments;
 }
 __host__ __device__ __forceinline__ int virtual_per_cta(int vtotal, int grid) {
     const int v = (vtotal + grid - 1) / grid;
@@ -310,19 +306,19 @@ __host__ __device__ __forceinline__ int virtual_per_cta(int vtotal, int grid) {
 
 // First page x with v(x) >= t (total when there is none), from the exclusive
 // prefixes of pages (pfx) and of sequences with pages (nzp) over B sequences.
-__device__ __forceinline__ int range_start(const int* pfx, const int* nzp, int B, int Hkv, int t) {
+__device__ __forceinline__ int range_start(const int* pfx, const int* nzp, int B, int Hkv, int cost, int t) {
     const int total = Hkv * pfx[B];
-    if (t >= virtual_total(total, Hkv * nzp[B])) return total;
+    if (t >= virtual_total(total, Hkv * nzp[B], cost)) return total;
     // largest b whose first virtual position is <= t (always a sequence with pages)
     int lo = 0, hi = B - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (virtual_total(Hkv * pfx[mid], Hkv * nzp[mid]) <= t) lo = mid; else hi = mid - 1;
+        if (virtual_total(Hkv * pfx[mid], Hkv * nzp[mid], cost) <= t) lo = mid; else hi = mid - 1;
     }
     const int np = pfx[lo + 1] - pfx[lo];
-    const int r = t - virtual_total(Hkv * pfx[lo], Hkv * nzp[lo]);
-    const int h = r / (np + kSegmentCost);
-    const int off = r - h * (np + kSegmentCost);
+    const int r = t - virtual_total(Hkv * pfx[lo], Hkv * nzp[lo], cost);
+    const int h = r / (np + cost);
+    const int off = r - h * (np + cost);
     // inside the gap after segment h: the range starts at the next segment
     return Hkv * pfx[lo] + h * np + (off < np ? off : np);
 }
@@ -1259,9 +1255,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeParams p) {
         end = sm.flag[3];
     } else {
         const int total = (int)p.Hkv * sm.pfx[p.B];
-        const int vper = virtual_per_cta(virtual_total(total, (int)p.Hkv * sm.nzp[p.B]), (int)gridDim.x);
-        begin = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, (int)blockIdx.x * vper);
-        end = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, ((int)blockIdx.x + 1) * vper);
+        const int cost = (int)p.seg_cost;
+        const int vper = virtual_per_cta(virtual_total(total, (int)p.Hkv * sm.nzp[p.B], cost), (int)gridDim.x);
+        begin = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, cost, (int)blockIdx.x * vper);
+        end = range_start(sm.pfx, sm.nzp, (int)p.B, (int)p.Hkv, cost, ((int)blockIdx.x + 1) * vper);
     }
     if (begin >= end) return;
 
@@ -1353,16 +1350,17 @@ __global__ void __launch_bounds__(kCombineThreads, kCombineMinBlocks) combine_ke
     }
     const int np = pages(b);
     if (np == 0) return;
-    const int vper = virtual_per_cta(virtual_total(Hkv * all, Hkv * nz_all), dec_grid);
+    const int cost = (int)p.seg_cost;
+    const int vper = virtual_per_cta(virtual_total(Hkv * all, Hkv * nz_all, cost), dec_grid);
     const int s_begin = Hkv * before + h * np;
     const int k = Hkv * nz_before + h;        // segment ordinal
-    const int v0 = s_begin + kSegmentCost * k;
+    const int v0 = s_begin + cost * k;
     const int c0 = v0 / vper, c1 = (v0 + np - 1) / vper;
     if (c0 == c1) return;                      // written out by the decode CTA itself
     // CTA c0 holds this segment in slot 0 when the segment starts its range
     // (the page before it, of segment k-1, lies in an earlier CTA), else in
     // slot 1 (its last segment); every later CTA starts inside it
-    const int slot0 = (k == 0 || (s_begin - 1) + kSegmentCost * (k - 1) < c0 * vper) ? 0 : 1;
+    const int slot0 = (k == 0 || (s_begin - 1) + cost * (k - 1) < c0 * vper) ? 0 : 1;
     griddep_wait();
     if (threadIdx.x == 0) VW_TRACE(13, globaltimer());
     const int g = (int)p.group;
@@ -1393,9 +1391,10 @@ __global__ void __launch_bounds__(32) plan_kernel(const DecodeParams p, int* pla
         for (int i = lane; i <= B; i += 32) { plan[kPlanPfx + i] = pfx[i]; plan[kPlanNzp + i] = nzp[i]; }
     }
     const int total = Hkv * pfx[B];
-    const int vper = virtual_per_cta(virtual_total(total, Hkv * nzp[B]), (int)gridDim.x);
-    const int begin = range_start(pfx, nzp, B, Hkv, (int)blockIdx.x * vper);
-    const int end = range_start(pfx, nzp, B, Hkv, ((int)blockIdx.x + 1) * vper);
+    const int cost = (int)p.seg_cost;
+    const int vper = virtual_per_cta(virtual_total(total, Hkv * nzp[B], cost), (int)gridDim.x);
+    const int begin = range_start(pfx, nzp, B, Hkv, cost, (int)blockIdx.x * vper);
+    const int end = range_start(pfx, nzp, B, Hkv, cost, ((int)blockIdx.x + 1) * vper);
     int* entry = plan + kPlanCta + (size_t)blockIdx.x * kPlanCtaInts;
     int first_ord = 0;
     if (begin < end) {

@@ -12,6 +12,7 @@ enum KvKind : uint32_t { kF16 = 0, kBF16 = 1, kFP8 = 2 };
 constexpr int kBlockSize = 16;          // tokens per page (engine/engine.bm:102)
 constexpr int kMaxBatchPerLaunch = 1024; // sequences per decode launch (prefix tables in smem)
 constexpr int kMinPagesPerCta = 8;      // work quantum when the batch is tiny
+constexpr int kMaxSegmentCost = 64;     // bound of DecodeParams::seg_cost
 
 // Everything a decode launch needs besides the tensor map.
 struct DecodeParams {
@@ -31,6 +32,7 @@ struct DecodeParams {
     float scale_log2;           // softmax scale * log2(e)
     float rope_theta;           // > 0: rotate q and the new K row (RoPE) at position seq_len-1
     uint32_t flags;             // kDecodePdl | kDecodeEarlyPages | kDecodePlanned
+    uint32_t seg_cost;          // virtual pages per segment boundary in the CTA split (<= kMaxSegmentCost)
     uint64_t wait_cycles;       // bound of the device waits in SM cycles (0: kWaitDeadlineCycles)
 };
 
