@@ -439,8 +439,9 @@ uint32_t env_decode_flags() {
 // Virtual pages charged per segment boundary when the decode CTAs split a
 // batch (the gap of the split in vw_decode.cu).  Measured on B200s: 2-byte
 // pages 18 (the Qwen2.5-7B batch-16 step 4658 GB/s against 4531 at 12, 4665
-// at 21, 4609 at 24, 4032 at 6; the Llama-3-70B batch within noise), FP8
-// pages 12 (the Llama-3-8B batch 4040 against 3996 at 18).
+// at 21, 4609 at 24, 4032 at 6; the Llama-3-70B one-KV-head batch 6265
+// against 6290 at 12 and 6244 at 24), FP8 pages 12 (the Llama-3-8B batch 4062
+// against 3995 at 0, 4081 at 6, 3996 at 18).
 // VOIDWEB_KV_SEGMENT_COST=n overrides it (at most kMaxSegmentCost).
 uint32_t segment_cost(const PoolGeom& g) {
     static const long env = [] {
