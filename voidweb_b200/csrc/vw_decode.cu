@@ -72,6 +72,11 @@
 #ifndef VW_DECODE_GRID_PER_SM
 #define VW_DECODE_GRID_PER_SM VW_DECODE_CTAS_PER_SM
 #endif
+// register bound of the 2-byte-page, one-tile decode: the threads of this many
+// CTAs per SM (3: 128 registers)
+#ifndef VW_DECODE_MIN_CTAS_2B
+#define VW_DECODE_MIN_CTAS_2B 3
+#endif
 #ifndef VW_DECODE_ISSUERS
 #define VW_DECODE_ISSUERS 4
 #endif
@@ -198,7 +203,7 @@ struct Traits {
     // registers (the bound of 3 CTAs' worth of threads), which leaves every SM
     // sub-partition room for the single-warp combine CTAs that wait beside the
     // decode CTAs; the others keep 168 (2 CTAs' worth) to avoid spills.
-    static constexpr int MIN_CTAS = (NT == 1 && KV != kFP8) ? 3 : 2;
+    static constexpr int MIN_CTAS = (NT == 1 && KV != kFP8) ? VW_DECODE_MIN_CTAS_2B : 2;
     static_assert(CHUNKS >= 1, "row must be at least 128 bytes");
     static_assert(S >= 4, "too few pipeline stages");
     static_assert(S % W == 0 && S % NI == 0, "stage ownership needs S % W == S % issuers == 0");
