@@ -879,6 +879,12 @@ def main():
         # the JSON line alone.)
         if args.gather == "overlap":
             os.environ.setdefault("NCCL_MAX_NCHANNELS", str(max(1, world_env // 2)))
+            # the gather's NCCL CTA displaces a decode CTA while the next step
+            # runs; the split with the smaller segment-boundary cost leaves the
+            # CTAs the slack to absorb it (2 B200s, Qwen step: 8981 GB/s at 12
+            # against 7869 at the library's 18, which is best on a GPU that only
+            # decodes: 4687 against 4531 at 12)
+            os.environ.setdefault("VOIDWEB_KV_SEGMENT_COST", "12")
     w = dict(WORKLOADS[args.workload])
     if args.layers > 0:
         w["L"] = min(args.layers, w["L"])
